@@ -1,0 +1,245 @@
+/* GLINT CPU oracle — TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of the reference's kernel-exact GLINT codec, used as the
+ * checker for the CUDA library in tests/, in __graft_entry__.smoke() and as the
+ * timed CPU baseline in bench.py.  Nothing in the product (glint_b200/) links,
+ * loads or calls this file.
+ *
+ * Every function follows one reference function, cited as path:line inside
+ * Jadon-Fox/glint:
+ *   - block absmax        cuda/glint_encode.cu:41-66, glint_np.py:32-40
+ *   - nearest16           cuda/glint_encode.cu:67-79 (first minimum, strict <),
+ *                         glint_np.py:41-52
+ *   - encode (pack)       cuda/glint_encode.cu:80-102, glint_np.py:53-83
+ *   - BF16 widening       cuda/glint_encode.cu:35-40, glint_np.py:16-19
+ *   - expand (f32)        cuda/glint_encode.cu:103-114, glint_np.py:84-92
+ *   - f32 -> BF16 RNE     glint_np.py:25-31, dtype_io.py:32-42
+ *   - H-TILE reference    cuda/glint_htile.cu:124-164 (weights dequantised in
+ *                         f32, products accumulated in f64 as in
+ *                         tests/test_htile_k_bounds_device.cu:90-95)
+ * Parity is pinned against golden vectors that tests/golden/make_golden.py wrote
+ * by running the reference's own glint_np.py / glint_htile_sim.py.
+ *
+ * Build (oracle/Makefile): gcc -O2 -fopenmp -shared -fPIC.  Never with
+ * -ffast-math: the divide must stay IEEE round-to-nearest and denormals must
+ * not be flushed.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+#include "../include/glint_cells.h"
+
+static int g_threads = 1;
+
+void orc_set_threads(int t) { g_threads = t > 0 ? t : 1; }
+int orc_max_threads(void)
+{
+#ifdef _OPENMP
+    return omp_get_num_procs();
+#else
+    return 1;
+#endif
+}
+
+/* cuda/glint_encode.cu:67-79: linear scan, strict < so the first minimum wins.
+ * NaN v makes every comparison false and returns 0. */
+static inline int nearest16(const float *tab, float v)
+{
+    int best = 0;
+    float bd = fabsf(v - tab[0]);
+    for (int k = 1; k < 16; ++k) {
+        float d = fabsf(v - tab[k]);
+        if (d < bd) {
+            bd = d;
+            best = k;
+        }
+    }
+    return best;
+}
+
+/* Combined code 16*hole + plug of one normalised value v (glint_encode.cu:91-92). */
+int orc_code(float v)
+{
+    int h = nearest16(GLINT_PARENT, v);
+    int p = nearest16(GLINT_CELLS[h], v);
+    return (h << 4) | p;
+}
+
+/* Codes for a contiguous range of f32 bit patterns [lo, lo+count). */
+void orc_codes_for_bits(uint32_t lo, int64_t count, uint8_t *out)
+{
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t i = 0; i < count; ++i) {
+        uint32_t u = lo + (uint32_t)i;
+        float v;
+        memcpy(&v, &u, 4);
+        out[i] = (uint8_t)orc_code(v);
+    }
+}
+
+static inline float bf16_to_f32(uint16_t b)
+{
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* glint_np.py:25-31: round to nearest even; NaN keeps its top bits and is quietened. */
+uint16_t orc_f32_to_bf16(float f)
+{
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if (isnan(f))
+        return (uint16_t)((u >> 16) | 0x40u);
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+/* cuda/glint_encode.cu:41-66: max |w| over each block, NaN skipped because
+ * (NaN > m) is false; the last block is padded with zeros. */
+static void block_absmax_f32(const float *w, int64_t n, int bs, float *am)
+{
+    int64_t nb = (n + bs - 1) / bs;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t b = 0; b < nb; ++b) {
+        float m = 0.f;
+        int64_t e = (b + 1) * (int64_t)bs < n ? (b + 1) * (int64_t)bs : n;
+        for (int64_t i = b * (int64_t)bs; i < e; ++i) {
+            float a = fabsf(w[i]);
+            if (a > m)
+                m = a;
+        }
+        am[b] = m;
+    }
+}
+
+/* One weight: v = (s == 0) ? 0 : w / s (IEEE f32 divide), then the two scans
+ * (cuda/glint_encode.cu:89-92). */
+static inline int encode_one(float w, float s)
+{
+    float v = (s == 0.f) ? 0.f : (w / s);
+    return orc_code(v);
+}
+
+/* cuda/glint_encode.cu:80-102 over the whole tensor: byte e holds element 2e in
+ * the low nibble and element 2e+1 in the high nibble; the pad nibble of an odd n
+ * is 0 in both planes. */
+static void encode_pack_f32(const float *w, int64_t n, int bs, const float *am,
+                            uint8_t *hole, uint8_t *plug)
+{
+    int64_t npack = (n + 1) / 2;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t e = 0; e < npack; ++e) {
+        int64_t i0 = 2 * e, i1 = i0 + 1;
+        int c0 = encode_one(w[i0], am[i0 / bs]);
+        int c1 = 0;
+        if (i1 < n)
+            c1 = encode_one(w[i1], am[i1 / bs]);
+        hole[e] = (uint8_t)(((c0 >> 4) & 15) | (((c1 >> 4) & 15) << 4));
+        plug[e] = (uint8_t)((c0 & 15) | ((c1 & 15) << 4));
+    }
+}
+
+/* glint_np.encode_f32 (glint_np.py:63-83). Returns 0, or -1 for bs <= 0. */
+int orc_encode_f32(const float *w, int64_t n, int bs, uint8_t *hole, uint8_t *plug, float *am)
+{
+    if (bs <= 0)
+        return -1;
+    if (n <= 0)
+        return 0;
+    block_absmax_f32(w, n, bs, am);
+    encode_pack_f32(w, n, bs, am, hole, plug);
+    return 0;
+}
+
+/* glint_np.encode_f32(glint_np.dense_to_f32("BF16", raw, n), bs): the BF16 bits
+ * are widened exactly (glint_np.py:17-19, cuda/glint_encode.cu:35-40), then the
+ * f32 encode runs block by block without a full f32 copy. */
+int orc_encode_bf16(const uint16_t *wb, int64_t n, int bs, uint8_t *hole, uint8_t *plug, float *am)
+{
+    if (bs <= 0)
+        return -1;
+    if (n <= 0)
+        return 0;
+    int64_t nb = (n + bs - 1) / bs;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t b = 0; b < nb; ++b) {
+        float m = 0.f;
+        int64_t e = (b + 1) * (int64_t)bs < n ? (b + 1) * (int64_t)bs : n;
+        for (int64_t i = b * (int64_t)bs; i < e; ++i) {
+            float a = fabsf(bf16_to_f32(wb[i]));
+            if (a > m)
+                m = a;
+        }
+        am[b] = m;
+    }
+    int64_t npack = (n + 1) / 2;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t e = 0; e < npack; ++e) {
+        int64_t i0 = 2 * e, i1 = i0 + 1;
+        int c0 = encode_one(bf16_to_f32(wb[i0]), am[i0 / bs]);
+        int c1 = 0;
+        if (i1 < n)
+            c1 = encode_one(bf16_to_f32(wb[i1]), am[i1 / bs]);
+        hole[e] = (uint8_t)(((c0 >> 4) & 15) | (((c1 >> 4) & 15) << 4));
+        plug[e] = (uint8_t)((c0 & 15) | ((c1 & 15) << 4));
+    }
+    return 0;
+}
+
+static inline float dequant(const uint8_t *hole, const uint8_t *plug, const float *am, int64_t i, int bs)
+{
+    int sh = (int)(i & 1) * 4;
+    int h = (hole[i >> 1] >> sh) & 15;
+    int p = (plug[i >> 1] >> sh) & 15;
+    return GLINT_CELLS[h][p] * am[i / bs];
+}
+
+/* cuda/glint_encode.cu:103-114 / glint_np.py:84-92: out[i] = cells[h][p] * absmax[i / bs],
+ * one f32 multiply. */
+int orc_expand_f32(const uint8_t *hole, const uint8_t *plug, const float *am, int64_t n, int bs, float *out)
+{
+    if (bs <= 0)
+        return -1;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t i = 0; i < n; ++i)
+        out[i] = dequant(hole, plug, am, i, bs);
+    return 0;
+}
+
+/* glint_unpin._expand for BF16 (glint_unpin.py:25-31): f32 expand, then RNE to BF16. */
+int orc_expand_bf16(const uint8_t *hole, const uint8_t *plug, const float *am, int64_t n, int bs, uint16_t *out)
+{
+    if (bs <= 0)
+        return -1;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t i = 0; i < n; ++i)
+        out[i] = orc_f32_to_bf16(dequant(hole, plug, am, i, bs));
+    return 0;
+}
+
+/* H-TILE reference: y[m,n] = sum_k cells[h][p]*absmax[(nK+k)/bs] * x[m,k]
+ * (cuda/glint_htile.cu:147-158), x BF16 row-major [M,K], W packed over the
+ * flattened [N,K] index, y f32 row-major [M,N].  The dequantised weight is the
+ * f32 product (as the kernel forms it); the sum runs in f64 with k ascending. */
+int orc_htile(const uint8_t *hole, const uint8_t *plug, const float *am, const uint16_t *x,
+              float *y, int M, int N, int K, int bs)
+{
+    if (bs <= 0)
+        return -2;
+#pragma omp parallel for num_threads(g_threads) schedule(static) collapse(2)
+    for (int m = 0; m < M; ++m) {
+        for (int nn = 0; nn < N; ++nn) {
+            double acc = 0.0;
+            for (int k = 0; k < K; ++k) {
+                int64_t i = (int64_t)nn * K + k;
+                acc += (double)dequant(hole, plug, am, i, bs) * (double)bf16_to_f32(x[(int64_t)m * K + k]);
+            }
+            y[(int64_t)m * N + nn] = (float)acc;
+        }
+    }
+    return 0;
+}

@@ -1,0 +1,151 @@
+"""GLINT CPU oracle loader — TEST INFRASTRUCTURE ONLY.
+
+numpy front end over oracle/libglint_oracle.so (oracle/glint_oracle.c), the C
+restatement of the reference's kernel-exact codec (glint_np.py, glint_encode.cu,
+glint_htile.cu of Jadon-Fox/glint).  Only tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg import this module; the product never does.
+
+Also locates the reference's own CUDA libraries built for sm_100a under
+oracle/_ref/ (see oracle/Makefile), used by GPU tests as a second checker.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+_LIB = None
+
+
+def build() -> Path:
+    """Compile the oracle (and oracle/_ref when the reference checkout is present)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return HERE / "libglint_oracle.so"
+
+
+def lib():
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    p = HERE / "libglint_oracle.so"
+    if not p.is_file():
+        build()
+    L = ctypes.CDLL(str(p))
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    L.orc_set_threads.argtypes = [i32]
+    L.orc_max_threads.restype = i32
+    L.orc_code.argtypes = [ctypes.c_float]
+    L.orc_code.restype = i32
+    L.orc_codes_for_bits.argtypes = [ctypes.c_uint32, i64, vp]
+    for f in (L.orc_encode_f32, L.orc_encode_bf16):
+        f.argtypes = [vp, i64, i32, vp, vp, vp]
+        f.restype = i32
+    for f in (L.orc_expand_f32, L.orc_expand_bf16):
+        f.argtypes = [vp, vp, vp, i64, i32, vp]
+        f.restype = i32
+    L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
+    L.orc_f32_to_bf16.restype = ctypes.c_uint16
+    L.orc_htile.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32]
+    L.orc_htile.restype = i32
+    _LIB = L
+    return L
+
+
+def set_threads(t: int | None = None) -> int:
+    """Use t host threads (default: every core). Returns the count used."""
+    L = lib()
+    t = t or L.orc_max_threads()
+    L.orc_set_threads(t)
+    return t
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def encode_bf16(w_bf16: np.ndarray, blocksize: int = 64):
+    """BF16 bits (uint16) -> (hole uint8[ceil(n/2)], plug uint8[ceil(n/2)], absmax f32[ceil(n/bs)])."""
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16).reshape(-1)
+    n = w.size
+    hole = np.zeros((n + 1) // 2, np.uint8)
+    plug = np.zeros((n + 1) // 2, np.uint8)
+    am = np.zeros((n + blocksize - 1) // blocksize, np.float32)
+    rc = lib().orc_encode_bf16(_ptr(w), n, blocksize, _ptr(hole), _ptr(plug), _ptr(am))
+    if rc:
+        raise ValueError(f"orc_encode_bf16 rc={rc}")
+    return hole, plug, am
+
+
+def encode_f32(w: np.ndarray, blocksize: int = 64):
+    w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+    n = w.size
+    hole = np.zeros((n + 1) // 2, np.uint8)
+    plug = np.zeros((n + 1) // 2, np.uint8)
+    am = np.zeros((n + blocksize - 1) // blocksize, np.float32)
+    rc = lib().orc_encode_f32(_ptr(w), n, blocksize, _ptr(hole), _ptr(plug), _ptr(am))
+    if rc:
+        raise ValueError(f"orc_encode_f32 rc={rc}")
+    return hole, plug, am
+
+
+def expand_f32(hole, plug, am, n: int, blocksize: int = 64) -> np.ndarray:
+    hole = np.ascontiguousarray(hole, np.uint8)
+    plug = np.ascontiguousarray(plug, np.uint8)
+    am = np.ascontiguousarray(am, np.float32)
+    out = np.empty(n, np.float32)
+    lib().orc_expand_f32(_ptr(hole), _ptr(plug), _ptr(am), n, blocksize, _ptr(out))
+    return out
+
+
+def expand_bf16(hole, plug, am, n: int, blocksize: int = 64) -> np.ndarray:
+    """-> uint16 BF16 bits, RNE with the reference NaN rule."""
+    hole = np.ascontiguousarray(hole, np.uint8)
+    plug = np.ascontiguousarray(plug, np.uint8)
+    am = np.ascontiguousarray(am, np.float32)
+    out = np.empty(n, np.uint16)
+    lib().orc_expand_bf16(_ptr(hole), _ptr(plug), _ptr(am), n, blocksize, _ptr(out))
+    return out
+
+
+def htile(hole, plug, am, x_bf16: np.ndarray, M: int, N: int, K: int, blocksize: int = 64) -> np.ndarray:
+    """y f32 [M,N] = x[M,K] . W^T, W dequantised in f32, summed in f64."""
+    hole = np.ascontiguousarray(hole, np.uint8)
+    plug = np.ascontiguousarray(plug, np.uint8)
+    am = np.ascontiguousarray(am, np.float32)
+    x = np.ascontiguousarray(x_bf16, np.uint16).reshape(-1)
+    y = np.empty((M, N), np.float32)
+    rc = lib().orc_htile(_ptr(hole), _ptr(plug), _ptr(am), _ptr(x), _ptr(y), M, N, K, blocksize)
+    if rc:
+        raise ValueError(f"orc_htile rc={rc}")
+    return y
+
+
+def codes_for_bits(lo: int, count: int) -> np.ndarray:
+    out = np.empty(count, np.uint8)
+    lib().orc_codes_for_bits(lo, count, _ptr(out))
+    return out
+
+
+def f32_to_bf16(a: np.ndarray) -> np.ndarray:
+    """RNE f32 -> BF16 bits with the reference NaN rule (glint_np.py:25-31), vectorised."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    r = ((u + (np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1)))) >> 16).astype(np.uint16)
+    return np.where(np.isnan(a), ((u >> 16) | np.uint32(0x40)).astype(np.uint16), r)
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def ref_lib_path(name: str) -> Path | None:
+    """oracle/_ref/<name> (the reference's CUDA library built for sm_100a), if built."""
+    p = HERE / "_ref" / name
+    return p if p.is_file() else None
+
+
+def cores() -> int:
+    return os.cpu_count() or 1
