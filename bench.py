@@ -1,0 +1,420 @@
+#!/usr/bin/env python3
+"""GLINT hot-path benchmark on B200 (one process per GPU).
+
+Headline: encode of a synthetic Llama-3-8B-shaped
+model, 225 BF16 tensors / 7,504,658,432 weights (N(0, 0.02), 0.1% x20
+outliers), blocksize 64, in GB/s of BF16 input.  Weak scaling: every rank
+converts its own copy of the model (the job is N models; tensors are placed per
+rank by LPT with no collective), value = BF16 bytes of all ranks / max-rank time.
+
+Sub-results in the same JSON line: expand of the same model to BF16, decode GEMV
+(configs[2]: M in {1,4,16}, K=4096/N=14336 and K=14336/N=4096) and prefill GEMM
+(configs[3]: M in {512,2048,8192}, K=4096, N in {4096,14336}), each with its
+roofline fraction against MEASURED_PEAKS.json.
+
+--impl reference times the reference's CPU path (the oracle/ restatement of
+glint_np.encode_f32, all host cores) on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BS = 64
+ENC_BYTES_PER_W = 2 + 0.5 + 0.5 + 4 / 64        # 3.0625: BF16 in, hole + plug out, absmax out
+EXP_BYTES_PER_W = 0.5 + 0.5 + 4 / 64 + 2        # 3.0625: planes + absmax in, BF16 out
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(f"/tmp/glint_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(nm)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_init(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, v: float) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def synth_model(specs, seed):
+    """BF16 N(0,0.02) with floor(0.001 n) entries x20 per tensor, generated on the GPU."""
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    out = []
+    for s in specs:
+        n = s.numel
+        w = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        step = 1 << 27
+        for i in range(0, n, step):
+            j = min(n, i + step)
+            w[i:j] = (torch.randn(j - i, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        k = n // 1000
+        if k:
+            idx = torch.randint(0, n, (k,), generator=g, device="cuda")
+            w[idx] = (w[idx].float() * 20).to(torch.bfloat16)
+        out.append(w)
+    return out
+
+
+def batches(items, size=32):
+    return [items[i:i + size] for i in range(0, len(items), size)]
+
+
+def bench_glint(args):
+    import torch
+    from glint_b200 import device as D
+    from glint_b200 import shard
+
+    world, rank, local = dist_init(args)
+    pk = peaks()
+    specs = shard.llama3_8b_tensors()
+    # weak scaling: the job is `world` copies of the model, LPT-placed (each rank gets one copy's worth)
+    job = [s for _ in range(world) for s in specs]
+    plan = shard.lpt_assign([s.numel for s in job], world)
+    mine = [job[i] for i in plan[rank]]
+    weights = sum(s.numel for s in mine)
+    total_weights = sum(s.numel for s in job)
+
+    ws = synth_model(mine, seed=1234 + rank)
+    planes = [D.alloc_planes(w.numel(), BS, w.device) for w in ws]
+    groups = batches(list(range(len(ws))))
+    torch.cuda.synchronize()
+
+    def encode_step(events=None):
+        for gi, grp in enumerate(groups):
+            if events is not None:
+                events[gi][0].record()
+            D.encode_batch([ws[i] for i in grp], BS, outs=[planes[i] for i in grp])
+            if events is not None:
+                events[gi][1].record()
+
+    for _ in range(args.warmup):
+        encode_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in groups]
+          for _ in range(args.steps)]
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)  # let the sampler come up before the timed region
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for k in range(args.steps):
+        encode_step(ev[k])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms_local = t0.elapsed_time(t1)
+    ms = max_over_ranks(world, ms_local)
+    kern_ms = sum(a.elapsed_time(b) for step in ev for (a, b) in step)
+    value = total_weights * 2 / (ms / args.steps / 1e3) / 1e9
+    achieved = weights * ENC_BYTES_PER_W * args.steps / (kern_ms / 1e3) / 1e9
+
+    result = {
+        "metric": "GLINT encode throughput, Llama-3-8B-shaped model (GB/s of BF16 input)",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16->u4+u4+f32 (f32 arithmetic)", "data": "synthetic",
+        "config": {"workload": "encode_llama3_8b (BASELINE configs[1])", "tensors_per_rank": len(mine),
+                   "weights_per_rank": weights, "blocksize": BS, "parallelism": f"per-tensor LPT x{world}, no collective",
+                   "l2": "inputs (15 GB per rank) far larger than L2; no flush needed"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": pk["source"], "bytes_per_weight": ENC_BYTES_PER_W},
+        "clocks": clk,
+        "gpu_launches": args.steps * len(groups),
+    }
+
+    # ---- expand the same model back to BF16 (sub-result)
+    outs = [torch.empty_like(w) for w in ws]
+
+    def expand_step():
+        for grp in groups:
+            D.expand_batch([planes[i] for i in grp], [outs[i] for i in grp], BS)
+    for _ in range(args.warmup):
+        expand_step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        expand_step()
+    b.record()
+    torch.cuda.synchronize()
+    ems = max_over_ranks(world, a.elapsed_time(b)) / args.steps
+    eg = weights * EXP_BYTES_PER_W / (ems / 1e3) / 1e9
+    result["expand"] = {"ms_per_step": round(ems, 4), "bf16_out_gbs_all_ranks": round(total_weights * 2 / (ems / 1e3) / 1e9, 2),
+                        "hbm_gbs_per_gpu": round(eg, 1), "frac": round(eg / pk["hbm_gbs"], 4),
+                        "bytes_per_weight": EXP_BYTES_PER_W}
+    del outs
+
+    # ---- e2e through the reference-facing host ABI (pinned host buffers, PCIe inside the timing)
+    result["e2e"] = e2e_encode(ws, args, world)
+    del ws, planes
+    torch.cuda.empty_cache()
+
+    # ---- decode GEMV and prefill GEMM (per GPU)
+    result["htile"] = bench_htile(args, pk)
+    result["gpu_launches"] += args.steps * len(groups)
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return rank, result
+
+
+def e2e_encode(ws, args, world):
+    """glint_encode_bf16_host on pinned host copies of the first layers' tensors:
+    H2D of the BF16 input and D2H of the planes are inside the timed region."""
+    import torch
+    from glint_b200 import glint_cuda
+    L = glint_cuda.load()
+    sample = ws[: min(len(ws), 1 + 7 * 4)]  # the embedding + 4 layers
+    hosts = []
+    for w in sample:
+        n = w.numel()
+        hosts.append((w.view(torch.int16).cpu().pin_memory(), torch.empty((n + 1) // 2, dtype=torch.uint8).pin_memory(),
+                      torch.empty((n + 1) // 2, dtype=torch.uint8).pin_memory(),
+                      torch.empty((n + BS - 1) // BS, dtype=torch.float32).pin_memory()))
+    nbytes = sum(h[0].numel() * 2 for h in hosts)
+    outbytes = sum(h[1].numel() * 2 + h[3].numel() * 4 for h in hosts)
+    steps = max(1, min(args.steps, 3))
+
+    def step():
+        for src, h, p, a in hosts:
+            rc = L.glint_encode_bf16_host(src.data_ptr(), src.numel(), BS, h.data_ptr(), p.data_ptr(), a.data_ptr())
+            if rc != 0:
+                raise RuntimeError(f"glint_encode_bf16_host rc={rc}")
+    step()
+    barrier(world)
+    t = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = max_over_ranks(world, (time.perf_counter() - t) / steps)
+    return {"value": round(nbytes * world / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": nbytes,
+            "d2h_bytes_per_step": outbytes, "api": "glint_encode_bf16_host (pinned host buffers)",
+            "sample": f"{len(hosts)} tensors ({nbytes / 1e9:.2f} GB BF16) per rank"}
+
+
+def flush_l2(buf):
+    buf.add_(1)
+
+
+def bench_htile(args, pk):
+    import torch
+    from glint_b200 import device as D
+    res = {}
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
+    cases = [(m, 4096, 14336) for m in (1, 4, 16)] + [(m, 14336, 4096) for m in (1, 4, 16)]
+    gemm = [(m, 4096, n) for m in (512, 2048, 8192) for n in (4096, 14336)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    planes_cache = {}
+
+    def planes_for(N, K):
+        if (N, K) not in planes_cache:
+            w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+            planes_cache[(N, K)] = D.encode(w, BS)
+        return planes_cache[(N, K)]
+
+    iters = 50
+    for (M, K, N) in cases + gemm:
+        hole, plug, am = planes_for(N, K)
+        x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        mode = "fast"
+        for _ in range(3):
+            D.htile(x, hole, plug, am, N, BS, mode=mode, out=y)
+        times = []
+        for _ in range(iters if M <= 16 else 10):
+            flush_l2(flush)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            D.htile(x, hole, plug, am, N, BS, mode=mode, out=y)
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        t = statistics.median(times) / 1e3
+        flops = 2.0 * M * N * K
+        if M <= 16:
+            byt = N * K * (1 + 4 / 64) + M * K * 2 + M * N * 4
+            gbs = byt / t / 1e9
+            res[f"gemv_m{M}_k{K}_n{N}"] = {"us": round(t * 1e6, 2), "hbm_gbs": round(gbs, 1),
+                                            "frac": round(gbs / pk["hbm_gbs"], 4), "mode": mode}
+        else:
+            tf = flops / t / 1e12
+            res[f"gemm_m{M}_k{K}_n{N}"] = {"us": round(t * 1e6, 1), "tflops": round(tf, 1),
+                                            "frac": round(tf / pk["bf16_tflops"], 4), "mode": mode}
+    return res
+
+
+# ------------------------------------------------------------------ CPU baselines
+def cpu_encode_sample(seconds: float = 10.0):
+    """The oracle's C restatement of glint_np.encode_f32 on all host cores, over a
+    bounded sample of config 2's tensors (repeated until ~`seconds` of CPU time)."""
+    import numpy as np
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import glint_oracle as O
+    threads = O.set_threads()
+    rng = np.random.default_rng(0)
+    n = 4096 * 4096
+    w = rng.normal(0, 0.02, n).astype(np.float32)
+    w[rng.choice(n, size=n // 1000, replace=False)] *= np.float32(20)
+    bits = O.f32_to_bf16(w)
+    O.encode_bf16(bits, BS)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        O.encode_bf16(bits, BS)
+        done += n
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done * 2 / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{done // n} x one 4096x4096 BF16 tensor of config 2 ({done / 1e6:.0f} M weights, {dt:.1f} s)"}
+
+
+def bench_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    vals = []
+    cb = None
+    for _ in range(args.warmup):
+        cpu_encode_sample(seconds=1.0)
+    for _ in range(max(1, args.steps)):
+        cb = cpu_encode_sample(seconds=max(2.0, 30.0 / max(1, args.steps)))
+        vals.append(cb["value"])
+    v = statistics.median(vals)
+    cb["value"] = v
+    line = {
+        "impl": "reference",
+        "metric": "GLINT encode throughput, Llama-3-8B-shaped model (GB/s of BF16 input)",
+        "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16->u4+u4+f32 (f32 arithmetic)", "data": "synthetic",
+        "config": {"workload": "encode_llama3_8b (BASELINE configs[1])", "blocksize": BS,
+                   "what": "reference CPU encode (glint_np.encode_f32 semantics) restated in oracle/glint_oracle.c"},
+        "cpu_baseline": cb,
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="glint_b200", choices=["glint_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        bench_reference(args)
+        return
+    cb = None
+    if not args.no_cpu_baseline and int(os.environ.get("RANK", "0")) == 0 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        # the CPU baseline runs first, before this process creates a CUDA context
+        cb = cpu_encode_sample()
+    rank, result = bench_glint(args)
+    if rank == 0:
+        result["cpu_baseline"] = cb
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,510 @@
+/* The C ABI of libglint_encode.so: the reference's entry points
+ * (include/glint_encode.h:11-29, include/glint_htile.h:11-19, cuda/p7_abi.c:3-11
+ * of Jadon-Fox/glint) plus additive device-pointer, BF16 and batched calls.
+ *
+ * Host-pointer calls (glint_encode_*_host, glint_expand_*_host) keep the
+ * reference's synchronous contract but do not allocate per call: each device
+ * keeps three grow-only slots of device memory (and of page-locked staging, only
+ * if a caller passes pageable buffers), and a tensor is streamed through them in
+ * chunks so that the host-to-device copy of one chunk, the kernel of the next
+ * and the device-to-host copy of a third overlap.  Page-locked caller buffers are
+ * read and written by DMA directly.  Calls on one device are serialised by a
+ * per-device mutex; the reference's unguarded `static int once` codebook upload
+ * (cuda/glint_encode.cu:115-127) has no counterpart because the codebook is
+ * compiled into the kernels, so every device sees it.
+ */
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/glint_b200.h"
+#include "../../include/glint_encode.h"
+#include "../../include/glint_htile.h"
+#include "common.cuh"
+#include "glint_internal.h"
+
+#ifndef GLINT_B200_VERSION
+#define GLINT_B200_VERSION "0.1.0"
+#endif
+
+namespace glint {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kSlots = 3;
+constexpr int64_t kChunkWeights = int64_t(1) << 24; /* 16 Mi weights per pipeline chunk */
+
+struct Buffer {
+    void *p = nullptr;
+    size_t cap = 0;
+};
+
+struct DevState {
+    std::mutex mu;       /* host pipelines */
+    std::mutex attr_mu;  /* kernel attributes */
+    int sms = 0;
+    std::vector<const void *> smem_done;
+    bool streams_ready = false;
+    cudaStream_t st[kSlots] = {};
+    cudaEvent_t done[kSlots] = {};
+    Buffer dbuf[kSlots];
+    Buffer hbuf[kSlots];
+};
+
+DevState g_dev[kMaxDevices];
+
+int current_device()
+{
+    int d = -1;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices)
+        return -1;
+    return d;
+}
+
+bool grow_device(Buffer &b, size_t need)
+{
+    if (b.cap >= need)
+        return true;
+    if (b.p)
+        cudaFree(b.p);
+    b.p = nullptr;
+    b.cap = 0;
+    if (cudaMalloc(&b.p, need) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    b.cap = need;
+    return true;
+}
+
+bool grow_pinned(Buffer &b, size_t need)
+{
+    if (b.cap >= need)
+        return true;
+    if (b.p)
+        cudaFreeHost(b.p);
+    b.p = nullptr;
+    b.cap = 0;
+    if (cudaMallocHost(&b.p, need) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    b.cap = need;
+    return true;
+}
+
+bool ensure_streams(DevState &S)
+{
+    if (S.streams_ready)
+        return true;
+    for (int i = 0; i < kSlots; ++i) {
+        if (cudaStreamCreateWithFlags(&S.st[i], cudaStreamNonBlocking) != cudaSuccess)
+            return false;
+        if (cudaEventCreateWithFlags(&S.done[i], cudaEventDisableTiming) != cudaSuccess)
+            return false;
+    }
+    S.streams_ready = true;
+    return true;
+}
+
+bool is_pinned(const void *p)
+{
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+int64_t gcd64(int64_t a, int64_t b)
+{
+    while (b) {
+        int64_t t = a % b;
+        a = b;
+        b = t;
+    }
+    return a;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+/* Chunk length: a multiple of the blocksize (blocks never straddle chunks) and of
+ * 512 (plane offsets stay 256-byte aligned). */
+int64_t chunk_len(int64_t n, int bs)
+{
+    const int64_t unit = (int64_t)bs / gcd64(bs, 512) * 512;
+    int64_t c = std::max(unit, kChunkWeights / unit * unit);
+    const int64_t need = (n + unit - 1) / unit * unit;
+    return std::min(c, need);
+}
+
+struct Layout {
+    size_t dense, planes, am, total;
+};
+Layout slot_layout(int64_t chunk, int bs, size_t dense_elem)
+{
+    Layout L;
+    L.dense = align256((size_t)chunk * dense_elem);
+    L.planes = align256((size_t)(chunk / 2));
+    L.am = align256((size_t)(chunk / bs) * sizeof(float));
+    L.total = L.dense + 2 * L.planes + L.am;
+    return L;
+}
+
+/* Encode (to_planes) or expand (!to_planes) a host tensor through the slots.
+ * dense: host input (encode) or output (expand) of n elements of dense_elem bytes. */
+int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs, uint8_t *hole, uint8_t *plug,
+                  float *am)
+{
+    const int dev = current_device();
+    if (dev < 0)
+        return kLaunch;
+    DevState &S = g_dev[dev];
+    std::lock_guard<std::mutex> lk(S.mu);
+    if (!ensure_streams(S))
+        return kLaunch;
+    const size_t de = f32_dense ? 4 : 2;
+    const int64_t chunk = chunk_len(n, bs);
+    const Layout L = slot_layout(chunk, bs, de);
+    const int64_t nb_total = (n + bs - 1) / bs;
+    const bool pin_dense = is_pinned(dense);
+    const bool pin_planes = is_pinned(hole) && is_pinned(plug) && is_pinned(am);
+    for (int s = 0; s < kSlots; ++s) {
+        if (!grow_device(S.dbuf[s], L.total))
+            return to_planes ? kBadArg : kLaunch;
+        if ((!pin_dense || !pin_planes) && !grow_pinned(S.hbuf[s], L.total))
+            return kLaunch;
+    }
+    const int64_t nchunks = (n + chunk - 1) / chunk;
+    std::vector<int64_t> pending(kSlots, -1); /* chunk whose results still sit in a staging slot */
+    int rc = kOk;
+
+    auto span = [&](int64_t ci, int64_t &off, int64_t &cn, int64_t &bytes_pk, int64_t &nam) {
+        off = ci * chunk;
+        cn = std::min(chunk, n - off);
+        bytes_pk = (cn + 1) / 2;
+        nam = std::min((cn + bs - 1) / bs, nb_total - off / bs);
+    };
+    /* move a finished chunk's results from staging to the caller (pageable output) */
+    auto drain = [&](int s) -> int {
+        if (pending[s] < 0)
+            return kOk;
+        if (cudaEventSynchronize(S.done[s]) != cudaSuccess)
+            return kLaunch;
+        int64_t off, cn, bpk, nam;
+        span(pending[s], off, cn, bpk, nam);
+        char *h = static_cast<char *>(S.hbuf[s].p);
+        if (to_planes && !pin_planes) {
+            memcpy(hole + off / 2, h + L.dense, bpk);
+            memcpy(plug + off / 2, h + L.dense + L.planes, bpk);
+            memcpy(am + off / bs, h + L.dense + 2 * L.planes, nam * sizeof(float));
+        }
+        if (!to_planes && !pin_dense)
+            memcpy(static_cast<char *>(dense) + off * de, h, cn * de);
+        pending[s] = -1;
+        return kOk;
+    };
+
+    for (int64_t ci = 0; ci < nchunks && rc == kOk; ++ci) {
+        const int s = (int)(ci % kSlots);
+        if (ci >= kSlots) {
+            if (cudaEventSynchronize(S.done[s]) != cudaSuccess) {
+                rc = kLaunch;
+                break;
+            }
+            if ((rc = drain(s)) != kOk)
+                break;
+        }
+        int64_t off, cn, bpk, nam;
+        span(ci, off, cn, bpk, nam);
+        char *d = static_cast<char *>(S.dbuf[s].p);
+        char *h = static_cast<char *>(S.hbuf[s].p);
+        uint8_t *d_hole = reinterpret_cast<uint8_t *>(d + L.dense);
+        uint8_t *d_plug = reinterpret_cast<uint8_t *>(d + L.dense + L.planes);
+        float *d_am = reinterpret_cast<float *>(d + L.dense + 2 * L.planes);
+        cudaStream_t st = S.st[s];
+        if (to_planes) {
+            const char *src = static_cast<const char *>(dense) + off * de;
+            if (!pin_dense) {
+                memcpy(h, src, cn * de);
+                src = h;
+            }
+            if (cudaMemcpyAsync(d, src, cn * de, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+                rc = kBadArg;
+                break;
+            }
+            EncodeJob j{d, cn, d_hole, d_plug, d_am};
+            if ((rc = encode_launch(&j, 1, bs, f32_dense, st)) != kOk)
+                break;
+            uint8_t *oh = pin_planes ? hole + off / 2 : reinterpret_cast<uint8_t *>(h + L.dense);
+            uint8_t *op = pin_planes ? plug + off / 2 : reinterpret_cast<uint8_t *>(h + L.dense + L.planes);
+            float *oa = pin_planes ? am + off / bs : reinterpret_cast<float *>(h + L.dense + 2 * L.planes);
+            if (cudaMemcpyAsync(oh, d_hole, bpk, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                cudaMemcpyAsync(op, d_plug, bpk, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                cudaMemcpyAsync(oa, d_am, nam * sizeof(float), cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+                rc = kLaunch;
+                break;
+            }
+        } else {
+            const uint8_t *sh = hole + off / 2, *sp = plug + off / 2;
+            const float *sa = am + off / bs;
+            if (!pin_planes) {
+                memcpy(h + L.dense, sh, bpk);
+                memcpy(h + L.dense + L.planes, sp, bpk);
+                memcpy(h + L.dense + 2 * L.planes, sa, nam * sizeof(float));
+                sh = reinterpret_cast<uint8_t *>(h + L.dense);
+                sp = reinterpret_cast<uint8_t *>(h + L.dense + L.planes);
+                sa = reinterpret_cast<float *>(h + L.dense + 2 * L.planes);
+            }
+            if (cudaMemcpyAsync(d_hole, sh, bpk, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                cudaMemcpyAsync(d_plug, sp, bpk, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                cudaMemcpyAsync(d_am, sa, nam * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess) {
+                rc = kBadArg;
+                break;
+            }
+            ExpandJob j{d_hole, d_plug, d_am, cn, d};
+            if ((rc = expand_launch(&j, 1, bs, f32_dense ? kOutF32 : kOutBF16, st)) != kOk)
+                break;
+            char *dst = pin_dense ? static_cast<char *>(dense) + off * de : h;
+            if (cudaMemcpyAsync(dst, d, cn * de, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+                rc = kLaunch;
+                break;
+            }
+        }
+        if (cudaEventRecord(S.done[s], st) != cudaSuccess) {
+            rc = kLaunch;
+            break;
+        }
+        pending[s] = ((to_planes && !pin_planes) || (!to_planes && !pin_dense)) ? ci : -1;
+    }
+    /* finish every slot, also after an error, so no copy into caller memory outlives the call */
+    for (int s = 0; s < kSlots; ++s) {
+        if (cudaStreamSynchronize(S.st[s]) != cudaSuccess && rc == kOk)
+            rc = kLaunch;
+        if (rc == kOk) {
+            int r = drain(s);
+            if (r != kOk)
+                rc = r;
+        }
+    }
+    if (cudaGetLastError() != cudaSuccess && rc == kOk)
+        rc = kLaunch;
+    return rc;
+}
+
+int encode_host(const void *w, int64_t n, int bs, uint8_t *hole, uint8_t *plug, float *am, bool f32)
+{
+    if (n < 0 || bs <= 0)
+        return kBadArg;
+    if (n == 0)
+        return kOk;
+    if (!w || !hole || !plug || !am)
+        return kBadArg;
+    return host_pipeline(true, f32, const_cast<void *>(w), n, bs, hole, plug, am);
+}
+
+int expand_host(const uint8_t *hole, const uint8_t *plug, const float *am, int64_t n, int bs, void *out, bool f32)
+{
+    if (n < 0 || bs <= 0)
+        return kBadArg;
+    if (n == 0)
+        return kOk;
+    if (!hole || !plug || !am || !out)
+        return kBadArg;
+    return host_pipeline(false, f32, out, n, bs, const_cast<uint8_t *>(hole), const_cast<uint8_t *>(plug),
+                         const_cast<float *>(am));
+}
+
+} // namespace
+
+int sm_count()
+{
+    const int d = current_device();
+    if (d < 0)
+        return 148;
+    DevState &S = g_dev[d];
+    if (S.sms <= 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || v <= 0)
+            v = 148;
+        S.sms = v;
+    }
+    return S.sms;
+}
+
+bool ensure_smem(const void *kernel, int bytes)
+{
+    const int d = current_device();
+    if (d < 0)
+        return false;
+    DevState &S = g_dev[d];
+    std::lock_guard<std::mutex> lk(S.attr_mu);
+    if (std::find(S.smem_done.begin(), S.smem_done.end(), kernel) != S.smem_done.end())
+        return true;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    S.smem_done.push_back(kernel);
+    return true;
+}
+
+int htile_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                 OutKind yk, int M, int N, int K, int bs, HtileMode mode, cudaStream_t st)
+{
+    if (!hole || !plug || !am || !x || !y)
+        return kBadArg;
+    if (bs <= 0)
+        return kBadBlocksize;
+    if (M < 0 || N < 0 || K < 0)
+        return kBadArg;
+    if (M == 0 || N == 0)
+        return kOk;
+    if (K == 0) {
+        const size_t bytes = (size_t)M * N * (yk == kOutBF16 ? 2 : 4);
+        return cudaMemsetAsync(y, 0, bytes, st) == cudaSuccess ? kOk : kLaunch;
+    }
+    return htile_gemv_launch(hole, plug, am, x, y, yk, M, N, K, bs, mode, st);
+}
+
+} // namespace glint
+
+using namespace glint;
+
+extern "C" {
+
+const char *p7_abi_version(void) { return "p7_attach_abi_v1"; }
+const char *glint_b200_version(void) { return "glint_b200 " GLINT_B200_VERSION " sm_100a"; }
+
+int glint_encode_n_absmax(int64_t n, int blocksize)
+{
+    if (blocksize <= 0)
+        return 0;
+    return (int)((n + blocksize - 1) / blocksize);
+}
+int glint_encode_n_packed(int64_t n) { return (int)((n + 1) / 2); }
+int64_t glint_encode_n_absmax64(int64_t n, int blocksize)
+{
+    if (blocksize <= 0 || n <= 0)
+        return 0;
+    return (n + blocksize - 1) / blocksize;
+}
+int64_t glint_encode_n_packed64(int64_t n) { return n <= 0 ? 0 : (n + 1) / 2; }
+
+int glint_encode_bf16_host(const uint16_t *w_bf16, int64_t n, int blocksize, uint8_t *hole_packed,
+                           uint8_t *plug_packed, float *absmax)
+{
+    return encode_host(w_bf16, n, blocksize, hole_packed, plug_packed, absmax, false);
+}
+int glint_encode_f32_host(const float *w, int64_t n, int blocksize, uint8_t *hole_packed, uint8_t *plug_packed,
+                          float *absmax)
+{
+    return encode_host(w, n, blocksize, hole_packed, plug_packed, absmax, true);
+}
+int glint_expand_packed_to_f32_host(const uint8_t *hole_packed, const uint8_t *plug_packed, const float *absmax,
+                                    int64_t n, int blocksize, float *out_f32)
+{
+    return expand_host(hole_packed, plug_packed, absmax, n, blocksize, out_f32, true);
+}
+int glint_expand_packed_to_bf16_host(const uint8_t *hole_packed, const uint8_t *plug_packed, const float *absmax,
+                                     int64_t n, int blocksize, uint16_t *out_bf16)
+{
+    return expand_host(hole_packed, plug_packed, absmax, n, blocksize, out_bf16, false);
+}
+
+static int device_encode(const void *w, int64_t n, int bs, uint8_t *h, uint8_t *p, float *a, bool f32,
+                         struct CUstream_st *stream)
+{
+    if (n < 0 || bs <= 0)
+        return kBadArg;
+    if (n == 0)
+        return kOk;
+    if (!w || !h || !p || !a)
+        return kBadArg;
+    EncodeJob j{w, n, h, p, a};
+    return encode_launch(&j, 1, bs, f32, (cudaStream_t)stream);
+}
+int glint_encode_bf16_device(const uint16_t *d_w_bf16, int64_t n, int blocksize, uint8_t *d_hole_packed,
+                             uint8_t *d_plug_packed, float *d_absmax, struct CUstream_st *stream)
+{
+    return device_encode(d_w_bf16, n, blocksize, d_hole_packed, d_plug_packed, d_absmax, false, stream);
+}
+int glint_encode_f32_device(const float *d_w, int64_t n, int blocksize, uint8_t *d_hole_packed,
+                            uint8_t *d_plug_packed, float *d_absmax, struct CUstream_st *stream)
+{
+    return device_encode(d_w, n, blocksize, d_hole_packed, d_plug_packed, d_absmax, true, stream);
+}
+
+static int device_expand(const uint8_t *h, const uint8_t *p, const float *a, int64_t n, int bs, void *out, OutKind k,
+                         struct CUstream_st *stream)
+{
+    if (!h || !p || !a || !out || bs <= 0)
+        return kBadArg;
+    if (n <= 0)
+        return kOk;
+    ExpandJob j{h, p, a, n, out};
+    return expand_launch(&j, 1, bs, k, (cudaStream_t)stream);
+}
+int glint_expand_packed_to_f32_device(const uint8_t *d_hole_packed, const uint8_t *d_plug_packed,
+                                      const float *d_absmax, int64_t n, int blocksize, float *d_out_f32,
+                                      struct CUstream_st *stream)
+{
+    return device_expand(d_hole_packed, d_plug_packed, d_absmax, n, blocksize, d_out_f32, kOutF32, stream);
+}
+int glint_expand_packed_to_bf16_device(const uint8_t *d_hole_packed, const uint8_t *d_plug_packed,
+                                       const float *d_absmax, int64_t n, int blocksize, uint16_t *d_out_bf16,
+                                       struct CUstream_st *stream)
+{
+    return device_expand(d_hole_packed, d_plug_packed, d_absmax, n, blocksize, d_out_bf16, kOutBF16, stream);
+}
+
+int glint_encode_bf16_device_batch(const GlintTensorDesc *t, int count, int blocksize, struct CUstream_st *stream)
+{
+    if (count < 0 || (count > 0 && !t) || blocksize <= 0)
+        return kBadArg;
+    std::vector<EncodeJob> jobs((size_t)count);
+    for (int i = 0; i < count; ++i) {
+        if (t[i].n < 0)
+            return kBadArg;
+        jobs[i] = EncodeJob{t[i].dense, t[i].n, t[i].hole_packed, t[i].plug_packed, t[i].absmax};
+    }
+    return encode_launch(jobs.data(), count, blocksize, false, (cudaStream_t)stream);
+}
+int glint_expand_packed_to_bf16_device_batch(const GlintTensorDesc *t, int count, int blocksize,
+                                             struct CUstream_st *stream)
+{
+    if (count < 0 || (count > 0 && !t) || blocksize <= 0)
+        return kBadArg;
+    std::vector<ExpandJob> jobs((size_t)count);
+    for (int i = 0; i < count; ++i) {
+        if (t[i].n < 0)
+            return kBadArg;
+        jobs[i] = ExpandJob{t[i].hole_packed, t[i].plug_packed, t[i].absmax, t[i].n, t[i].dense};
+    }
+    return expand_launch(jobs.data(), count, blocksize, kOutBF16, (cudaStream_t)stream);
+}
+
+int launch_glint_htile_s3_f32_stream(const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
+                                     const __nv_bfloat16 *d_x, float *d_y, int M, int N, int K, int blocksize,
+                                     cudaStream_t stream)
+{
+    return htile_launch(d_hole, d_plug, d_absmax, d_x, d_y, kOutF32, M, N, K, blocksize, kPrecise, stream);
+}
+int launch_glint_htile_s3_f32(const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
+                              const __nv_bfloat16 *d_x, float *d_y, int M, int N, int K, int blocksize)
+{
+    return launch_glint_htile_s3_f32_stream(d_hole, d_plug, d_absmax, d_x, d_y, M, N, K, blocksize, 0);
+}
+int glint_htile_stream(const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
+                       const __nv_bfloat16 *d_x, void *d_y, int y_dtype, int M, int N, int K, int blocksize,
+                       int mode, cudaStream_t stream)
+{
+    if ((y_dtype != GLINT_Y_F32 && y_dtype != GLINT_Y_BF16) || (mode != GLINT_HTILE_PRECISE && mode != GLINT_HTILE_FAST))
+        return kBadArg;
+    return htile_launch(d_hole, d_plug, d_absmax, d_x, d_y, y_dtype == GLINT_Y_BF16 ? kOutBF16 : kOutF32, M, N, K,
+                        blocksize, mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
+}
+
+} /* extern "C" */

@@ -1,0 +1,59 @@
+/* Host-side launchers shared between the kernel files and the C ABI (abi.cu). */
+#ifndef GLINT_B200_INTERNAL_H_
+#define GLINT_B200_INTERNAL_H_
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace glint {
+
+/* One tensor of an encode: BF16 bits (or f32) in, packed planes + absmax out. */
+struct EncodeJob {
+    const void *w;
+    int64_t n;
+    uint8_t *hole;
+    uint8_t *plug;
+    float *absmax;
+};
+
+/* One tensor of an expand: packed planes + absmax in, BF16 bits or f32 out. */
+struct ExpandJob {
+    const uint8_t *hole;
+    const uint8_t *plug;
+    const float *absmax;
+    int64_t n;
+    void *out;
+};
+
+enum OutKind : int { kOutF32 = 0, kOutBF16 = 1 };
+
+/* H-TILE arithmetic: kPrecise splits every dequantised weight into a BF16 pair
+ * (hi + lo) so the tensor-core sums match an f32 dot product to ~1e-6; kFast uses
+ * one BF16 value per weight (relative error 2^-9 per weight). */
+enum HtileMode : int { kPrecise = 0, kFast = 1 };
+
+/* Launch the encode of `count` tensors with one blocksize on `stream`.  Returns a
+ * Status (0 ok).  Device pointers; nothing is allocated. */
+int encode_launch(const EncodeJob *jobs, int count, int blocksize, bool f32_in, cudaStream_t stream);
+
+/* Launch the expand of `count` tensors. */
+int expand_launch(const ExpandJob *jobs, int count, int blocksize, OutKind out, cudaStream_t stream);
+
+/* y[M,N] = x[M,K] . W^T with W dequantised from hole/plug/absmax. */
+int htile_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
+                 void *y, OutKind y_kind, int M, int N, int K, int blocksize, HtileMode mode, cudaStream_t stream);
+
+/* Decode-shaped path (tensor-core GEMV for K % 64 == 0 and bs % 64 == 0, generic otherwise). */
+int htile_gemv_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
+                      void *y, OutKind y_kind, int M, int N, int K, int blocksize, HtileMode mode,
+                      cudaStream_t stream);
+
+/* SM count of the current device (cached per device). */
+int sm_count();
+/* Raise a kernel's dynamic shared memory limit once per device. */
+bool ensure_smem(const void *kernel, int bytes);
+
+} // namespace glint
+
+#endif

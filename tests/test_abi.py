@@ -1,0 +1,86 @@
+"""The C-ABI library without a GPU: it loads, exports exactly what include/*.h
+declares, and rejects bad arguments before touching a device (reference return
+codes: cuda/glint_encode.cu:134-262, cuda/glint_htile.cu:170-179)."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from glint_b200 import build, glint_cuda
+    build.build()
+    L = glint_cuda.load()
+    assert L is not None, glint_cuda._ERR
+    return L
+
+
+def declared_functions():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(\w+)\s*\(", text, flags=re.M):
+            name = m.group(1)
+            if name in ("if", "return", "sizeof") or text[m.start():m.end()].lstrip().startswith("static"):
+                continue
+            names.add(name)
+    return names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    decl = declared_functions()
+    assert {"glint_encode_bf16_host", "glint_encode_f32_host", "glint_encode_n_absmax", "glint_encode_n_packed",
+            "glint_expand_packed_to_f32_host", "glint_expand_packed_to_f32_device",
+            "launch_glint_htile_s3_f32_stream", "launch_glint_htile_s3_f32", "p7_abi_version"} <= decl
+    so = ROOT / "glint_b200" / "libglint_encode.so"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(so)], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert decl <= exported, sorted(decl - exported)
+    # only the C ABI leaves the library (kernels and C++ helpers stay local)
+    assert all(s.startswith(("glint_", "launch_glint_htile_", "p7_abi_version")) for s in exported), exported
+
+
+def test_attach_abi_version(lib):
+    assert lib.p7_abi_version() == b"p7_attach_abi_v1"
+    assert lib.glint_b200_version().startswith(b"glint_b200 ")
+
+
+def test_size_helpers_match_reference(lib):
+    # glint_encode.cu:128-133: ceil(n/bs) (0 for bs <= 0) and ceil(n/2), as int
+    for n, bs in [(0, 64), (1, 64), (64, 64), (65, 64), (16777216, 64), (7, 23), (5, 0), (5, -3)]:
+        assert lib.glint_encode_n_absmax(n, bs) == ((n + bs - 1) // bs if bs > 0 else 0)
+        assert lib.glint_encode_n_packed(n) == (n + 1) // 2
+    assert lib.glint_encode_n_absmax64(1 << 40, 64) == (1 << 40) // 64
+    assert lib.glint_encode_n_packed64((1 << 40) + 1) == (1 << 39) + 1
+
+
+def test_bad_arguments_rejected_without_gpu(lib):
+    buf = (ctypes.c_uint8 * 64)()
+    p = ctypes.addressof(buf)
+    assert lib.glint_encode_bf16_host(p, 4, 0, p, p, p) == -1          # blocksize <= 0
+    assert lib.glint_encode_bf16_host(p, -1, 64, p, p, p) == -1        # n < 0
+    assert lib.glint_encode_bf16_host(None, 4, 64, p, p, p) == -1      # null
+    assert lib.glint_encode_bf16_host(p, 0, 64, p, p, p) == 0          # nothing to do
+    assert lib.glint_expand_packed_to_f32_device(None, p, p, 4, 64, p, None) == -1
+    assert lib.glint_expand_packed_to_f32_device(p, p, p, 4, 0, p, None) == -1
+    assert lib.glint_expand_packed_to_f32_device(p, p, p, 0, 64, p, None) == 0
+    assert lib.launch_glint_htile_s3_f32(None, p, p, p, p, 1, 1, 1, 64) == -1
+    assert lib.launch_glint_htile_s3_f32(p, p, p, p, p, 1, 1, 1, 0) == -2
+    assert lib.launch_glint_htile_s3_f32(p, p, p, p, p, 0, 5, 5, 64) == 0
+    assert lib.glint_htile_stream(p, p, p, p, p, 7, 1, 1, 1, 64, 0, None) == -1   # bad y dtype
+    assert lib.glint_htile_stream(p, p, p, p, p, 0, 1, 1, 1, 64, 9, None) == -1   # bad mode
+
+
+def test_glint_cuda_mirror_interface():
+    """Same public names and signatures as the reference's glint_cuda.py:1-85."""
+    import inspect
+    from glint_b200 import glint_cuda as G
+    for name in ("lib_path", "load", "encode_bf16_cuda", "expand_cuda", "gpu_ok"):
+        assert callable(getattr(G, name))
+    assert list(inspect.signature(G.encode_bf16_cuda).parameters) == ["raw_bf16", "n", "blocksize"]
+    assert list(inspect.signature(G.expand_cuda).parameters) == ["hole", "plug", "absmax_f32", "n", "blocksize"]
