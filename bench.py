@@ -393,6 +393,44 @@ def bench_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_case(case: str, iters: int = 5):
+    """A small, fixed workload of one kernel family for ncu captures (a few
+    launches, a few hundred MB on the device, inputs larger than L2)."""
+    import torch
+    from glint_b200 import device as D
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    shapes = [(14336, 4096)] * 4  # 235 M weights, 470 MB BF16
+    ws = [(torch.randn(r * c, generator=g, device="cuda") * 0.02).to(torch.bfloat16) for r, c in shapes]
+    planes = D.encode_batch(ws, BS)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = sum(w.numel() for w in ws)
+    if case == "encode":
+        fn = lambda: D.encode_batch(ws, BS, outs=planes)  # noqa: E731
+    elif case == "expand":
+        outs = [torch.empty_like(w) for w in ws]
+        fn = lambda: D.expand_batch(planes, outs, BS)  # noqa: E731
+    elif case.startswith("gemv"):
+        M = int(case[4:] or 1)
+        x = torch.randn((M, 4096), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, 14336), dtype=torch.float32, device="cuda")
+        n = 14336 * 4096
+        fn = lambda: D.htile(x, *planes[0], 14336, BS, mode="fast", out=y)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown case {case}")
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    print(json.dumps({"case": case, "ms": round(ms, 4), "weights": n, "gweights_per_s": round(n / ms / 1e6, 2)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -400,7 +438,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="glint_b200", choices=["glint_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", default=None, help="run one small kernel case (encode|expand|gemv<M>) for ncu")
     args = ap.parse_args()
+    if args.profile:
+        profile_case(args.profile)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

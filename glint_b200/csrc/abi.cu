@@ -366,6 +366,8 @@ int htile_launch(const uint8_t *hole, const uint8_t *plug, const float *am, cons
         const size_t bytes = (size_t)M * N * (yk == kOutBF16 ? 2 : 4);
         return cudaMemsetAsync(y, 0, bytes, st) == cudaSuccess ? kOk : kLaunch;
     }
+    if (mode == kFast && htile_gemm_supported(hole, plug, am, x, y, yk == kOutBF16, M, N, K, bs))
+        return htile_gemm_launch(hole, plug, am, x, y, yk == kOutBF16, M, N, K, bs, st);
     return htile_gemv_launch(hole, plug, am, x, y, yk, M, N, K, bs, mode, st);
 }
 
@@ -376,6 +378,7 @@ using namespace glint;
 extern "C" {
 
 const char *p7_abi_version(void) { return "p7_attach_abi_v1"; }
+int glint_kernel_error(int clear) { return read_kernel_error(clear != 0); }
 const char *glint_b200_version(void) { return "glint_b200 " GLINT_B200_VERSION " sm_100a"; }
 
 int glint_encode_n_absmax(int64_t n, int blocksize)

@@ -49,6 +49,14 @@ int htile_gemv_launch(const uint8_t *hole, const uint8_t *plug, const float *abs
                       void *y, OutKind y_kind, int M, int N, int K, int blocksize, HtileMode mode,
                       cudaStream_t stream);
 
+/* Prefill-shaped path on tcgen05 tensor cores (GLINT_HTILE_FAST arithmetic). */
+bool htile_gemm_supported(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
+                          const void *y, bool y_bf16, int M, int N, int K, int blocksize);
+int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x, void *y,
+                      bool y_bf16, int M, int N, int K, int blocksize, cudaStream_t stream);
+/* Sticky error word written by kernels whose bounded waits ran out (0 = none). */
+int read_kernel_error(bool clear);
+
 /* SM count of the current device (cached per device). */
 int sm_count();
 /* Raise a kernel's dynamic shared memory limit once per device. */

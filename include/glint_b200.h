@@ -12,6 +12,10 @@ extern "C" {
 const char *p7_abi_version(void);
 /* "glint_b200 <version> sm_100a" */
 const char *glint_b200_version(void);
+/* Error word of the current device, set by a kernel whose bounded wait on a
+ * pipeline barrier ran out (1 = timeout); 0 when none.  Synchronous.  clear != 0
+ * resets it. */
+int glint_kernel_error(int clear);
 #ifdef __cplusplus
 }
 #endif
