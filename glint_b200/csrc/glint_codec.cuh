@@ -9,7 +9,7 @@
  *   plug = first-minimum nearest of v within GLINT_CELLS[hole].
  * The combined code 16*hole + plug is a non-decreasing step function of v, so
  * it is fully described by 255 f32 thresholds.  A uniform grid of 513 cells over
- * [-1, 1] (cell = RN(256*v + 256)) holds at most one threshold per cell, so
+ * [-1, 1] (cell = RN(512 * RN(v/2 + 1/2))) holds at most one threshold per cell, so
  *   code(v) = cell_base[c] + (v >= cell_thr[c])
  * with one table read.  The tables are built on the host from the scan itself
  * (gen_lut.cpp) and checked against the CPU oracle over every f32 in [-1, 1].
@@ -38,7 +38,7 @@
 
 namespace glint {
 
-/* grid of the code lookup: cell = RN(v * kCellScale + kCellScale) in [0, 2*kCellScale] */
+/* grid of the code lookup: cell_of(v) in [0, 2*kCellScale], 1/kCellScale wide in v */
 constexpr int kCellScale = 256;
 constexpr int kNumCells = 2 * kCellScale + 1; /* 513 */
 /* 1.5 * 2^23: adding it to a value in [0, 2^22) leaves RN(value) in the low mantissa bits */
@@ -96,14 +96,25 @@ GLINT_HD float div_rn(float a, float b)
 }
 GLINT_HD float bf16_bits_to_f32(uint32_t b16) { return u2f(b16 << 16); }
 
-/* Grid cell of a normalised value.  Encode only produces v in [-1, 1] or NaN
- * (|w| <= s); NaN maps to -1, whose code 0 is what the reference scan returns
- * for NaN.  The clamp keeps every table index in range whatever v is; finite
- * values outside [-1, 1] get the code of the nearer end, as the scan gives. */
+/* Grid cell of a normalised value: u = RN(v/2 + 1/2) clamped to [0, 1] (NaN -> 0,
+ * the code the reference scan gives NaN), cell = RN(512 u) in [0, 512].  On the
+ * GPU the clamp is the .sat form of the fma; the host restates it.  Encode only
+ * produces v in [-1, 1] or NaN (|w| <= s); finite values outside get the code of
+ * the nearer end, as the scan does. */
+GLINT_HD float half_sat(float v)
+{
+#if defined(__CUDA_ARCH__)
+    float u;
+    asm("fma.rn.sat.f32 %0, %1, 0f3F000000, 0f3F000000;" : "=f"(u) : "f"(v));
+    return u;
+#else
+    const float u = fmaf(v, 0.5f, 0.5f);
+    return (u > 0.0f) ? (u < 1.0f ? u : 1.0f) : 0.0f;
+#endif
+}
 GLINT_HD uint32_t cell_of(float v)
 {
-    float c = fminf(fmaxf(v, -1.0f), 1.0f);
-    return f2u(fma_rn(c, (float)kCellScale, kMagic + (float)kCellScale)) - kMagicBits;
+    return f2u(fma_rn(half_sat(v), 512.0f, kMagic)) - kMagicBits;
 }
 
 /* One cell of the lookup table: the code at the cell's lowest value and the one
