@@ -6,29 +6,33 @@
  * 64-weight block, then scans 2 x 16 table entries per weight.  Here one pass
  * reads the input once:
  *
- *   - persistent CTAs of 8 consumer warps and 1 producer warp; the producer
- *     streams units of 4096 weights (8 KB of BF16) into a 5-slot shared-memory
- *     ring with cp.async.bulk, so ~80 KB per SM are in flight regardless of
+ *   - one persistent CTA per SM: 24 consumer warps and a producer warp that
+ *     streams 24 KB units (12288 BF16 weights) into a 6-slot shared-memory ring
+ *     with cp.async.bulk, so up to 144 KB per SM are in flight whatever the
  *     register pressure; full/empty mbarriers hand the slots over;
- *   - a consumer lane takes 8 consecutive weights (one 16-byte shared load) of
- *     two 256-weight groups per unit, so a block of bs weights is bs/8 adjacent
- *     lanes and its absmax a shuffle-max over them (fmaxf skips NaN, as the
- *     reference's `a > m` does);
+ *   - a consumer lane owns 16 consecutive weights (two 16-byte shared loads), so
+ *     a block of bs weights is bs/16 adjacent lanes and its absmax a shuffle-max
+ *     over them.  The maximum is taken on |w|'s bits with packed 16-bit integer
+ *     max, where NaN sorts above inf, so the same pass tells whether the block
+ *     holds a NaN; such blocks recompute absmax with fmaxf, which skips NaN as
+ *     the reference's `a > m` does;
  *   - v = RN(w / s) comes from one correctly rounded reciprocal per block and
- *     Markstein's correction per weight (glint_codec.cuh), IEEE division for
- *     blocks whose scale is out of the theorem's range, and 0 when s == 0;
+ *     Markstein's correction per weight (glint_codec.cuh), evaluated two weights
+ *     per instruction with the f32x2 forms; blocks with a NaN, with s == 0 or
+ *     with s outside the theorem's range use the IEEE divide (and 0 when s == 0);
  *   - code = base + (v >= thr) from a 513-cell table in shared memory, 16
  *     replicas so the 8-byte lookups of a half-warp hit 16 distinct bank pairs;
- *     the cell comes from a saturating fma (which also sends NaN to code 0) and
- *     its address from one multiply-add;
- *   - codes are byte-permuted into one 32-bit hole word and one plug word per 8
- *     weights, lo nibble first (element 2e in the low nibble of byte e).
+ *     on NaN-free blocks v lies in [-1, 1], so the cell is one fma and its
+ *     address one multiply-add (the other blocks clamp first);
+ *   - codes are byte-permuted into 8 bytes of hole and 8 bytes of plug per lane
+ *     (one 8-byte store each), lo nibble first (element 2e in the low nibble of
+ *     byte e).
  *
  * Up to 32 tensors share one launch (a unit prefix table in the kernel
  * parameters), so a whole model is encoded in a handful of launches.  Ragged
  * last units and inputs that are not 16-byte aligned are read by the consumers
  * straight from global memory.  Blocksizes that are not a power of two in
- * [8, 256] and planes that are not 4-byte aligned go through the generic
+ * [16, 512] and planes that are not 8-byte aligned go through the generic
  * two-kernel path, which follows the reference's structure (absmax, then one
  * thread per output byte) with the same arithmetic.
  */
@@ -45,10 +49,9 @@ namespace {
 constexpr int kMaxItems = 32;
 constexpr int kEncReplicas = 16;
 constexpr int kLutBytes = kNumCells * kEncReplicas * (int)sizeof(uint2); /* 65,664 */
-constexpr int kUnitW = 4096;                                            /* weights per ring slot */
-constexpr int kConsumerWarps = 8;                                       /* 512 weights per warp per unit */
-constexpr int kEncThreads = (kConsumerWarps + 1) * 32;                  /* + one producer warp */
-constexpr int kRingBytes = 40 * 1024;
+constexpr int kSlotBytes = 24 * 1024;                                   /* one unit of input */
+constexpr int kSlots = 6;
+constexpr int kWpl = 16;                                                /* weights per consumer lane */
 
 __device__ int g_encode_error = 0;
 
@@ -58,17 +61,19 @@ struct EncodeBatch {
     uint8_t *plug[kMaxItems];
     float *absmax[kMaxItems];
     int64_t n[kMaxItems];
-    int64_t unit_end[kMaxItems]; /* inclusive prefix sum of ceil(n / kUnitW) */
+    int64_t unit_end[kMaxItems]; /* inclusive prefix sum of ceil(n / unit weights) */
     uint32_t direct;             /* bit i: item i is read straight from global (input not 16-B aligned) */
     int count;
 };
 
+/* one unit fills a slot: 12288 BF16 or 6144 f32 weights, 16 per consumer lane */
 template <typename In>
-constexpr int slot_bytes() { return kUnitW * (int)sizeof(In); }
+constexpr int unit_w() { return kSlotBytes / (int)sizeof(In); }
 template <typename In>
-constexpr int ring_slots() { return kRingBytes / slot_bytes<In>(); }
+constexpr int consumer_warps() { return unit_w<In>() / (32 * kWpl); }
 template <typename In>
-constexpr int enc_smem() { return kLutBytes + kRingBytes + 2 * 8 * ring_slots<In>() + 128; }
+constexpr int enc_threads() { return (consumer_warps<In>() + 1) * 32; }
+constexpr int kEncSmem = kLutBytes + kSlots * kSlotBytes + 2 * 8 * kSlots + 128;
 
 /* generic-path lookup (non-replicated table) */
 __device__ __forceinline__ uint32_t lut_code(const uint2 *lut, int stride, float v)
@@ -77,77 +82,163 @@ __device__ __forceinline__ uint32_t lut_code(const uint2 *lut, int stride, float
     return e.y + (v >= __uint_as_float(e.x) ? 1u : 0u);
 }
 
-/* the 8 weights at element offset `off` of the lane's group, from shared memory or
- * (ragged / unaligned units) from global memory */
-__device__ __forceinline__ void group_from_smem(const uint16_t *, uint32_t a, float w[8])
+__device__ __forceinline__ uint64_t pack2(float lo, float hi)
 {
-    const uint4 q = lds128(a);
-    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        w[2 * i] = __uint_as_float(u[i] << 16);
-        w[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
-    }
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
 }
-__device__ __forceinline__ void group_from_smem(const float *, uint32_t a, float w[8])
+__device__ __forceinline__ void unpack2(uint64_t v, float &lo, float &hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t umax16x2(uint32_t a, uint32_t b)
+{
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+/* 16 weights of one lane as f32, and the lane's |w| bit maximum (NaN above inf) */
+struct Lane16 {
+    float w[16];
+    uint32_t mag; /* max over the lane of |w| as an order-preserving integer */
+};
+__device__ __forceinline__ void from_words(const uint16_t *, const uint32_t (&u)[8], Lane16 &L)
+{
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        L.w[2 * i] = __uint_as_float(u[i] << 16);
+        L.w[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+        m = umax16x2(m, u[i] & 0x7FFF7FFFu);
+    }
+    L.mag = max(m & 0xFFFFu, m >> 16) << 16; /* as f32 bits */
+}
+__device__ __forceinline__ void from_words(const float *, const uint32_t (&u)[16], Lane16 &L)
+{
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        L.w[i] = __uint_as_float(u[i]);
+        m = max(m, u[i] & 0x7FFFFFFFu);
+    }
+    L.mag = m;
+}
+template <typename In>
+struct Words {
+    static constexpr int N = 16 * (int)sizeof(In) / 4;
+};
+__device__ __forceinline__ void smem_words(const uint16_t *, uint32_t a, uint32_t (&u)[8])
 {
     const uint4 q0 = lds128(a), q1 = lds128(a + 16);
-    w[0] = __uint_as_float(q0.x), w[1] = __uint_as_float(q0.y), w[2] = __uint_as_float(q0.z), w[3] = __uint_as_float(q0.w);
-    w[4] = __uint_as_float(q1.x), w[5] = __uint_as_float(q1.y), w[6] = __uint_as_float(q1.z), w[7] = __uint_as_float(q1.w);
+    u[0] = q0.x, u[1] = q0.y, u[2] = q0.z, u[3] = q0.w, u[4] = q1.x, u[5] = q1.y, u[6] = q1.z, u[7] = q1.w;
 }
-__device__ __forceinline__ float gload(const uint16_t *p, int64_t i) { return __uint_as_float((uint32_t)__ldcs(p + i) << 16); }
-__device__ __forceinline__ float gload(const float *p, int64_t i) { return __ldcs(p + i); }
-
-/* Codes of 8 weights of one block (absmax s) -> 8 hole nibbles and 8 plug nibbles. */
-__device__ __forceinline__ void encode8(const float w[8], float s, uint32_t lut_c, uint32_t &hw, uint32_t &pw)
+__device__ __forceinline__ void smem_words(const float *, uint32_t a, uint32_t (&u)[16])
 {
-    uint32_t c[8];
-    if (s >= kMarksteinLo && s <= kMarksteinHi) {
-        const float y = __frcp_rn(s);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float v = quotient_markstein(w[j], s, y);
-            const float t = __fmaf_rn(half_sat(v), 512.0f, kMagic);
-            const uint2 e = lds64(__float_as_uint(t) * (uint32_t)(kEncReplicas * 8) + lut_c);
-            c[j] = e.y + (v >= __uint_as_float(e.x) ? 1u : 0u);
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float v = (s == 0.f) ? 0.f : __fdiv_rn(w[j], s);
-            const float t = __fmaf_rn(half_sat(v), 512.0f, kMagic);
-            const uint2 e = lds64(__float_as_uint(t) * (uint32_t)(kEncReplicas * 8) + lut_c);
-            c[j] = e.y + (v >= __uint_as_float(e.x) ? 1u : 0u);
-        }
+    for (int i = 0; i < 4; ++i) {
+        const uint4 q = lds128(a + 16 * i);
+        u[4 * i] = q.x, u[4 * i + 1] = q.y, u[4 * i + 2] = q.z, u[4 * i + 3] = q.w;
     }
-    /* A = codes of elements 0,2,4,6 as bytes, B = elements 1,3,5,7 */
+}
+__device__ __forceinline__ void global_words(const uint16_t *p, int64_t e0, int valid, uint32_t (&u)[8])
+{
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t lo = 2 * i < valid ? (uint32_t)__ldcs(p + e0 + 2 * i) : 0u;
+        const uint32_t hi = 2 * i + 1 < valid ? (uint32_t)__ldcs(p + e0 + 2 * i + 1) : 0u;
+        u[i] = lo | (hi << 16);
+    }
+}
+__device__ __forceinline__ void global_words(const float *p, int64_t e0, int valid, uint32_t (&u)[16])
+{
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        u[i] = i < valid ? __float_as_uint(__ldcs(p + e0 + i)) : 0u;
+}
+
+/* A = codes of elements 0,2,4,6 of c[o..o+7] as bytes, B = elements 1,3,5,7 ->
+ * one hole word and one plug word (lo nibble first). */
+__device__ __forceinline__ void pack8(const uint32_t *c, uint32_t &hw, uint32_t &pw)
+{
     const uint32_t A = __byte_perm(__byte_perm(c[0], c[2], 0x0040), __byte_perm(c[4], c[6], 0x0040), 0x5410);
     const uint32_t B = __byte_perm(__byte_perm(c[1], c[3], 0x0040), __byte_perm(c[5], c[7], 0x0040), 0x5410);
     hw = ((A >> 4) & 0x0F0F0F0Fu) | (B & 0xF0F0F0F0u);
     pw = (A & 0x0F0F0F0Fu) | ((B << 4) & 0xF0F0F0F0u);
 }
 
-template <typename In, int BS_LOG2>
-__global__ void __launch_bounds__(kEncThreads, 2) encode_stream_kernel(const __grid_constant__ EncodeBatch b)
+/* Codes of the lane's 16 weights, all in one block of absmax s. */
+__device__ __forceinline__ void codes16(const Lane16 &L, float s, bool nan_free, uint32_t lut_c, uint32_t (&c)[16])
 {
-    constexpr int S = ring_slots<In>();
-    constexpr int SB = slot_bytes<In>();
-    constexpr int G = (1 << BS_LOG2) / 8; /* lanes per block */
+    if (nan_free && s >= kMarksteinLo && s <= kMarksteinHi) {
+        /* v = RN(w / s) exactly, so v is in [-1, 1] and the cell needs no clamp */
+        const float y = __frcp_rn(s);
+        const uint64_t y2 = pack2(y, y), ns2 = pack2(-s, -s);
+        const uint64_t k256 = pack2(256.0f, 256.0f), kadd = pack2(kMagic + 256.0f, kMagic + 256.0f);
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const uint64_t w2 = pack2(L.w[j], L.w[j + 1]);
+            const uint64_t q2 = mul2(w2, y2);
+            const uint64_t v2 = fma2(fma2(q2, ns2, w2), y2, q2);
+            const uint64_t t2 = fma2(v2, k256, kadd);
+            float v0, v1, t0, t1;
+            unpack2(v2, v0, v1);
+            unpack2(t2, t0, t1);
+            const uint2 e0 = lds64(__float_as_uint(t0) * (uint32_t)(kEncReplicas * 8) + lut_c);
+            const uint2 e1 = lds64(__float_as_uint(t1) * (uint32_t)(kEncReplicas * 8) + lut_c);
+            c[j] = e0.y + (v0 >= __uint_as_float(e0.x) ? 1u : 0u);
+            c[j + 1] = e1.y + (v1 >= __uint_as_float(e1.x) ? 1u : 0u);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float v = (s == 0.f) ? 0.f : __fdiv_rn(L.w[j], s);
+            const uint2 e = lds64((cell_of(v) + kMagicBits) * (uint32_t)(kEncReplicas * 8) + lut_c);
+            c[j] = e.y + (v >= __uint_as_float(e.x) ? 1u : 0u);
+        }
+    }
+}
+
+template <int G>
+__device__ __forceinline__ uint32_t group_max_u32(uint32_t v)
+{
+#pragma unroll
+    for (int off = G / 2; off > 0; off >>= 1)
+        v = max(v, __shfl_xor_sync(0xFFFFFFFFu, v, off));
+    return v;
+}
+
+template <typename In, int BS_LOG2>
+__global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(const __grid_constant__ EncodeBatch b)
+{
+    constexpr int UW = unit_w<In>();
+    constexpr int CW = consumer_warps<In>();
+    constexpr int G = (1 << BS_LOG2) / kWpl; /* lanes per block */
     extern __shared__ __align__(128) uint8_t smem[];
     uint2 *lut = reinterpret_cast<uint2 *>(smem);
     uint8_t *ring = smem + kLutBytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + kRingBytes);
-    uint64_t *empty = full + S;
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + kSlots * kSlotBytes);
+    uint64_t *empty = full + kSlots;
     __shared__ int64_t unit_end[kMaxItems];
 
-    for (int i = threadIdx.x; i < kNumCells * kEncReplicas; i += kEncThreads)
+    for (int i = threadIdx.x; i < kNumCells * kEncReplicas; i += enc_threads<In>())
         lut[i] = g_encode_lut[i / kEncReplicas];
     if (threadIdx.x < kMaxItems)
         unit_end[threadIdx.x] = threadIdx.x < b.count ? b.unit_end[threadIdx.x] : INT64_MAX;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < kSlots; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], CW);
         }
         mbar_init_fence();
     }
@@ -157,23 +248,23 @@ __global__ void __launch_bounds__(kEncThreads, 2) encode_stream_kernel(const __g
     const uint32_t lane = lane_id();
     const int64_t total = unit_end[b.count - 1];
 
-    if (warp == kConsumerWarps) {
+    if (warp == CW) {
         /* producer: one bulk copy per full, aligned unit */
         if (lane == 0) {
             int it = 0;
             int64_t i = 0;
             bool ok = true;
             for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
-                const int s = (int)(i % S);
-                const uint32_t ph = (uint32_t)(i / S) & 1u;
-                if (i >= S && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_encode_error)))
+                const int s = (int)(i % kSlots);
+                const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
+                if (i >= kSlots && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_encode_error)))
                     break;
                 while (unit_end[it] <= u)
                     ++it;
-                const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * kUnitW;
-                if (b.n[it] - off >= kUnitW && !((b.direct >> it) & 1u)) {
-                    mbar_expect_tx(&full[s], SB);
-                    bulk_g2s(ring + s * SB, static_cast<const In *>(b.w[it]) + off, SB, &full[s]);
+                const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * UW;
+                if (b.n[it] - off >= UW && !((b.direct >> it) & 1u)) {
+                    mbar_expect_tx(&full[s], kSlotBytes);
+                    bulk_g2s(ring + s * kSlotBytes, static_cast<const In *>(b.w[it]) + off, kSlotBytes, &full[s]);
                 } else {
                     mbar_arrive(&full[s]);
                 }
@@ -181,69 +272,81 @@ __global__ void __launch_bounds__(kEncThreads, 2) encode_stream_kernel(const __g
             /* after a timeout, let the copies already issued land before the CTA exits */
             if (!ok) {
                 const int64_t issued = i;
-                for (int64_t j = issued > S ? issued - S : 0; j < issued; ++j)
-                    if (!mbar_wait_bounded(&full[(int)(j % S)], (uint32_t)(j / S) & 1u, &g_encode_error))
+                for (int64_t j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
+                    if (!mbar_wait_bounded(&full[(int)(j % kSlots)], (uint32_t)(j / kSlots) & 1u, &g_encode_error))
                         break;
             }
         }
         return;
     }
 
-    /* consumers: a warp owns 512 weights of a unit, as two groups of 256 (8 per lane) */
+    /* consumers: lane owns 16 consecutive weights; a block of bs weights is bs/16 lanes */
     const uint32_t lut_c = saddr(lut) + (lane & (kEncReplicas - 1)) * 8u - kMagicBits * (uint32_t)(kEncReplicas * 8);
+    const int rel = (warp * 32 + (int)lane) * kWpl; /* element offset inside a unit */
     int it = 0;
     int64_t i = 0;
     for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
-        const int s = (int)(i % S);
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
+        const int s = (int)(i % kSlots);
+        const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
         const bool ok = lane == 0 ? mbar_wait_bounded(&full[s], ph, &g_encode_error) : true;
         if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
             break;
         while (unit_end[it] <= u)
             ++it;
-        const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * kUnitW;
+        const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * UW;
         const int64_t n = b.n[it];
-        const bool staged = n - off >= kUnitW && !((b.direct >> it) & 1u);
+        const int64_t e0 = off + rel;
+        const int valid = n - e0 >= kWpl ? kWpl : (n - e0 > 0 ? (int)(n - e0) : 0);
+        const bool staged = n - off >= UW && !((b.direct >> it) & 1u);
         const In *src = static_cast<const In *>(b.w[it]);
-#pragma unroll
-        for (int grp = 0; grp < 2; ++grp) {
-            const int rel = warp * 512 + grp * 256 + (int)lane * 8; /* element offset inside the unit */
-            const int64_t e0 = off + rel;
-            const int valid = n - e0 >= 8 ? 8 : (n - e0 > 0 ? (int)(n - e0) : 0);
-            float w[8];
-            if (staged) {
-                group_from_smem(src, saddr(ring + s * SB) + rel * (int)sizeof(In), w);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    w[j] = j < valid ? gload(src, e0 + j) : 0.f;
-            }
+        uint32_t words[Words<In>::N];
+        if (staged)
+            smem_words(src, saddr(ring + s * kSlotBytes) + rel * (int)sizeof(In), words);
+        else
+            global_words(src, e0, valid, words);
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&empty[s]); /* the slot's data now lives in registers */
+
+        Lane16 L;
+        from_words(src, words, L);
+        const uint32_t mag = group_max_u32<G>(L.mag);
+        const bool nan_free = mag <= 0x7F800000u; /* NaN sorts above inf */
+        float sc = __uint_as_float(mag);
+        if (!nan_free) {
+            /* block holds a NaN: absmax skips it, as the reference's (a > m) does */
             float a = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                a = fmaxf(a, fabsf(w[j]));
-            const float sc = group_max<G>(a);
-            uint32_t hw, pw;
-            encode8(w, sc, lut_c, hw, pw);
-            if (valid > 0 && (lane & (G - 1)) == 0)
-                b.absmax[it][e0 >> BS_LOG2] = sc;
-            if (valid == 8) {
-                __stcs(reinterpret_cast<uint32_t *>(b.hole[it] + (e0 >> 1)), hw);
-                __stcs(reinterpret_cast<uint32_t *>(b.plug[it] + (e0 >> 1)), pw);
-            } else if (valid > 0) {
-                /* ragged end: nibbles past n stay 0 (the odd-n pad nibble) */
-                const uint32_t keep = 0xFFFFFFFFu >> (32 - 4 * valid);
-                hw &= keep;
-                pw &= keep;
-                for (int bb = 0; bb < (valid + 1) / 2; ++bb) {
-                    b.hole[it][(e0 >> 1) + bb] = (uint8_t)(hw >> (8 * bb));
-                    b.plug[it][(e0 >> 1) + bb] = (uint8_t)(pw >> (8 * bb));
+            for (int j = 0; j < kWpl; ++j)
+                a = fmaxf(a, fabsf(L.w[j]));
+            const unsigned act = __activemask();
+#pragma unroll
+            for (int o = G / 2; o > 0; o >>= 1)
+                a = fmaxf(a, __shfl_xor_sync(act, a, o));
+            sc = a;
+        }
+        uint32_t c[16];
+        codes16(L, sc, nan_free, lut_c, c);
+        uint32_t hw[2], pw[2];
+        pack8(c, hw[0], pw[0]);
+        pack8(c + 8, hw[1], pw[1]);
+        if (valid > 0 && (lane & (G - 1)) == 0)
+            b.absmax[it][e0 >> BS_LOG2] = sc;
+        if (valid == kWpl) {
+            __stcs(reinterpret_cast<uint2 *>(b.hole[it] + (e0 >> 1)), make_uint2(hw[0], hw[1]));
+            __stcs(reinterpret_cast<uint2 *>(b.plug[it] + (e0 >> 1)), make_uint2(pw[0], pw[1]));
+        } else if (valid > 0) {
+            /* ragged end: nibbles past n stay 0 (the odd-n pad nibble) */
+            const uint64_t keep = ~0ull >> (64 - 4 * valid);
+            const uint64_t h64 = ((uint64_t)hw[1] << 32 | hw[0]) & keep, p64 = ((uint64_t)pw[1] << 32 | pw[0]) & keep;
+#pragma unroll
+            for (int bb = 0; bb < 8; ++bb) {
+                if (bb < (valid + 1) / 2) {
+                    b.hole[it][(e0 >> 1) + bb] = (uint8_t)(h64 >> (8 * bb));
+                    b.plug[it][(e0 >> 1) + bb] = (uint8_t)(p64 >> (8 * bb));
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0)
-            mbar_arrive(&empty[s]);
     }
 }
 
@@ -311,11 +414,11 @@ template <typename In, int BS_LOG2>
 int launch_fast_bs(const EncodeBatch &b, cudaStream_t st)
 {
     auto kern = encode_stream_kernel<In, BS_LOG2>;
-    if (!ensure_smem((const void *)kern, enc_smem<In>()))
+    if (!ensure_smem((const void *)kern, kEncSmem))
         return kLaunch;
     const int64_t total = b.unit_end[b.count - 1];
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total, (int64_t)sm_count() * 2));
-    kern<<<grid, kEncThreads, enc_smem<In>(), st>>>(b);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total, (int64_t)sm_count()));
+    kern<<<grid, enc_threads<In>(), kEncSmem, st>>>(b);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
 }
 
@@ -323,12 +426,12 @@ template <typename In>
 int launch_fast(const EncodeBatch &b, int bs_log2, cudaStream_t st)
 {
     switch (bs_log2) {
-    case 3: return launch_fast_bs<In, 3>(b, st);
     case 4: return launch_fast_bs<In, 4>(b, st);
     case 5: return launch_fast_bs<In, 5>(b, st);
     case 6: return launch_fast_bs<In, 6>(b, st);
     case 7: return launch_fast_bs<In, 7>(b, st);
     case 8: return launch_fast_bs<In, 8>(b, st);
+    case 9: return launch_fast_bs<In, 9>(b, st);
     default: return kBadBlocksize;
     }
 }
@@ -348,7 +451,7 @@ int encode_launch(const EncodeJob *jobs, int count, int bs, bool f32_in, cudaStr
     if (bs <= 0)
         return kBadArg;
     const int l2 = log2_if_pow2(bs);
-    const bool fast_bs = l2 >= 3 && l2 <= 8;
+    const bool fast_bs = l2 >= 4 && l2 <= 9;
     EncodeBatch b{};
     int rc = kOk;
     auto flush = [&]() -> int {
@@ -364,7 +467,7 @@ int encode_launch(const EncodeJob *jobs, int count, int bs, bool f32_in, cudaStr
             continue;
         if (!j.w || !j.hole || !j.plug || !j.absmax)
             return kBadArg;
-        const bool aligned = aligned_to(j.hole, 4) && aligned_to(j.plug, 4) && aligned_to(j.absmax, 4);
+        const bool aligned = aligned_to(j.hole, 8) && aligned_to(j.plug, 8) && aligned_to(j.absmax, 4);
         if (!fast_bs || !aligned) {
             rc = f32_in ? launch_generic<float>(j, bs, st) : launch_generic<uint16_t>(j, bs, st);
             continue;
@@ -375,7 +478,8 @@ int encode_launch(const EncodeJob *jobs, int count, int bs, bool f32_in, cudaStr
         b.plug[k] = j.plug;
         b.absmax[k] = j.absmax;
         b.n[k] = j.n;
-        b.unit_end[k] = (k ? b.unit_end[k - 1] : 0) + (j.n + kUnitW - 1) / kUnitW;
+        const int64_t uw = f32_in ? unit_w<float>() : unit_w<uint16_t>();
+        b.unit_end[k] = (k ? b.unit_end[k - 1] : 0) + (j.n + uw - 1) / uw;
         if (!aligned_to(j.w, 16))
             b.direct |= 1u << k;
         b.count = k + 1;

@@ -6,13 +6,16 @@
  * multiply, then for BF16 a round to nearest even with the NaN rule
  * (u >> 16) | 0x40.
  *
- * A lane expands 8 weights per step: one 32-bit load from each plane and one
- * 16-byte BF16 store (two for f32), so a warp instruction moves 128 contiguous
- * bytes of each plane and 512 contiguous bytes of output.  The 256-entry f32
- * codebook sits in shared memory with one replica per lane (32 KB), so the
- * per-weight lookups never conflict.  Blocksizes that are a multiple of 8 keep
- * a lane's 8 weights inside one block (one absmax load per 8 weights); other
- * blocksizes and unaligned pointers go through a one-thread-per-weight kernel.
+ * Persistent CTAs of 8 consumer warps and one producer warp: the producer
+ * streams 2 KB of each plane per 4096-weight unit into a 10-slot shared-memory
+ * ring with cp.async.bulk; a consumer lane expands two groups of 8 weights per
+ * unit, one 16-byte BF16 store each (512 contiguous bytes per warp store).  The
+ * 256-entry f32 codebook sits in shared memory with one replica per lane
+ * (32 KB), so the lookups never conflict.  absmax is read through the read-only
+ * cache (one load per 8 weights, shared by the lanes of a block).  Blocksizes
+ * that are not a power of two >= 8 and unaligned outputs go through a
+ * one-thread-per-weight kernel; ragged last units and planes that are not
+ * 16-byte aligned are read straight from global memory.
  *
  * NaN absmax: the reference's host expand multiplies on x86, which returns the
  * NaN operand (quietened) unchanged, so the product carries absmax's bits.  The
@@ -23,14 +26,22 @@
 
 #include "common.cuh"
 #include "glint_internal.h"
+#include "ptx.cuh"
 
 namespace glint {
 namespace {
 
-constexpr int kExpThreads = 256;
 constexpr int kMaxItems = 32;
-constexpr int kRow = 256; /* weights per warp row: 32 lanes x 8 */
-constexpr int kExpSmem = 256 * 32 * (int)sizeof(float);
+constexpr int kUnitW = 4096;                 /* weights per ring slot */
+constexpr int kPlaneBytes = kUnitW / 2;      /* 2 KB of each plane per unit */
+constexpr int kSlotBytes = 2 * kPlaneBytes;  /* hole | plug */
+constexpr int kSlots = 10;
+constexpr int kConsumerWarps = 8;            /* 512 weights per warp per unit */
+constexpr int kExpThreads = (kConsumerWarps + 1) * 32;
+constexpr int kLutBytes = 256 * 32 * (int)sizeof(float);
+constexpr int kExpSmem = kLutBytes + kSlots * kSlotBytes + 2 * 8 * kSlots + 128;
+
+__device__ int g_expand_error = 0;
 
 struct ExpandBatch {
     const uint8_t *hole[kMaxItems];
@@ -38,82 +49,132 @@ struct ExpandBatch {
     const float *absmax[kMaxItems];
     void *out[kMaxItems];
     int64_t n[kMaxItems];
-    int64_t row_end[kMaxItems]; /* inclusive prefix sum of ceil(n / 256) */
+    int64_t unit_end[kMaxItems]; /* inclusive prefix sum of ceil(n / kUnitW) */
+    uint32_t direct;             /* bit i: item i's planes are read straight from global */
     int count;
-    uint32_t bs8; /* blocksize / 8 */
+    int bs_log2;
 };
 
 __device__ __forceinline__ float quiet_nan_of(float s) { return __uint_as_float(__float_as_uint(s) | 0x00400000u); }
 
-/* values of the 8 weights whose nibbles are in H and P (lo nibble first) */
-__device__ __forceinline__ void dequant8(const float *cells, uint32_t H, uint32_t P, float s, float v[8])
+/* values of the 8 weights whose nibbles are in H and P (lo nibble first);
+ * cells_lane = shared address of this lane's replica (entry stride 128 B) */
+__device__ __forceinline__ void dequant8(uint32_t cells_lane, uint32_t H, uint32_t P, float s, float v[8])
 {
     /* byte b of E holds the code of element 2b, byte b of O the code of element 2b+1 */
     const uint32_t E = ((H << 4) & 0xF0F0F0F0u) | (P & 0x0F0F0F0Fu);
     const uint32_t O = (H & 0xF0F0F0F0u) | ((P >> 4) & 0x0F0F0F0Fu);
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-        v[2 * b] = cells[((E >> (8 * b)) & 0xFFu) * 32] * s;
-        v[2 * b + 1] = cells[((O >> (8 * b)) & 0xFFu) * 32] * s;
+        v[2 * b] = __uint_as_float(lds32(cells_lane + (((E >> (8 * b)) & 0xFFu) << 7))) * s;
+        v[2 * b + 1] = __uint_as_float(lds32(cells_lane + (((O >> (8 * b)) & 0xFFu) << 7))) * s;
     }
 }
 
-template <int U, bool BF16>
-__global__ void __launch_bounds__(kExpThreads) expand_fast_kernel(const __grid_constant__ ExpandBatch b)
+template <bool BF16>
+__global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __grid_constant__ ExpandBatch b)
 {
-    extern __shared__ float cells_rep[];
+    extern __shared__ __align__(128) uint8_t smem[];
+    float *cells_rep = reinterpret_cast<float *>(smem);
+    uint8_t *ring = smem + kLutBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + kSlots * kSlotBytes);
+    uint64_t *empty = full + kSlots;
+    __shared__ int64_t unit_end[kMaxItems];
+
     for (int i = threadIdx.x; i < 256 * 32; i += kExpThreads)
         cells_rep[i] = (&g_cells[0][0])[i >> 5];
+    if (threadIdx.x < kMaxItems)
+        unit_end[threadIdx.x] = threadIdx.x < b.count ? b.unit_end[threadIdx.x] : INT64_MAX;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        mbar_init_fence();
+    }
     __syncthreads();
+    const int warp = threadIdx.x >> 5;
     const uint32_t lane = lane_id();
-    const float *cells = cells_rep + lane;
-    const int64_t total = b.row_end[b.count - 1];
-    const int64_t nwarps = (int64_t)gridDim.x * (kExpThreads / 32);
+    const int64_t total = unit_end[b.count - 1];
 
-    for (int64_t g0 = ((int64_t)blockIdx.x * (kExpThreads / 32) + (threadIdx.x >> 5)) * U; g0 < total;
-         g0 += nwarps * U) {
-        uint32_t H[U], P[U];
-        float S[U];
-        int item[U], valid[U];
-        int64_t start[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t g = g0 + u;
-            item[u] = 0;
-            valid[u] = 0;
-            start[u] = 0;
-            H[u] = P[u] = 0;
-            S[u] = 0.f;
-            if (g < total) {
-                int it = 0;
-                while (b.row_end[it] <= g)
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            int it = 0;
+            int64_t i = 0;
+            bool ok = true;
+            for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
+                const int s = (int)(i % kSlots);
+                const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
+                if (i >= kSlots && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_expand_error)))
+                    break;
+                while (unit_end[it] <= u)
                     ++it;
-                const int64_t first = it ? b.row_end[it - 1] : 0;
-                const int64_t s0 = (g - first) * kRow + 8 * (int64_t)lane;
-                const int64_t left = b.n[it] - s0;
-                item[u] = it;
-                start[u] = s0;
-                valid[u] = left >= 8 ? 8 : (left > 0 ? (int)left : 0);
-                if (valid[u] == 8) {
-                    H[u] = __ldcs(reinterpret_cast<const uint32_t *>(b.hole[it] + (s0 >> 1)));
-                    P[u] = __ldcs(reinterpret_cast<const uint32_t *>(b.plug[it] + (s0 >> 1)));
-                } else if (valid[u] > 0) {
-                    for (int bb = 0; bb < (valid[u] + 1) / 2; ++bb) {
-                        H[u] |= (uint32_t)b.hole[it][(s0 >> 1) + bb] << (8 * bb);
-                        P[u] |= (uint32_t)b.plug[it][(s0 >> 1) + bb] << (8 * bb);
-                    }
+                const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * kUnitW;
+                if (b.n[it] - off >= kUnitW && !((b.direct >> it) & 1u)) {
+                    mbar_expect_tx(&full[s], kSlotBytes);
+                    bulk_g2s(ring + s * kSlotBytes, b.hole[it] + off / 2, kPlaneBytes, &full[s]);
+                    bulk_g2s(ring + s * kSlotBytes + kPlaneBytes, b.plug[it] + off / 2, kPlaneBytes, &full[s]);
+                } else {
+                    mbar_arrive(&full[s]);
                 }
-                if (valid[u] > 0)
-                    S[u] = __ldg(b.absmax[it] + (uint32_t)(s0 >> 3) / b.bs8);
+            }
+            if (!ok) {
+                const int64_t issued = i;
+                for (int64_t j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
+                    if (!mbar_wait_bounded(&full[(int)(j % kSlots)], (uint32_t)(j / kSlots) & 1u, &g_expand_error))
+                        break;
             }
         }
+        return;
+    }
+
+    const uint32_t cells_lane = saddr(cells_rep) + lane * 4u;
+    int it = 0;
+    int64_t i = 0;
+    for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
+        const int s = (int)(i % kSlots);
+        const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
+        const bool ok = lane == 0 ? mbar_wait_bounded(&full[s], ph, &g_expand_error) : true;
+        if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
+            break;
+        while (unit_end[it] <= u)
+            ++it;
+        const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * kUnitW;
+        const int64_t n = b.n[it];
+        const bool staged = n - off >= kUnitW && !((b.direct >> it) & 1u);
+        uint32_t H[2], P[2];
+        float S[2];
+        int valid[2];
+        int64_t e0[2];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (valid[u] == 0)
+        for (int grp = 0; grp < 2; ++grp) {
+            const int rel = warp * 512 + grp * 256 + (int)lane * 8;
+            e0[grp] = off + rel;
+            valid[grp] = n - e0[grp] >= 8 ? 8 : (n - e0[grp] > 0 ? (int)(n - e0[grp]) : 0);
+            H[grp] = P[grp] = 0;
+            S[grp] = 0.f;
+            if (staged) {
+                H[grp] = lds32(saddr(ring + s * kSlotBytes) + rel / 2);
+                P[grp] = lds32(saddr(ring + s * kSlotBytes + kPlaneBytes) + rel / 2);
+            } else {
+                for (int bb = 0; bb < (valid[grp] + 1) / 2; ++bb) {
+                    H[grp] |= (uint32_t)b.hole[it][(e0[grp] >> 1) + bb] << (8 * bb);
+                    P[grp] |= (uint32_t)b.plug[it][(e0[grp] >> 1) + bb] << (8 * bb);
+                }
+            }
+            if (valid[grp] > 0)
+                S[grp] = __ldg(b.absmax[it] + (e0[grp] >> b.bs_log2));
+        }
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&empty[s]); /* the planes are in registers now */
+#pragma unroll
+        for (int grp = 0; grp < 2; ++grp) {
+            if (valid[grp] == 0)
                 continue;
             float v[8];
-            dequant8(cells, H[u], P[u], S[u], v);
-            const bool nan_scale = isnan(S[u]);
+            dequant8(cells_lane, H[grp], P[grp], S[grp], v);
+            const bool nan_scale = isnan(S[grp]);
             if (BF16) {
                 uint32_t o[4];
                 if (!nan_scale) {
@@ -123,32 +184,36 @@ __global__ void __launch_bounds__(kExpThreads) expand_fast_kernel(const __grid_c
                         o[q] = *reinterpret_cast<uint32_t *>(&h2);
                     }
                 } else {
-                    const uint32_t nb = (__float_as_uint(S[u]) >> 16) | 0x40u;
+                    const uint32_t nb = (__float_as_uint(S[grp]) >> 16) | 0x40u;
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         o[q] = nb | (nb << 16);
                 }
-                uint16_t *dst = static_cast<uint16_t *>(b.out[item[u]]) + start[u];
-                if (valid[u] == 8) {
+                uint16_t *dst = static_cast<uint16_t *>(b.out[it]) + e0[grp];
+                if (valid[grp] == 8) {
                     __stcs(reinterpret_cast<uint4 *>(dst), make_uint4(o[0], o[1], o[2], o[3]));
                 } else {
-                    for (int j = 0; j < valid[u]; ++j)
-                        dst[j] = (uint16_t)(o[j >> 1] >> (16 * (j & 1)));
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (j < valid[grp])
+                            dst[j] = (uint16_t)(o[j >> 1] >> (16 * (j & 1)));
                 }
             } else {
                 if (nan_scale) {
-                    const float qn = quiet_nan_of(S[u]);
+                    const float qn = quiet_nan_of(S[grp]);
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
                         v[j] = qn;
                 }
-                float *dst = static_cast<float *>(b.out[item[u]]) + start[u];
-                if (valid[u] == 8) {
+                float *dst = static_cast<float *>(b.out[it]) + e0[grp];
+                if (valid[grp] == 8) {
                     __stcs(reinterpret_cast<float4 *>(dst), make_float4(v[0], v[1], v[2], v[3]));
                     __stcs(reinterpret_cast<float4 *>(dst + 4), make_float4(v[4], v[5], v[6], v[7]));
                 } else {
-                    for (int j = 0; j < valid[u]; ++j)
-                        dst[j] = v[j];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (j < valid[grp])
+                            dst[j] = v[j];
                 }
             }
         }
@@ -172,20 +237,24 @@ __global__ void expand_generic_kernel(const uint8_t *hole, const uint8_t *plug, 
     }
 }
 
-constexpr int kUnroll = 4;
-
 template <bool BF16>
 int launch_fast(const ExpandBatch &b, cudaStream_t st)
 {
-    auto kern = expand_fast_kernel<kUnroll, BF16>;
+    auto kern = expand_stream_kernel<BF16>;
     if (!ensure_smem((const void *)kern, kExpSmem))
         return kLaunch;
-    const int64_t total = b.row_end[b.count - 1];
-    const int64_t warps_needed = (total + kUnroll - 1) / kUnroll;
-    const int64_t ctas_needed = (warps_needed + (kExpThreads / 32) - 1) / (kExpThreads / 32);
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ctas_needed, (int64_t)sm_count() * 6));
+    const int64_t total = b.unit_end[b.count - 1];
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total, (int64_t)sm_count() * 3));
     kern<<<grid, kExpThreads, kExpSmem, st>>>(b);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+}
+
+int log2_if_pow2(int bs)
+{
+    for (int l = 0; l < 31; ++l)
+        if (bs == (1 << l))
+            return l;
+    return -1;
 }
 
 } // namespace
@@ -195,16 +264,16 @@ int expand_launch(const ExpandJob *jobs, int count, int bs, OutKind out, cudaStr
     if (bs <= 0)
         return kBadArg;
     const bool bf16 = out == kOutBF16;
+    const int l2 = log2_if_pow2(bs);
     ExpandBatch b{};
-    b.bs8 = (uint32_t)(bs / 8);
+    b.bs_log2 = l2;
     int rc = kOk;
     auto flush = [&]() -> int {
         if (b.count == 0)
             return kOk;
         int r = bf16 ? launch_fast<true>(b, st) : launch_fast<false>(b, st);
-        const uint32_t keep = b.bs8;
         b = ExpandBatch{};
-        b.bs8 = keep;
+        b.bs_log2 = l2;
         return r;
     };
     for (int i = 0; i < count && rc == kOk; ++i) {
@@ -213,10 +282,9 @@ int expand_launch(const ExpandJob *jobs, int count, int bs, OutKind out, cudaStr
             continue;
         if (!j.hole || !j.plug || !j.absmax || !j.out)
             return kBadArg;
-        const bool aligned = aligned_to(j.hole, 4) && aligned_to(j.plug, 4) && aligned_to(j.absmax, 4) &&
-                             aligned_to(j.out, 16);
-        /* fast path: 8-weight steps inside one block, and (i / 8) fits the 32-bit divide */
-        const bool fast = (bs % 8 == 0) && aligned && (j.n >> 3) < (int64_t)0xFFFFFFFF;
+        /* fast path: a power-of-two blocksize >= 8 (8-weight groups inside one block,
+         * absmax index by shift) and a 16-byte aligned output */
+        const bool fast = l2 >= 3 && aligned_to(j.absmax, 4) && aligned_to(j.out, 16);
         if (!fast) {
             const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((j.n + 255) / 256, (int64_t)sm_count() * 8));
             if (bf16)
@@ -232,7 +300,9 @@ int expand_launch(const ExpandJob *jobs, int count, int bs, OutKind out, cudaStr
         b.absmax[k] = j.absmax;
         b.out[k] = j.out;
         b.n[k] = j.n;
-        b.row_end[k] = (k ? b.row_end[k - 1] : 0) + (j.n + kRow - 1) / kRow;
+        b.unit_end[k] = (k ? b.unit_end[k - 1] : 0) + (j.n + kUnitW - 1) / kUnitW;
+        if (!aligned_to(j.hole, 16) || !aligned_to(j.plug, 16))
+            b.direct |= 1u << k;
         b.count = k + 1;
         if (b.count == kMaxItems)
             rc = flush();

@@ -9,7 +9,7 @@
  *   plug = first-minimum nearest of v within GLINT_CELLS[hole].
  * The combined code 16*hole + plug is a non-decreasing step function of v, so
  * it is fully described by 255 f32 thresholds.  A uniform grid of 513 cells over
- * [-1, 1] (cell = RN(512 * RN(v/2 + 1/2))) holds at most one threshold per cell, so
+ * [-1, 1] (cell = RN(256 v + 256)) holds at most one threshold per cell, so
  *   code(v) = cell_base[c] + (v >= cell_thr[c])
  * with one table read.  The tables are built on the host from the scan itself
  * (gen_lut.cpp) and checked against the CPU oracle over every f32 in [-1, 1].
@@ -96,25 +96,17 @@ GLINT_HD float div_rn(float a, float b)
 }
 GLINT_HD float bf16_bits_to_f32(uint32_t b16) { return u2f(b16 << 16); }
 
-/* Grid cell of a normalised value: u = RN(v/2 + 1/2) clamped to [0, 1] (NaN -> 0,
- * the code the reference scan gives NaN), cell = RN(512 u) in [0, 512].  On the
- * GPU the clamp is the .sat form of the fma; the host restates it.  Encode only
- * produces v in [-1, 1] or NaN (|w| <= s); finite values outside get the code of
- * the nearer end, as the scan does. */
-GLINT_HD float half_sat(float v)
-{
-#if defined(__CUDA_ARCH__)
-    float u;
-    asm("fma.rn.sat.f32 %0, %1, 0f3F000000, 0f3F000000;" : "=f"(u) : "f"(v));
-    return u;
-#else
-    const float u = fmaf(v, 0.5f, 0.5f);
-    return (u > 0.0f) ? (u < 1.0f ? u : 1.0f) : 0.0f;
-#endif
-}
+/* Grid cell of a normalised value in [-1, 1]: key = RN(256 v + 256 + 1.5*2^23),
+ * cell = bits(key) - bits(1.5*2^23) = RN(256 v + 256) in [0, 512].  One fma; the
+ * kernels use it directly where v is known to lie in [-1, 1] (Markstein's
+ * quotient of |w| <= s). */
+GLINT_HD float cell_key(float v) { return fma_rn(v, (float)kCellScale, kMagic + (float)kCellScale); }
+
+/* Clamped form for any v: NaN maps to -1 (code 0, what the reference scan gives
+ * NaN), finite values outside [-1, 1] to the nearer end (the scan's answer too). */
 GLINT_HD uint32_t cell_of(float v)
 {
-    return f2u(fma_rn(half_sat(v), 512.0f, kMagic)) - kMagicBits;
+    return f2u(cell_key(fminf(fmaxf(v, -1.0f), 1.0f))) - kMagicBits;
 }
 
 /* One cell of the lookup table: the code at the cell's lowest value and the one
