@@ -44,6 +44,9 @@
 #include "ptx.cuh"
 
 namespace glint {
+
+__device__ int g_encode_error = 0;
+
 namespace {
 
 constexpr int kMaxItems = 32;
@@ -53,7 +56,6 @@ constexpr int kSlotBytes = 24 * 1024;                                   /* one u
 constexpr int kSlots = 6;
 constexpr int kWpl = 16;                                                /* weights per consumer lane */
 
-__device__ int g_encode_error = 0;
 
 struct EncodeBatch {
     const void *w[kMaxItems];
@@ -489,6 +491,19 @@ int encode_launch(const EncodeJob *jobs, int count, int bs, bool f32_in, cudaStr
     if (rc == kOk)
         rc = flush();
     return rc;
+}
+
+/* This file's kernel error word (bounded waits that ran out); clear resets it. */
+int encode_error_word(bool clear)
+{
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_encode_error, sizeof(int)) != cudaSuccess)
+        return -1;
+    if (clear && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_encode_error, &z, sizeof(int));
+    }
+    return v;
 }
 
 } // namespace glint

@@ -29,6 +29,9 @@
 #include "ptx.cuh"
 
 namespace glint {
+
+__device__ int g_expand_error = 0;
+
 namespace {
 
 constexpr int kMaxItems = 32;
@@ -41,7 +44,6 @@ constexpr int kExpThreads = (kConsumerWarps + 1) * 32;
 constexpr int kLutBytes = 256 * 32 * (int)sizeof(float);
 constexpr int kExpSmem = kLutBytes + kSlots * kSlotBytes + 2 * 8 * kSlots + 128;
 
-__device__ int g_expand_error = 0;
 
 struct ExpandBatch {
     const uint8_t *hole[kMaxItems];
@@ -310,6 +312,19 @@ int expand_launch(const ExpandJob *jobs, int count, int bs, OutKind out, cudaStr
     if (rc == kOk)
         rc = flush();
     return rc;
+}
+
+/* This file's kernel error word (bounded waits that ran out); clear resets it. */
+int expand_error_word(bool clear)
+{
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_expand_error, sizeof(int)) != cudaSuccess)
+        return -1;
+    if (clear && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_expand_error, &z, sizeof(int));
+    }
+    return v;
 }
 
 } // namespace glint

@@ -54,8 +54,17 @@ bool htile_gemm_supported(const uint8_t *hole, const uint8_t *plug, const float 
                           const void *y, bool y_bf16, int M, int N, int K, int blocksize);
 int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x, void *y,
                       bool y_bf16, int M, int N, int K, int blocksize, cudaStream_t stream);
-/* Sticky error word written by kernels whose bounded waits ran out (0 = none). */
+/* Sticky error words written by kernels whose bounded waits ran out (0 = none),
+ * one per kernel file; read_kernel_error ORs them. */
 int read_kernel_error(bool clear);
+int encode_error_word(bool clear);
+int expand_error_word(bool clear);
+int decode_error_word(bool clear);
+/* Decode-shaped path streamed through TMA (bs == 64, K % 256 == 0, M <= 32). */
+bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
+                            int M, int N, int K, int blocksize);
+int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
+                        void *y, OutKind y_kind, int M, int N, int K, HtileMode mode, cudaStream_t stream);
 
 /* SM count of the current device (cached per device). */
 int sm_count();

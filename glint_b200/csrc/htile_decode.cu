@@ -1,0 +1,479 @@
+/* GLINT H-TILE for decode-shaped calls (small M), streamed at HBM speed.
+ *
+ * Reference behaviour: cuda/glint_htile.cu:124-164 (glint_htile_s3_f32):
+ *   y[m, n] = sum_k GLINT_CELLS[h][p] * absmax[(n*K + k) / bs] * bf16(x[m, k]),
+ * x BF16 [M, K] row-major, W packed over the flattened [N, K] index, y [M, N]
+ * row-major, overwritten.
+ *
+ * Decode reads each packed weight once (1.0625 B), so the kernel is a stream:
+ *   - work units of 128 weight rows x 256 k; a persistent CTA (one per SM) takes
+ *     a contiguous range of units in row-block-major order (stream-K), so every
+ *     SM gets the same number of units whatever N and K are;
+ *   - a producer warp fetches each unit's hole and plug tiles (128 rows x 128 B,
+ *     128B swizzle) and its absmax tile (128 rows x 4 blocks) with 2-D TMA loads
+ *     into a 4-slot shared-memory ring (~136 KB in flight per SM);
+ *   - each of the 8 consumer warps owns 16 of the 128 rows and runs swap-AB
+ *     mma.sync.m16n8k16: 16 weight rows are the A operand, up to 8 activation
+ *     rows the B operand (MT such tiles).  A lane holds 16 weights of rows g and
+ *     g+8 per 64-k block; the MMA's k positions are mapped onto those weights and
+ *     the activations read with the same map (a dot product does not depend on
+ *     the order of k);
+ *   - each 64-block's sums come out of a fresh accumulator and are scaled by its
+ *     absmax in f32; the codebook sits in shared memory as BF16 pairs
+ *     hi = RN(cell), lo = RN(cell - hi), one replica per lane: precise mode
+ *     issues an MMA for each half (~17 significant bits per weight, f32-class
+ *     results), fast mode uses hi only;
+ *   - a row block split between CTAs is finished by whichever part arrives
+ *     last: each CTA's warp writes its 16 rows' partial sums to a workspace slot
+ *     and bumps a counter for (row block, warp); the last one adds the slots in
+ *     k order (so results do not depend on timing) and writes y.  The workspace
+ *     is allocated once per (device, stream) and reused.
+ * Requires bs == 64, K % 256 == 0, 16-byte aligned planes and absmax; other
+ * shapes use htile_gemv.cu.  Every barrier wait is bounded (~1 s); a timeout
+ * sets this file's error word and the kernel stops.
+ */
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "glint_internal.h"
+#include "ptx.cuh"
+
+namespace glint {
+
+__device__ int g_decode_error = 0;
+
+namespace {
+
+constexpr int kRows = 128;                 /* weight rows per unit */
+constexpr int kKU = 256;                   /* k per unit */
+constexpr int kPlaneTile = kRows * kKU / 2; /* 16 KB per plane */
+constexpr int kAmTile = kRows * 4 * 4;     /* 128 rows x 4 blocks x f32 = 2 KB */
+constexpr int kSlotBytes = 2 * kPlaneTile + kAmTile;
+constexpr int kSlots = 4;
+constexpr int kConsumers = 8;
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kLutBytes = 256 * 32 * 4;
+constexpr int kSmem = 1024 + kSlots * kSlotBytes + kLutBytes + 2 * 8 * kSlots + 64;
+
+__device__ __forceinline__ void mma_bf16_16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t split_pair(float c)
+{
+    const uint32_t hi = f32_to_bf16_bits(c);
+    const float rest = c - __uint_as_float(hi << 16);
+    return hi | (f32_to_bf16_bits(rest) << 16);
+}
+
+struct DecodeArgs {
+    const __nv_bfloat16 *x;
+    void *y;
+    float *ws;          /* partial sums: [row block][part][128][8*MT] */
+    int *counters;      /* per row block and consumer warp, zero between calls */
+    int M, N, K;
+    int KU;             /* units per row block (K / 256) */
+    int64_t units;      /* row blocks * KU */
+    int max_parts;
+};
+
+/* first unit of CTA c under the even split of `units` over `ctas` */
+__device__ __forceinline__ int64_t unit_start(int64_t c, int64_t units, int64_t ctas) { return c * units / ctas; }
+/* CTA whose range holds unit u */
+__device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t ctas)
+{
+    int64_t c = (u * ctas) / units;
+    while (c + 1 < ctas && unit_start(c + 1, units, ctas) <= u)
+        ++c;
+    while (c > 0 && unit_start(c, units, ctas) > u)
+        --c;
+    return c;
+}
+
+template <int MT, bool SPLIT, bool BF16OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    htile_decode_kernel(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap pmap,
+                        const __grid_constant__ CUtensorMap amap, const DecodeArgs a)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint32_t *lut = reinterpret_cast<uint32_t *>(ring + kSlots * kSlotBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(lut) + kLutBytes);
+    uint64_t *empty = full + kSlots;
+
+    for (int i = threadIdx.x; i < 256 * 32; i += kThreads) {
+        const int idx = i >> 5;
+        lut[i] = split_pair(g_cells[idx >> 4][idx & 15]);
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumers);
+        }
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5;
+    const uint32_t lane = lane_id();
+    const int64_t ctas = gridDim.x;
+    const int64_t u0 = unit_start(blockIdx.x, a.units, ctas), u1 = unit_start(blockIdx.x + 1, a.units, ctas);
+
+    if (warp == kConsumers) {
+        if (lane == 0) {
+            int64_t i = 0;
+            bool ok = true;
+            for (int64_t u = u0; u < u1; ++u, ++i) {
+                const int s = (int)(i % kSlots);
+                const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
+                if (i >= kSlots && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_decode_error)))
+                    break;
+                const int rb = (int)(u / a.KU), ku = (int)(u % a.KU);
+                uint8_t *slot = ring + s * kSlotBytes;
+                mbar_expect_tx(&full[s], kSlotBytes);
+                tma_load_2d(slot, &hmap, &full[s], ku * (kKU / 2), rb * kRows);
+                tma_load_2d(slot + kPlaneTile, &pmap, &full[s], ku * (kKU / 2), rb * kRows);
+                tma_load_2d(slot + 2 * kPlaneTile, &amap, &full[s], ku * 4, rb * kRows);
+            }
+            if (!ok) {
+                const int64_t issued = i;
+                for (int64_t j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
+                    if (!mbar_wait_bounded(&full[(int)(j % kSlots)], (uint32_t)(j / kSlots) & 1u, &g_decode_error))
+                        break;
+            }
+        }
+        return;
+    }
+
+    /* consumer warp: rows r0 + g and r0 + g + 8 of each unit's 128 */
+    const int g = (int)(lane >> 2), t = (int)(lane & 3);
+    const int r0 = warp * 16;
+    const uint32_t lut_lane = saddr(lut) + lane * 4u;
+    float acc[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+        acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+    int cur_rb = -1, seg_k0 = 0;
+
+    /* Publish this warp's sums for its 16 rows of row block rb (k units [k0, k1) of
+     * the block): straight to y when this CTA covered the whole block, otherwise
+     * to the workspace; the last of the block's parts to arrive (a per row block
+     * and warp counter) adds the parts in k order and writes y. */
+    auto flush = [&](int rb, int k0, int k1) {
+        constexpr int MP = 8 * MT;
+        const bool whole = k0 == 0 && k1 == a.KU;
+        const int64_t first = cta_of((int64_t)rb * a.KU, a.units, ctas);
+        const int part = whole ? 0 : (int)(blockIdx.x - first);
+        const int parts = whole ? 1 : (int)(cta_of((int64_t)rb * a.KU + a.KU - 1, a.units, ctas) - first + 1);
+        float *wsp = a.ws + ((int64_t)rb * a.max_parts) * kRows * MP;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int row = r0 + g + (q >> 1) * 8;
+                const int col = mt * 8 + 2 * t + (q & 1);
+                const int n = rb * kRows + row;
+                if (whole) {
+                    if (n < a.N && col < a.M) {
+                        if (BF16OUT)
+                            static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(acc[mt][q]);
+                        else
+                            static_cast<float *>(a.y)[(int64_t)col * a.N + n] = acc[mt][q];
+                    }
+                } else {
+                    wsp[((int64_t)part * kRows + row) * MP + col] = acc[mt][q];
+                }
+            }
+        }
+        if (whole)
+            return;
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0)
+            last = atomicAdd(&a.counters[rb * kConsumers + warp], 1) == parts - 1;
+        if (!__shfl_sync(0xFFFFFFFFu, last, 0))
+            return;
+        __threadfence();
+        for (int e = (int)lane; e < 16 * MP; e += 32) {
+            const int row = r0 + e / MP, col = e % MP;
+            float v = 0.f;
+            for (int pp = 0; pp < parts; ++pp)
+                v += __ldcg(wsp + ((int64_t)pp * kRows + row) * MP + col);
+            const int n = rb * kRows + row;
+            if (n < a.N && col < a.M) {
+                if (BF16OUT)
+                    static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(v);
+                else
+                    static_cast<float *>(a.y)[(int64_t)col * a.N + n] = v;
+            }
+        }
+        if (lane == 0)
+            a.counters[rb * kConsumers + warp] = 0; /* ready for the next call */
+    };
+
+    int64_t i = 0;
+    for (int64_t u = u0; u < u1; ++u, ++i) {
+        const int rb = (int)(u / a.KU), ku = (int)(u % a.KU);
+        if (rb != cur_rb) {
+            if (cur_rb >= 0)
+                flush(cur_rb, seg_k0, a.KU);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+                acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+            cur_rb = rb;
+            seg_k0 = ku;
+        }
+        const int s = (int)(i % kSlots);
+        const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
+        const bool ok = lane == 0 ? mbar_wait_bounded(&full[s], ph, &g_decode_error) : true;
+        if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0)) {
+            cur_rb = -1; /* give up: no partial results are published */
+            break;
+        }
+        const uint32_t slot = saddr(ring + s * kSlotBytes);
+        /* x fragments of this unit: row m = mt*8 + g, 16 consecutive k per lane per 64-block */
+        const int kbase = ku * kKU;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint4 xb[MT][2];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int m = mt * 8 + g;
+                if (m < a.M) {
+                    const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (int64_t)m * a.K + kbase + c * 64 + t * 16);
+                    xb[mt][0] = __ldg(src);
+                    xb[mt][1] = __ldg(src + 1);
+                } else {
+                    xb[mt][0] = xb[mt][1] = make_uint4(0, 0, 0, 0);
+                }
+            }
+            /* packed nibbles of rows g and g+8: 8 bytes at k-byte c*32 + t*8 (128B-swizzled rows) */
+            uint32_t E[2][2], O[2][2];
+            float sc[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int row = r0 + g + 8 * r;
+                const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(row & 7);
+                const uint32_t off = (uint32_t)row * 128u + (chunk << 4) + (uint32_t)(t & 1) * 8u;
+                const uint2 hw = lds64(slot + off), pw = lds64(slot + kPlaneTile + off);
+                const uint32_t hv[2] = {hw.x, hw.y}, pv[2] = {pw.x, pw.y};
+#pragma unroll
+                for (int wd = 0; wd < 2; ++wd) {
+                    E[r][wd] = ((hv[wd] << 4) & 0xF0F0F0F0u) | (pv[wd] & 0x0F0F0F0Fu);
+                    O[r][wd] = (hv[wd] & 0xF0F0F0F0u) | ((pv[wd] >> 4) & 0x0F0F0F0Fu);
+                }
+                sc[r] = __uint_as_float(lds32(slot + 2 * kPlaneTile + (uint32_t)(row * 4 + c) * 4u));
+            }
+            float part[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+                part[mt][0] = part[mt][1] = part[mt][2] = part[mt][3] = 0.f;
+#pragma unroll
+            for (int st = 0; st < 4; ++st) {
+                const int wd = st >> 1, b0 = (st & 1) * 2;
+                uint32_t e[2][4];
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+                    e[r][0] = lds32(lut_lane + (((E[r][wd] >> (8 * b0)) & 0xFFu) << 7));
+                    e[r][1] = lds32(lut_lane + (((O[r][wd] >> (8 * b0)) & 0xFFu) << 7));
+                    e[r][2] = lds32(lut_lane + (((E[r][wd] >> (8 * b0 + 8)) & 0xFFu) << 7));
+                    e[r][3] = lds32(lut_lane + (((O[r][wd] >> (8 * b0 + 8)) & 0xFFu) << 7));
+                }
+                const uint32_t ahi[4] = {__byte_perm(e[0][0], e[0][1], 0x5410), __byte_perm(e[1][0], e[1][1], 0x5410),
+                                         __byte_perm(e[0][2], e[0][3], 0x5410), __byte_perm(e[1][2], e[1][3], 0x5410)};
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+                    const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
+                    mma_bf16_16816(part[mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+                }
+                if (SPLIT) {
+                    const uint32_t alo[4] = {__byte_perm(e[0][0], e[0][1], 0x7632), __byte_perm(e[1][0], e[1][1], 0x7632),
+                                             __byte_perm(e[0][2], e[0][3], 0x7632), __byte_perm(e[1][2], e[1][3], 0x7632)};
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
+                        mma_bf16_16816(part[mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                acc[mt][0] = fmaf(sc[0], part[mt][0], acc[mt][0]);
+                acc[mt][1] = fmaf(sc[0], part[mt][1], acc[mt][1]);
+                acc[mt][2] = fmaf(sc[1], part[mt][2], acc[mt][2]);
+                acc[mt][3] = fmaf(sc[1], part[mt][3], acc[mt][3]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&empty[s]);
+    }
+    if (cur_rb >= 0)
+        flush(cur_rb, seg_k0, (int)(u1 - 1 - (int64_t)cur_rb * a.KU) + 1);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows,
+              uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw)
+{
+    auto enc = encoder();
+    if (!enc)
+        return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+/* Per (device, stream) scratch: partial sums and row-block counters. */
+struct Scratch {
+    float *ws = nullptr;
+    size_t ws_floats = 0;
+    int *counters = nullptr;
+    size_t n_counters = 0;
+};
+std::mutex g_scratch_mu;
+std::unordered_map<uint64_t, Scratch> g_scratch;
+
+bool get_scratch(cudaStream_t st, size_t ws_floats, size_t n_counters, Scratch &out)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return false;
+    const uint64_t key = (reinterpret_cast<uint64_t>(st) << 8) ^ (uint64_t)dev;
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    Scratch &S = g_scratch[key];
+    if (S.ws_floats < ws_floats) {
+        if (S.ws)
+            cudaFree(S.ws);
+        S.ws = nullptr;
+        S.ws_floats = 0;
+        if (cudaMalloc(&S.ws, ws_floats * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        S.ws_floats = ws_floats;
+    }
+    if (S.n_counters < n_counters) {
+        if (S.counters)
+            cudaFree(S.counters);
+        S.counters = nullptr;
+        S.n_counters = 0;
+        if (cudaMalloc(&S.counters, n_counters * sizeof(int)) != cudaSuccess ||
+            cudaMemset(S.counters, 0, n_counters * sizeof(int)) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        S.n_counters = n_counters;
+    }
+    out = S;
+    return true;
+}
+
+template <int MT, bool SPLIT, bool BF16OUT>
+int launch_t(const CUtensorMap &hm, const CUtensorMap &pm, const CUtensorMap &am, const DecodeArgs &a, int grid,
+             cudaStream_t st)
+{
+    auto kern = htile_decode_kernel<MT, SPLIT, BF16OUT>;
+    if (!ensure_smem((const void *)kern, kSmem))
+        return kLaunch;
+    kern<<<grid, kThreads, kSmem, st>>>(hm, pm, am, a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+}
+
+template <bool SPLIT, bool BF16OUT>
+int launch_mt(int MT, const CUtensorMap &hm, const CUtensorMap &pm, const CUtensorMap &am, const DecodeArgs &a,
+              int grid, cudaStream_t st)
+{
+    if (MT == 1)
+        return launch_t<1, SPLIT, BF16OUT>(hm, pm, am, a, grid, st);
+    if (MT == 2)
+        return launch_t<2, SPLIT, BF16OUT>(hm, pm, am, a, grid, st);
+    return launch_t<4, SPLIT, BF16OUT>(hm, pm, am, a, grid, st);
+}
+
+} // namespace
+
+bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
+                            int M, int N, int K, int bs)
+{
+    return M >= 1 && M <= 32 && bs == 64 && K % kKU == 0 && aligned_to(hole, 16) && aligned_to(plug, 16) &&
+           aligned_to(am, 16) && aligned_to(x, 16) && N >= 1 && encoder() != nullptr;
+}
+
+int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                        OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
+{
+    CUtensorMap hm, pm, amm;
+    if (!make_map(&hm, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, kKU / 2,
+                  kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&pm, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, kKU / 2,
+                  kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&amm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4, 4,
+                  kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return kLaunch;
+    const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+    DecodeArgs a{};
+    a.x = x;
+    a.y = y;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.KU = K / kKU;
+    const int64_t rbs = (N + kRows - 1) / kRows;
+    a.units = rbs * a.KU;
+    const int grid = (int)std::min<int64_t>(a.units, sm_count());
+    /* parts per row block: at most ceil(KU / units_per_cta) + 1 */
+    const int64_t per_cta = std::max<int64_t>(1, a.units / grid);
+    a.max_parts = (int)std::min<int64_t>(grid, (a.KU + per_cta - 1) / per_cta + 1);
+    Scratch S;
+    if (!get_scratch(st, (size_t)rbs * a.max_parts * kRows * 8 * MT, (size_t)rbs * kConsumers, S))
+        return kLaunch;
+    a.ws = S.ws;
+    a.counters = S.counters;
+    const bool bf = yk == kOutBF16;
+    if (mode == kPrecise)
+        return bf ? launch_mt<true, true>(MT, hm, pm, amm, a, grid, st) : launch_mt<true, false>(MT, hm, pm, amm, a, grid, st);
+    return bf ? launch_mt<false, true>(MT, hm, pm, amm, a, grid, st) : launch_mt<false, false>(MT, hm, pm, amm, a, grid, st);
+}
+
+/* This file's kernel error word (bounded waits that ran out); clear resets it. */
+int decode_error_word(bool clear)
+{
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_decode_error, sizeof(int)) != cudaSuccess)
+        return -1;
+    if (clear && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_decode_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+} // namespace glint

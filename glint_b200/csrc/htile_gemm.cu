@@ -421,7 +421,10 @@ int read_kernel_error(bool clear)
         const int z = 0;
         cudaMemcpyToSymbol(g_glint_kernel_error, &z, sizeof(int));
     }
-    return v;
+    const int e = encode_error_word(clear), x = expand_error_word(clear), d = decode_error_word(clear);
+    if (e < 0 || x < 0 || d < 0)
+        return -1;
+    return v | e | x | d;
 }
 
 } // namespace glint

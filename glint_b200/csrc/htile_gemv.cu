@@ -313,6 +313,8 @@ int htile_gemv_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
 {
     const bool fast_shape = K % 64 == 0 && bs % 64 == 0 && aligned_to(hole, 8) && aligned_to(plug, 8) &&
                             aligned_to(x, 16) && aligned_to(am, 4) && (int64_t)N * (K / 64) < (int64_t)0xFFFFFFFF;
+    if (htile_decode_supported(hole, plug, am, x, M, N, K, bs))
+        return htile_decode_launch(hole, plug, am, x, y, yk, M, N, K, mode, st);
     if (fast_shape) {
         if (mode == kPrecise)
             return yk == kOutBF16 ? launch_gemv_slices<true, true>(hole, plug, am, x, y, M, N, K, bs, st)

@@ -440,3 +440,29 @@ def test_htile_prefill_tcgen05_vs_oracle(M, N, K):
     assert np.all(np.isfinite(yf))
     assert rel_err(yf, ref) <= FAST_TOL, rel_err(yf, ref)
     assert rel_err(yb, ref) <= FAST_TOL, rel_err(yb, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 100, 256), (3, 1000, 512), (16, 4096, 14336), (17, 384, 2048), (32, 200, 4096),
+                                   (5, 14336, 4096), (2, 130, 768)])
+def test_htile_decode_stream_k_vs_oracle(M, N, K):
+    """Decode shapes on the TMA-streamed stream-K kernel: ragged N, single-unit K,
+    row blocks split across CTAs; precise within 1e-5, fast within 1e-2, and two
+    calls give identical bits (the split parts are added in a fixed order)."""
+    from glint_b200 import glint_cuda
+    L = glint_cuda.load()
+    bits = synth_bf16(N * K, seed=N + K + M)
+    ho, po, ao = O.encode_bf16(bits, 64)
+    x = O.f32_to_bf16(np.random.default_rng(M * N).normal(0, 1, M * K).astype(np.float32))
+    ref = O.htile(ho, po, ao, x, M, N, K, 64).astype(np.float64)
+    dev = [torch.from_numpy(a).cuda() for a in (ho, po, ao)]
+    dx = to_dev_bf16(x).view(M, K)
+    yp = D().htile(dx, *dev, N, 64, mode="precise")
+    yp2 = D().htile(dx, *dev, N, 64, mode="precise")
+    yf = D().htile(dx, *dev, N, 64, mode="fast")
+    yb = D().htile(dx, *dev, N, 64, mode="fast", out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert L.glint_kernel_error(1) == 0
+    assert torch.equal(yp, yp2)
+    assert rel_err(yp.cpu().numpy(), ref) <= PRECISE_TOL
+    assert rel_err(yf.cpu().numpy(), ref) <= FAST_TOL
+    assert rel_err(yb.float().cpu().numpy(), ref) <= FAST_TOL
