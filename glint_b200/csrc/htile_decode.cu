@@ -10,8 +10,9 @@
  *     a contiguous range of units in row-block-major order (stream-K), so every
  *     SM gets the same number of units whatever N and K are;
  *   - a producer warp fetches each unit's hole and plug tiles (128 rows x 128 B,
- *     128B swizzle) and its absmax tile (128 rows x 4 blocks) with 2-D TMA loads
- *     into a 4-slot shared-memory ring (~136 KB in flight per SM);
+ *     128B swizzle), its absmax tile (128 rows x 4 blocks) and the activation
+ *     slice (8*MT rows x 256 k, 128B swizzle, rows past M zero-filled) with 2-D
+ *     TMA loads into a 3-4 slot shared-memory ring (~150 KB in flight per SM);
  *   - each of the 8 consumer warps owns 16 of the 128 rows and runs swap-AB
  *     mma.sync.m16n8k16: 16 weight rows are the A operand, up to 8 activation
  *     rows the B operand (MT such tiles).  A lane holds 16 weights of rows g and
@@ -52,12 +53,18 @@ constexpr int kRows = 128;                 /* weight rows per unit */
 constexpr int kKU = 256;                   /* k per unit */
 constexpr int kPlaneTile = kRows * kKU / 2; /* 16 KB per plane */
 constexpr int kAmTile = kRows * 4 * 4;     /* 128 rows x 4 blocks x f32 = 2 KB */
-constexpr int kSlotBytes = 2 * kPlaneTile + kAmTile;
-constexpr int kSlots = 4;
 constexpr int kConsumers = 8;
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kLutBytes = 256 * 32 * 4;
-constexpr int kSmem = 1024 + kSlots * kSlotBytes + kLutBytes + 2 * 8 * kSlots + 64;
+/* x tile of a unit: 4 boxes of 64 k x 8*MT rows (128B swizzle), 1 KB per 8 rows */
+template <int MT>
+constexpr int x_tile() { return 4 * 8 * MT * 128; }
+template <int MT>
+constexpr int slot_bytes() { return 2 * kPlaneTile + kAmTile + x_tile<MT>(); }
+template <int MT>
+constexpr int n_slots() { return MT >= 4 ? 3 : 4; }
+template <int MT>
+constexpr int smem_bytes() { return 1024 + n_slots<MT>() * slot_bytes<MT>() + kLutBytes + 2 * 8 * n_slots<MT>() + 64; }
 
 __device__ __forceinline__ void mma_bf16_16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
 {
@@ -101,17 +108,25 @@ __device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t ctas
 template <int MT, bool SPLIT, bool BF16OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     htile_decode_kernel(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap pmap,
-                        const __grid_constant__ CUtensorMap amap, const DecodeArgs a)
+                        const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap xmap,
+                        const DecodeArgs a)
 {
+    constexpr int kSlots = n_slots<MT>();
+    constexpr int kSlotBytes = slot_bytes<MT>();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint32_t *lut = reinterpret_cast<uint32_t *>(ring + kSlots * kSlotBytes);
     uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(lut) + kLutBytes);
     uint64_t *empty = full + kSlots;
 
-    for (int i = threadIdx.x; i < 256 * 32; i += kThreads) {
-        const int idx = i >> 5;
-        lut[i] = split_pair(g_cells[idx >> 4][idx & 15]);
+    /* codebook as BF16 hi/lo pairs, one replica per lane: each thread converts one
+     * entry and writes its 32 replicas */
+    if (threadIdx.x < 256) {
+        const uint32_t e = split_pair(g_cells[threadIdx.x >> 4][threadIdx.x & 15]);
+        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 32);
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            dst[r] = make_uint4(e, e, e, e);
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -142,6 +157,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_2d(slot, &hmap, &full[s], ku * (kKU / 2), rb * kRows);
                 tma_load_2d(slot + kPlaneTile, &pmap, &full[s], ku * (kKU / 2), rb * kRows);
                 tma_load_2d(slot + 2 * kPlaneTile, &amap, &full[s], ku * 4, rb * kRows);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tma_load_2d(slot + 2 * kPlaneTile + kAmTile + c * (8 * MT * 128), &xmap, &full[s], ku * kKU + c * 64, 0);
             }
             if (!ok) {
                 const int64_t issued = i;
@@ -240,22 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
         }
         const uint32_t slot = saddr(ring + s * kSlotBytes);
-        /* x fragments of this unit: row m = mt*8 + g, 16 consecutive k per lane per 64-block */
-        const int kbase = ku * kKU;
+        const uint32_t xs = slot + 2 * kPlaneTile + kAmTile;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            uint4 xb[MT][2];
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                const int m = mt * 8 + g;
-                if (m < a.M) {
-                    const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (int64_t)m * a.K + kbase + c * 64 + t * 16);
-                    xb[mt][0] = __ldg(src);
-                    xb[mt][1] = __ldg(src + 1);
-                } else {
-                    xb[mt][0] = xb[mt][1] = make_uint4(0, 0, 0, 0);
-                }
-            }
             /* packed nibbles of rows g and g+8: 8 bytes at k-byte c*32 + t*8 (128B-swizzled rows) */
             uint32_t E[2][2], O[2][2];
             float sc[2];
@@ -273,10 +278,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 sc[r] = __uint_as_float(lds32(slot + 2 * kPlaneTile + (uint32_t)(row * 4 + c) * 4u));
             }
-            float part[MT][4];
+            /* x fragments: row m = mt*8 + g of the 64-k box c, 16 consecutive k at 32*t bytes
+             * (16-byte chunks 2t and 2t+1, 128B swizzle: chunk ^ (m & 7)) */
+            uint4 xb[MT][2];
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-                part[mt][0] = part[mt][1] = part[mt][2] = part[mt][3] = 0.f;
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint32_t rowb = xs + (uint32_t)c * (8 * MT * 128) + (uint32_t)(mt * 8 + g) * 128u;
+                xb[mt][0] = lds128(rowb + ((uint32_t)((2 * t) ^ g) << 4));
+                xb[mt][1] = lds128(rowb + ((uint32_t)((2 * t + 1) ^ g) << 4));
+            }
+            /* one accumulator per MMA step keeps the four steps independent */
+            float part[4][MT][4];
 #pragma unroll
             for (int st = 0; st < 4; ++st) {
                 const int wd = st >> 1, b0 = (st & 1) * 2;
@@ -292,8 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          __byte_perm(e[0][2], e[0][3], 0x5410), __byte_perm(e[1][2], e[1][3], 0x5410)};
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
+                    part[st][mt][0] = part[st][mt][1] = part[st][mt][2] = part[st][mt][3] = 0.f;
                     const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-                    mma_bf16_16816(part[mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+                    mma_bf16_16816(part[st][mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
                 }
                 if (SPLIT) {
                     const uint32_t alo[4] = {__byte_perm(e[0][0], e[0][1], 0x7632), __byte_perm(e[1][0], e[1][1], 0x7632),
@@ -301,16 +314,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
                         const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-                        mma_bf16_16816(part[mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+                        mma_bf16_16816(part[st][mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
                     }
                 }
             }
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-                acc[mt][0] = fmaf(sc[0], part[mt][0], acc[mt][0]);
-                acc[mt][1] = fmaf(sc[0], part[mt][1], acc[mt][1]);
-                acc[mt][2] = fmaf(sc[1], part[mt][2], acc[mt][2]);
-                acc[mt][3] = fmaf(sc[1], part[mt][3], acc[mt][3]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float blk = (part[0][mt][q] + part[1][mt][q]) + (part[2][mt][q] + part[3][mt][q]);
+                    acc[mt][q] = fmaf(sc[q >> 1], blk, acc[mt][q]);
+                }
             }
         }
         __syncwarp();
@@ -396,26 +410,28 @@ bool get_scratch(cudaStream_t st, size_t ws_floats, size_t n_counters, Scratch &
     return true;
 }
 
+struct Maps {
+    CUtensorMap h, p, am, x;
+};
+
 template <int MT, bool SPLIT, bool BF16OUT>
-int launch_t(const CUtensorMap &hm, const CUtensorMap &pm, const CUtensorMap &am, const DecodeArgs &a, int grid,
-             cudaStream_t st)
+int launch_t(const Maps &m, const DecodeArgs &a, int grid, cudaStream_t st)
 {
     auto kern = htile_decode_kernel<MT, SPLIT, BF16OUT>;
-    if (!ensure_smem((const void *)kern, kSmem))
+    if (!ensure_smem((const void *)kern, smem_bytes<MT>()))
         return kLaunch;
-    kern<<<grid, kThreads, kSmem, st>>>(hm, pm, am, a);
+    kern<<<grid, kThreads, smem_bytes<MT>(), st>>>(m.h, m.p, m.am, m.x, a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
 }
 
 template <bool SPLIT, bool BF16OUT>
-int launch_mt(int MT, const CUtensorMap &hm, const CUtensorMap &pm, const CUtensorMap &am, const DecodeArgs &a,
-              int grid, cudaStream_t st)
+int launch_mt(int MT, const Maps &m, const DecodeArgs &a, int grid, cudaStream_t st)
 {
     if (MT == 1)
-        return launch_t<1, SPLIT, BF16OUT>(hm, pm, am, a, grid, st);
+        return launch_t<1, SPLIT, BF16OUT>(m, a, grid, st);
     if (MT == 2)
-        return launch_t<2, SPLIT, BF16OUT>(hm, pm, am, a, grid, st);
-    return launch_t<4, SPLIT, BF16OUT>(hm, pm, am, a, grid, st);
+        return launch_t<2, SPLIT, BF16OUT>(m, a, grid, st);
+    return launch_t<4, SPLIT, BF16OUT>(m, a, grid, st);
 }
 
 } // namespace
@@ -430,15 +446,17 @@ bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const floa
 int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
                         OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
 {
-    CUtensorMap hm, pm, amm;
-    if (!make_map(&hm, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, kKU / 2,
-                  kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&pm, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, kKU / 2,
-                  kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&amm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4, 4,
-                  kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
-        return kLaunch;
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+    Maps maps;
+    if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
+                  4, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
+                  (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B))
+        return kLaunch;
     DecodeArgs a{};
     a.x = x;
     a.y = y;
@@ -459,8 +477,8 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
     a.counters = S.counters;
     const bool bf = yk == kOutBF16;
     if (mode == kPrecise)
-        return bf ? launch_mt<true, true>(MT, hm, pm, amm, a, grid, st) : launch_mt<true, false>(MT, hm, pm, amm, a, grid, st);
-    return bf ? launch_mt<false, true>(MT, hm, pm, amm, a, grid, st) : launch_mt<false, false>(MT, hm, pm, amm, a, grid, st);
+        return bf ? launch_mt<true, true>(MT, maps, a, grid, st) : launch_mt<true, false>(MT, maps, a, grid, st);
+    return bf ? launch_mt<false, true>(MT, maps, a, grid, st) : launch_mt<false, false>(MT, maps, a, grid, st);
 }
 
 /* This file's kernel error word (bounded waits that ran out); clear resets it. */

@@ -241,10 +241,13 @@ __global__ void __launch_bounds__(kThreads, 1) htile_gemm_kernel(const __grid_co
         am_idx /= (uint32_t)args.bs64;
         uint8_t *brow_base = sB + r * 128;
         const uint32_t sw = (uint32_t)(r & 7);
-        uint4 h0, h1, p0, p1;
-        float sc = 0.f;
-        auto fetch = [&](int ks) {
-            if (rv) {
+        /* register ring: the planes and absmax of the next kPF K steps are in flight
+         * while a step is dequantised (global latency is far above one step) */
+        constexpr int kPF = 4;
+        uint4 rh0[kPF], rh1[kPF], rp0[kPF], rp1[kPF];
+        float rsc[kPF];
+        auto fetch = [&](int ks, uint4 &h0, uint4 &h1, uint4 &p0, uint4 &p1, float &sc) {
+            if (rv && ks < ksteps) {
                 const uint4 *hp = reinterpret_cast<const uint4 *>(hrow + ks * 32);
                 const uint4 *pp = reinterpret_cast<const uint4 *>(prow + ks * 32);
                 h0 = __ldcs(hp);
@@ -261,44 +264,50 @@ __global__ void __launch_bounds__(kThreads, 1) htile_gemm_kernel(const __grid_co
                 ++am_idx;
             }
         };
-        if (ksteps > 0)
-            fetch(0);
-        for (int ks = 0; ks < ksteps && alive; ++ks) {
-            const int s = ks % STAGES;
-            const uint32_t ph = (uint32_t)(ks / STAGES) & 1u;
-            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-            const uint32_t pw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-            const float scur = sc;
-            if (ks + 1 < ksteps)
-                fetch(ks + 1);
-            if (ks >= STAGES) {
-                /* one lane waits, the warp follows its verdict (keeps the warp converged) */
-                bool go = lane == 0 ? mbar_wait(&empty[s], ph ^ 1u, alive) : true;
-                if (!__shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0)) {
-                    alive = false;
+#pragma unroll
+        for (int j = 0; j < kPF; ++j)
+            fetch(j, rh0[j], rh1[j], rp0[j], rp1[j], rsc[j]);
+        for (int ks0 = 0; ks0 < ksteps && alive; ks0 += kPF) {
+#pragma unroll
+            for (int j = 0; j < kPF; ++j) {
+                const int ks = ks0 + j;
+                if (ks >= ksteps || !alive)
                     break;
+                const int s = ks % STAGES;
+                const uint32_t ph = (uint32_t)(ks / STAGES) & 1u;
+                const uint32_t hw[8] = {rh0[j].x, rh0[j].y, rh0[j].z, rh0[j].w, rh1[j].x, rh1[j].y, rh1[j].z, rh1[j].w};
+                const uint32_t pw[8] = {rp0[j].x, rp0[j].y, rp0[j].z, rp0[j].w, rp1[j].x, rp1[j].y, rp1[j].z, rp1[j].w};
+                const float scur = rsc[j];
+                fetch(ks + kPF, rh0[j], rh1[j], rp0[j], rp1[j], rsc[j]);
+                if (ks >= STAGES) {
+                    /* one lane waits, the warp follows its verdict (keeps the warp converged) */
+                    bool go = lane == 0 ? mbar_wait(&empty[s], ph ^ 1u, alive) : true;
+                    if (!__shfl_sync(0xFFFFFFFFu, go ? 1 : 0, 0)) {
+                        alive = false;
+                        break;
+                    }
                 }
-            }
-            uint8_t *brow = brow_base + s * kStageB;
+                uint8_t *brow = brow_base + s * kStageB;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                /* 8 weights: codes of elements 2b (E) and 2b+1 (O) in byte b */
-                const uint32_t E = ((hw[c] << 4) & 0xF0F0F0F0u) | (pw[c] & 0x0F0F0F0Fu);
-                const uint32_t O = (hw[c] & 0xF0F0F0F0u) | ((pw[c] >> 4) & 0x0F0F0F0Fu);
-                uint32_t o[4];
+                for (int c = 0; c < 8; ++c) {
+                    /* 8 weights: codes of elements 2b (E) and 2b+1 (O) in byte b */
+                    const uint32_t E = ((hw[c] << 4) & 0xF0F0F0F0u) | (pw[c] & 0x0F0F0F0Fu);
+                    const uint32_t O = (hw[c] & 0xF0F0F0F0u) | ((pw[c] >> 4) & 0x0F0F0F0Fu);
+                    uint32_t o[4];
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const float v0 = cl[((E >> (8 * b)) & 0xFFu) * 32] * scur;
-                    const float v1 = cl[((O >> (8 * b)) & 0xFFu) * 32] * scur;
-                    __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
-                    o[b] = *reinterpret_cast<uint32_t *>(&h2);
+                    for (int b = 0; b < 4; ++b) {
+                        const float v0 = cl[((E >> (8 * b)) & 0xFFu) * 32] * scur;
+                        const float v1 = cl[((O >> (8 * b)) & 0xFFu) * 32] * scur;
+                        __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+                        o[b] = *reinterpret_cast<uint32_t *>(&h2);
+                    }
+                    *reinterpret_cast<uint4 *>(brow + (((uint32_t)c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
-                *reinterpret_cast<uint4 *>(brow + (((uint32_t)c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&full_b[s]);
             }
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(&full_b[s]);
         }
         /* ---- epilogue: TMEM -> y.  Warp w reads TMEM lanes 32*(w % 4); warps 2..5
          * take accumulator 0 (rows 0..127), warps 6..9 accumulator 1. */
