@@ -6,14 +6,15 @@
  * row-major, overwritten.
  *
  * Decode reads each packed weight once (1.0625 B), so the kernel is a stream:
- *   - work units of 128 weight rows x 256 k; a persistent CTA (one per SM) takes
+ *   - work units of 256 weight rows x 128 k; a persistent CTA (one per SM) takes
  *     a contiguous range of units in row-block-major order (stream-K), so every
  *     SM gets the same number of units whatever N and K are;
- *   - a producer warp fetches each unit's hole and plug tiles (128 rows x 128 B,
- *     128B swizzle), its absmax tile (128 rows x 4 blocks) and the activation
- *     slice (8*MT rows x 256 k, 128B swizzle, rows past M zero-filled) with 2-D
- *     TMA loads into a 3-4 slot shared-memory ring (~150 KB in flight per SM);
- *   - each of the 8 consumer warps owns 16 of the 128 rows and runs swap-AB
+ *   - a producer warp fetches each unit's hole and plug tiles (256 rows x 64 B,
+ *     64B swizzle), its absmax tile (256 rows x 4 blocks, taken at an even unit
+ *     so the TMA coordinate stays 16-byte aligned) and the activation slice
+ *     (8*MT rows x 128 k, 128B swizzle, rows past M zero-filled) with 2-D TMA
+ *     loads into a 3-slot shared-memory ring (~115 KB in flight per SM);
+ *   - each of the 16 consumer warps owns 16 of the 256 rows and runs swap-AB
  *     mma.sync.m16n8k16: 16 weight rows are the A operand, up to 8 activation
  *     rows the B operand (MT such tiles).  A lane holds 16 weights of rows g and
  *     g+8 per 64-k block; the MMA's k positions are mapped onto those weights and
@@ -21,7 +22,8 @@
  *     the order of k);
  *   - each 64-block's sums come out of a fresh accumulator and are scaled by its
  *     absmax in f32; the codebook sits in shared memory as BF16 pairs
- *     hi = RN(cell), lo = RN(cell - hi), one replica per lane: precise mode
+ *     hi = RN(cell), lo = RN(cell - hi), one replica per lane with a 256-byte
+ *     entry stride, so a lookup address is one byte permute: precise mode
  *     issues an MMA for each half (~17 significant bits per weight, f32-class
  *     results), fast mode uses hi only;
  *   - a row block split between CTAs is finished by whichever part arrives
@@ -49,22 +51,24 @@ __device__ int g_decode_error = 0;
 
 namespace {
 
-constexpr int kRows = 128;                 /* weight rows per unit */
-constexpr int kKU = 256;                   /* k per unit */
-constexpr int kPlaneTile = kRows * kKU / 2; /* 16 KB per plane */
-constexpr int kAmTile = kRows * 4 * 4;     /* 128 rows x 4 blocks x f32 = 2 KB */
-constexpr int kConsumers = 8;
+constexpr int kRows = 256;                 /* weight rows per unit */
+constexpr int kKU = 128;                   /* k per unit */
+constexpr int kPlaneTile = kRows * kKU / 2; /* 16 KB per plane (64 B per row, 64B swizzle) */
+constexpr int kAmTile = kRows * 4 * 4;     /* 256 rows x 4 blocks x f32: this unit's 2 blocks + its neighbour's */
+constexpr int kConsumers = 16;             /* 16 rows each */
 constexpr int kThreads = (kConsumers + 1) * 32;
-constexpr int kLutBytes = 256 * 32 * 4;
-/* x tile of a unit: 4 boxes of 64 k x 8*MT rows (128B swizzle), 1 KB per 8 rows */
+/* codebook hi|lo pairs, one replica per lane, entry stride 256 B: the lookup address
+ * of code byte b of a word is one byte permute, (code << 8) | (lane << 2) */
+constexpr int kLutBytes = 256 * 256;
+/* x tile of a unit: 2 boxes of 64 k x 8*MT rows (128B swizzle), 1 KB per 8 rows */
 template <int MT>
-constexpr int x_tile() { return 4 * 8 * MT * 128; }
+constexpr int x_tile() { return 2 * 8 * MT * 128; }
 template <int MT>
 constexpr int slot_bytes() { return 2 * kPlaneTile + kAmTile + x_tile<MT>(); }
 template <int MT>
-constexpr int n_slots() { return MT >= 4 ? 3 : 4; }
+constexpr int n_slots() { return 3; }
 template <int MT>
-constexpr int smem_bytes() { return 1024 + n_slots<MT>() * slot_bytes<MT>() + kLutBytes + 2 * 8 * n_slots<MT>() + 64; }
+constexpr int smem_bytes() { return kLutBytes + 1024 + n_slots<MT>() * slot_bytes<MT>() + 2 * 8 * n_slots<MT>() + 64; }
 
 __device__ __forceinline__ void mma_bf16_16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1)
 {
@@ -114,16 +118,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kSlots = n_slots<MT>();
     constexpr int kSlotBytes = slot_bytes<MT>();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint32_t *lut = reinterpret_cast<uint32_t *>(ring + kSlots * kSlotBytes);
-    uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(lut) + kLutBytes);
+    uint32_t *lut = reinterpret_cast<uint32_t *>(smem_raw);
+    uint8_t *ring = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + kSlots * kSlotBytes);
     uint64_t *empty = full + kSlots;
 
-    /* codebook as BF16 hi/lo pairs, one replica per lane: each thread converts one
-     * entry and writes its 32 replicas */
+    /* codebook as BF16 hi/lo pairs, one replica per lane (first 128 B of each 256-B
+     * entry row): each thread converts one entry and writes its 32 replicas */
     if (threadIdx.x < 256) {
         const uint32_t e = split_pair(g_cells[threadIdx.x >> 4][threadIdx.x & 15]);
-        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 32);
+        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 64);
 #pragma unroll
         for (int r = 0; r < 8; ++r)
             dst[r] = make_uint4(e, e, e, e);
@@ -156,9 +161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_expect_tx(&full[s], kSlotBytes);
                 tma_load_2d(slot, &hmap, &full[s], ku * (kKU / 2), rb * kRows);
                 tma_load_2d(slot + kPlaneTile, &pmap, &full[s], ku * (kKU / 2), rb * kRows);
-                tma_load_2d(slot + 2 * kPlaneTile, &amap, &full[s], ku * 4, rb * kRows);
+                /* absmax box at an even unit so the x coordinate stays 16-byte aligned */
+                tma_load_2d(slot + 2 * kPlaneTile, &amap, &full[s], (ku >> 1) * 4, rb * kRows);
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 2; ++c)
                     tma_load_2d(slot + 2 * kPlaneTile + kAmTile + c * (8 * MT * 128), &xmap, &full[s], ku * kKU + c * 64, 0);
             }
             if (!ok) {
@@ -174,7 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     /* consumer warp: rows r0 + g and r0 + g + 8 of each unit's 128 */
     const int g = (int)(lane >> 2), t = (int)(lane & 3);
     const int r0 = warp * 16;
-    const uint32_t lut_lane = saddr(lut) + lane * 4u;
+    const uint32_t lut_base = saddr(lut);
+    const uint32_t lane4 = lane * 4u;
     float acc[MT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -259,16 +266,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t slot = saddr(ring + s * kSlotBytes);
         const uint32_t xs = slot + 2 * kPlaneTile + kAmTile;
+        const uint32_t am_col = (uint32_t)(ku & 1) * 2;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            /* packed nibbles of rows g and g+8: 8 bytes at k-byte c*32 + t*8 (128B-swizzled rows) */
+        for (int c = 0; c < 2; ++c) {
+            /* packed nibbles of rows g and g+8: 8 bytes at k-byte c*32 + t*8 of the
+             * row's 64 B (64B swizzle: 16-byte chunk j sits at j ^ ((row >> 1) & 3)) */
             uint32_t E[2][2], O[2][2];
             float sc[2];
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int row = r0 + g + 8 * r;
-                const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(row & 7);
-                const uint32_t off = (uint32_t)row * 128u + (chunk << 4) + (uint32_t)(t & 1) * 8u;
+                const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)((row >> 1) & 3);
+                const uint32_t off = (uint32_t)row * 64u + (chunk << 4) + (uint32_t)(t & 1) * 8u;
                 const uint2 hw = lds64(slot + off), pw = lds64(slot + kPlaneTile + off);
                 const uint32_t hv[2] = {hw.x, hw.y}, pv[2] = {pw.x, pw.y};
 #pragma unroll
@@ -276,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     E[r][wd] = ((hv[wd] << 4) & 0xF0F0F0F0u) | (pv[wd] & 0x0F0F0F0Fu);
                     O[r][wd] = (hv[wd] & 0xF0F0F0F0u) | ((pv[wd] >> 4) & 0x0F0F0F0Fu);
                 }
-                sc[r] = __uint_as_float(lds32(slot + 2 * kPlaneTile + (uint32_t)(row * 4 + c) * 4u));
+                sc[r] = __uint_as_float(lds32(slot + 2 * kPlaneTile + (uint32_t)row * 16u + (am_col + c) * 4u));
             }
             /* x fragments: row m = mt*8 + g of the 64-k box c, 16 consecutive k at 32*t bytes
              * (16-byte chunks 2t and 2t+1, 128B swizzle: chunk ^ (m & 7)) */
@@ -287,26 +296,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 xb[mt][0] = lds128(rowb + ((uint32_t)((2 * t) ^ g) << 4));
                 xb[mt][1] = lds128(rowb + ((uint32_t)((2 * t + 1) ^ g) << 4));
             }
-            /* one accumulator per MMA step keeps the four steps independent */
-            float part[4][MT][4];
+            /* two accumulators (even and odd MMA steps) keep the chains independent */
+            float part[2][MT][4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                    part[h][mt][0] = part[h][mt][1] = part[h][mt][2] = part[h][mt][3] = 0.f;
 #pragma unroll
             for (int st = 0; st < 4; ++st) {
                 const int wd = st >> 1, b0 = (st & 1) * 2;
                 uint32_t e[2][4];
 #pragma unroll
                 for (int r = 0; r < 2; ++r) {
-                    e[r][0] = lds32(lut_lane + (((E[r][wd] >> (8 * b0)) & 0xFFu) << 7));
-                    e[r][1] = lds32(lut_lane + (((O[r][wd] >> (8 * b0)) & 0xFFu) << 7));
-                    e[r][2] = lds32(lut_lane + (((E[r][wd] >> (8 * b0 + 8)) & 0xFFu) << 7));
-                    e[r][3] = lds32(lut_lane + (((O[r][wd] >> (8 * b0 + 8)) & 0xFFu) << 7));
+                    /* address = (code << 8) | (lane << 2): byte b0 or b0+1 of E / O into byte 1 */
+                    e[r][0] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | (b0 << 4)));
+                    e[r][1] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | (b0 << 4)));
+                    e[r][2] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
+                    e[r][3] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
                 }
                 const uint32_t ahi[4] = {__byte_perm(e[0][0], e[0][1], 0x5410), __byte_perm(e[1][0], e[1][1], 0x5410),
                                          __byte_perm(e[0][2], e[0][3], 0x5410), __byte_perm(e[1][2], e[1][3], 0x5410)};
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
-                    part[st][mt][0] = part[st][mt][1] = part[st][mt][2] = part[st][mt][3] = 0.f;
                     const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-                    mma_bf16_16816(part[st][mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+                    mma_bf16_16816(part[st & 1][mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
                 }
                 if (SPLIT) {
                     const uint32_t alo[4] = {__byte_perm(e[0][0], e[0][1], 0x7632), __byte_perm(e[1][0], e[1][1], 0x7632),
@@ -314,17 +328,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
                         const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-                        mma_bf16_16816(part[st][mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+                        mma_bf16_16816(part[st & 1][mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
                     }
                 }
             }
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float blk = (part[0][mt][q] + part[1][mt][q]) + (part[2][mt][q] + part[3][mt][q]);
-                    acc[mt][q] = fmaf(sc[q >> 1], blk, acc[mt][q]);
-                }
+                for (int q = 0; q < 4; ++q)
+                    acc[mt][q] = fmaf(sc[q >> 1], part[0][mt][q] + part[1][mt][q], acc[mt][q]);
             }
         }
         __syncwarp();
@@ -439,7 +451,8 @@ int launch_mt(int MT, const Maps &m, const DecodeArgs &a, int grid, cudaStream_t
 bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
                             int M, int N, int K, int bs)
 {
-    return M >= 1 && M <= 32 && bs == 64 && K % kKU == 0 && aligned_to(hole, 16) && aligned_to(plug, 16) &&
+    /* K % 256: the absmax rows (K/64 floats) must be a multiple of 16 bytes for TMA */
+    return M >= 1 && M <= 32 && bs == 64 && K % 256 == 0 && aligned_to(hole, 16) && aligned_to(plug, 16) &&
            aligned_to(am, 16) && aligned_to(x, 16) && N >= 1 && encoder() != nullptr;
 }
 
@@ -449,9 +462,9 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
     Maps maps;
     if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
         !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
                   4, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
