@@ -52,9 +52,9 @@ namespace {
 constexpr int kMaxItems = 32;
 constexpr int kEncReplicas = 16;
 constexpr int kLutBytes = kNumCells * kEncReplicas * (int)sizeof(uint2); /* 65,664 */
-constexpr int kSlotBytes = 24 * 1024;                                   /* one unit of input */
-constexpr int kSlots = 6;
-constexpr int kWpl = 16;                                                /* weights per consumer lane */
+constexpr int kSlotBytes = 48 * 1024;                                   /* one unit of input */
+constexpr int kSlots = 3;
+constexpr int kWpl = 32;                                                /* weights per consumer lane */
 
 
 struct EncodeBatch {
@@ -68,14 +68,29 @@ struct EncodeBatch {
     int count;
 };
 
-/* one unit fills a slot: 12288 BF16 or 6144 f32 weights, 16 per consumer lane */
+/* one unit fills a slot: 24576 BF16 or 12288 f32 weights, 32 per consumer lane */
 template <typename In>
 constexpr int unit_w() { return kSlotBytes / (int)sizeof(In); }
 template <typename In>
 constexpr int consumer_warps() { return unit_w<In>() / (32 * kWpl); }
 template <typename In>
 constexpr int enc_threads() { return (consumer_warps<In>() + 1) * 32; }
-constexpr int kEncSmem = kLutBytes + kSlots * kSlotBytes + 2 * 8 * kSlots + 128;
+constexpr int kMetaBytes = 48;
+constexpr int kEncSmem = kLutBytes + kSlots * kSlotBytes + kSlots * kMetaBytes + 2 * 8 * kSlots + 128;
+
+/* What the producer tells the consumers about the unit in a slot: pointers already
+ * offset to the unit's first element, how many weights it holds, and whether its
+ * input sits in the slot (or must be read from global memory). */
+struct UnitMeta {
+    const void *src;
+    uint8_t *hole;
+    uint8_t *plug;
+    float *absmax;
+    int valid;
+    int staged;
+    int pad[2];
+};
+static_assert(sizeof(UnitMeta) == kMetaBytes, "slot descriptor layout");
 
 /* generic-path lookup (non-replicated table) */
 __device__ __forceinline__ uint32_t lut_code(const uint2 *lut, int stride, float v)
@@ -179,17 +194,17 @@ __device__ __forceinline__ void pack8(const uint32_t *c, uint32_t &hw, uint32_t 
     pw = (A & 0x0F0F0F0Fu) | ((B << 4) & 0xF0F0F0F0u);
 }
 
-/* Codes of the lane's 16 weights, all in one block of absmax s. */
-__device__ __forceinline__ void codes16(const Lane16 &L, float s, bool nan_free, uint32_t lut_c, uint32_t (&c)[16])
+/* Codes of 16 weights of one block of absmax s; y = RN(1/s) when `fast` (the block
+ * is NaN-free and s lies in the Markstein range). */
+__device__ __forceinline__ void codes16(const float *w, float s, float y, bool fast, uint32_t lut_c, uint32_t (&c)[16])
 {
-    if (nan_free && s >= kMarksteinLo && s <= kMarksteinHi) {
+    if (fast) {
         /* v = RN(w / s) exactly, so v is in [-1, 1] and the cell needs no clamp */
-        const float y = __frcp_rn(s);
         const uint64_t y2 = pack2(y, y), ns2 = pack2(-s, -s);
         const uint64_t k256 = pack2(256.0f, 256.0f), kadd = pack2(kMagic + 256.0f, kMagic + 256.0f);
 #pragma unroll
         for (int j = 0; j < 16; j += 2) {
-            const uint64_t w2 = pack2(L.w[j], L.w[j + 1]);
+            const uint64_t w2 = pack2(w[j], w[j + 1]);
             const uint64_t q2 = mul2(w2, y2);
             const uint64_t v2 = fma2(fma2(q2, ns2, w2), y2, q2);
             const uint64_t t2 = fma2(v2, k256, kadd);
@@ -204,11 +219,18 @@ __device__ __forceinline__ void codes16(const Lane16 &L, float s, bool nan_free,
     } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            const float v = (s == 0.f) ? 0.f : __fdiv_rn(L.w[j], s);
+            const float v = (s == 0.f) ? 0.f : __fdiv_rn(w[j], s);
             const uint2 e = lds64((cell_of(v) + kMagicBits) * (uint32_t)(kEncReplicas * 8) + lut_c);
             c[j] = e.y + (v >= __uint_as_float(e.x) ? 1u : 0u);
         }
     }
+}
+
+/* hole and plug bytes of 16 codes (8 bytes each, as two words) */
+__device__ __forceinline__ void pack16(const uint32_t (&c)[16], uint32_t &h0, uint32_t &h1, uint32_t &p0, uint32_t &p1)
+{
+    pack8(c, h0, p0);
+    pack8(c + 8, h1, p1);
 }
 
 template <int G>
@@ -220,23 +242,37 @@ __device__ __forceinline__ uint32_t group_max_u32(uint32_t v)
     return v;
 }
 
+/* the block absmax of one lane group: NaN-ignoring max over the group's weights */
+template <int G>
+__device__ __forceinline__ float nan_skipping_max(const float *w, int n)
+{
+    float a = 0.f;
+    for (int j = 0; j < n; ++j)
+        a = fmaxf(a, fabsf(w[j]));
+    const unsigned act = __activemask();
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1)
+        a = fmaxf(a, __shfl_xor_sync(act, a, o));
+    return a;
+}
+
 template <typename In, int BS_LOG2>
 __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(const __grid_constant__ EncodeBatch b)
 {
     constexpr int UW = unit_w<In>();
     constexpr int CW = consumer_warps<In>();
-    constexpr int G = (1 << BS_LOG2) / kWpl; /* lanes per block */
+    /* lanes per block for bs >= 32 (a lane's 32 weights share one block); for bs == 16
+     * each 16-weight half of a lane is its own block */
+    constexpr int G = BS_LOG2 >= 5 ? (1 << BS_LOG2) / kWpl : 1;
     extern __shared__ __align__(128) uint8_t smem[];
     uint2 *lut = reinterpret_cast<uint2 *>(smem);
     uint8_t *ring = smem + kLutBytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + kSlots * kSlotBytes);
+    UnitMeta *meta = reinterpret_cast<UnitMeta *>(ring + kSlots * kSlotBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(meta + kSlots);
     uint64_t *empty = full + kSlots;
-    __shared__ int64_t unit_end[kMaxItems];
 
     for (int i = threadIdx.x; i < kNumCells * kEncReplicas; i += enc_threads<In>())
         lut[i] = g_encode_lut[i / kEncReplicas];
-    if (threadIdx.x < kMaxItems)
-        unit_end[threadIdx.x] = threadIdx.x < b.count ? b.unit_end[threadIdx.x] : INT64_MAX;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&full[s], 1);
@@ -248,10 +284,10 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
 
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = lane_id();
-    const int64_t total = unit_end[b.count - 1];
+    const int64_t total = b.unit_end[b.count - 1];
 
     if (warp == CW) {
-        /* producer: one bulk copy per full, aligned unit */
+        /* producer: publish each unit's descriptor, then one bulk copy per full, aligned unit */
         if (lane == 0) {
             int it = 0;
             int64_t i = 0;
@@ -261,12 +297,21 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
                 const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
                 if (i >= kSlots && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_encode_error)))
                     break;
-                while (unit_end[it] <= u)
+                while (b.unit_end[it] <= u)
                     ++it;
-                const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * UW;
-                if (b.n[it] - off >= UW && !((b.direct >> it) & 1u)) {
+                const int64_t off = (u - (it ? b.unit_end[it - 1] : 0)) * UW;
+                const int64_t left = b.n[it] - off;
+                const bool staged = left >= UW && !((b.direct >> it) & 1u);
+                UnitMeta &m = meta[s];
+                m.src = static_cast<const In *>(b.w[it]) + off;
+                m.hole = b.hole[it] + off / 2;
+                m.plug = b.plug[it] + off / 2;
+                m.absmax = b.absmax[it] + (off >> BS_LOG2);
+                m.valid = left >= UW ? UW : (int)left;
+                m.staged = staged ? 1 : 0;
+                if (staged) {
                     mbar_expect_tx(&full[s], kSlotBytes);
-                    bulk_g2s(ring + s * kSlotBytes, static_cast<const In *>(b.w[it]) + off, kSlotBytes, &full[s]);
+                    bulk_g2s(ring + s * kSlotBytes, m.src, kSlotBytes, &full[s]);
                 } else {
                     mbar_arrive(&full[s]);
                 }
@@ -282,10 +327,9 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
         return;
     }
 
-    /* consumers: lane owns 16 consecutive weights; a block of bs weights is bs/16 lanes */
+    /* consumers: a lane owns 32 consecutive weights of a unit */
     const uint32_t lut_c = saddr(lut) + (lane & (kEncReplicas - 1)) * 8u - kMagicBits * (uint32_t)(kEncReplicas * 8);
     const int rel = (warp * 32 + (int)lane) * kWpl; /* element offset inside a unit */
-    int it = 0;
     int64_t i = 0;
     for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
         const int s = (int)(i % kSlots);
@@ -293,59 +337,78 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
         const bool ok = lane == 0 ? mbar_wait_bounded(&full[s], ph, &g_encode_error) : true;
         if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
             break;
-        while (unit_end[it] <= u)
-            ++it;
-        const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * UW;
-        const int64_t n = b.n[it];
-        const int64_t e0 = off + rel;
-        const int valid = n - e0 >= kWpl ? kWpl : (n - e0 > 0 ? (int)(n - e0) : 0);
-        const bool staged = n - off >= UW && !((b.direct >> it) & 1u);
-        const In *src = static_cast<const In *>(b.w[it]);
-        uint32_t words[Words<In>::N];
-        if (staged)
-            smem_words(src, saddr(ring + s * kSlotBytes) + rel * (int)sizeof(In), words);
-        else
-            global_words(src, e0, valid, words);
+        const UnitMeta m = meta[s];
+        const int valid = m.valid - rel >= kWpl ? kWpl : (m.valid - rel > 0 ? m.valid - rel : 0);
+        const In *src = static_cast<const In *>(m.src);
+        uint32_t wa[Words<In>::N], wb[Words<In>::N];
+        if (m.staged) {
+            const uint32_t a = saddr(ring + s * kSlotBytes) + rel * (int)sizeof(In);
+            smem_words(src, a, wa);
+            smem_words(src, a + 16 * (int)sizeof(In), wb);
+        } else {
+            global_words(src, rel, valid, wa);
+            global_words(src, rel + 16, valid - 16, wb);
+        }
         __syncwarp();
         if (lane == 0)
             mbar_arrive(&empty[s]); /* the slot's data now lives in registers */
 
-        Lane16 L;
-        from_words(src, words, L);
-        const uint32_t mag = group_max_u32<G>(L.mag);
-        const bool nan_free = mag <= 0x7F800000u; /* NaN sorts above inf */
-        float sc = __uint_as_float(mag);
-        if (!nan_free) {
-            /* block holds a NaN: absmax skips it, as the reference's (a > m) does */
-            float a = 0.f;
+        Lane16 A, B;
+        from_words(src, wa, A);
+        from_words(src, wb, B);
+        uint32_t ca[16], cb[16];
+        float sa, sb;
+        if (BS_LOG2 >= 5) {
+            const uint32_t mag = group_max_u32<G>(max(A.mag, B.mag));
+            const bool nan_free = mag <= 0x7F800000u; /* NaN sorts above inf */
+            float sc = __uint_as_float(mag);
+            if (!nan_free) {
+                float both[32];
 #pragma unroll
-            for (int j = 0; j < kWpl; ++j)
-                a = fmaxf(a, fabsf(L.w[j]));
-            const unsigned act = __activemask();
-#pragma unroll
-            for (int o = G / 2; o > 0; o >>= 1)
-                a = fmaxf(a, __shfl_xor_sync(act, a, o));
-            sc = a;
+                for (int j = 0; j < 16; ++j)
+                    both[j] = A.w[j], both[16 + j] = B.w[j];
+                sc = nan_skipping_max<G>(both, 32); /* absmax skips NaN, as the reference's (a > m) does */
+            }
+            const bool fast = nan_free && sc >= kMarksteinLo && sc <= kMarksteinHi;
+            const float y = fast ? __frcp_rn(sc) : 0.f;
+            codes16(A.w, sc, y, fast, lut_c, ca);
+            codes16(B.w, sc, y, fast, lut_c, cb);
+            sa = sb = sc;
+        } else {
+            /* bs == 16: two blocks per lane */
+            const bool nfa = A.mag <= 0x7F800000u, nfb = B.mag <= 0x7F800000u;
+            sa = nfa ? __uint_as_float(A.mag) : nan_skipping_max<1>(A.w, 16);
+            sb = nfb ? __uint_as_float(B.mag) : nan_skipping_max<1>(B.w, 16);
+            const bool fa = nfa && sa >= kMarksteinLo && sa <= kMarksteinHi;
+            const bool fb = nfb && sb >= kMarksteinLo && sb <= kMarksteinHi;
+            codes16(A.w, sa, fa ? __frcp_rn(sa) : 0.f, fa, lut_c, ca);
+            codes16(B.w, sb, fb ? __frcp_rn(sb) : 0.f, fb, lut_c, cb);
         }
-        uint32_t c[16];
-        codes16(L, sc, nan_free, lut_c, c);
-        uint32_t hw[2], pw[2];
-        pack8(c, hw[0], pw[0]);
-        pack8(c + 8, hw[1], pw[1]);
-        if (valid > 0 && (lane & (G - 1)) == 0)
-            b.absmax[it][e0 >> BS_LOG2] = sc;
+        uint32_t h[4], p[4];
+        pack16(ca, h[0], h[1], p[0], p[1]);
+        pack16(cb, h[2], h[3], p[2], p[3]);
+        if (BS_LOG2 >= 5) {
+            if (valid > 0 && (lane & (G - 1)) == 0)
+                m.absmax[rel >> BS_LOG2] = sa;
+        } else {
+            if (valid > 0)
+                m.absmax[rel >> BS_LOG2] = sa;
+            if (valid > 16)
+                m.absmax[(rel >> BS_LOG2) + 1] = sb;
+        }
+        uint8_t *hd = m.hole + (rel >> 1), *pd = m.plug + (rel >> 1);
         if (valid == kWpl) {
-            __stcs(reinterpret_cast<uint2 *>(b.hole[it] + (e0 >> 1)), make_uint2(hw[0], hw[1]));
-            __stcs(reinterpret_cast<uint2 *>(b.plug[it] + (e0 >> 1)), make_uint2(pw[0], pw[1]));
+            __stcs(reinterpret_cast<uint4 *>(hd), make_uint4(h[0], h[1], h[2], h[3]));
+            __stcs(reinterpret_cast<uint4 *>(pd), make_uint4(p[0], p[1], p[2], p[3]));
         } else if (valid > 0) {
             /* ragged end: nibbles past n stay 0 (the odd-n pad nibble) */
-            const uint64_t keep = ~0ull >> (64 - 4 * valid);
-            const uint64_t h64 = ((uint64_t)hw[1] << 32 | hw[0]) & keep, p64 = ((uint64_t)pw[1] << 32 | pw[0]) & keep;
 #pragma unroll
-            for (int bb = 0; bb < 8; ++bb) {
+            for (int bb = 0; bb < 16; ++bb) {
                 if (bb < (valid + 1) / 2) {
-                    b.hole[it][(e0 >> 1) + bb] = (uint8_t)(h64 >> (8 * bb));
-                    b.plug[it][(e0 >> 1) + bb] = (uint8_t)(p64 >> (8 * bb));
+                    const int e = 2 * bb; /* first element of this byte */
+                    const uint32_t keep = (e + 1 < valid) ? 0xFFu : 0x0Fu;
+                    hd[bb] = (uint8_t)((h[bb >> 2] >> (8 * (bb & 3))) & keep);
+                    pd[bb] = (uint8_t)((p[bb >> 2] >> (8 * (bb & 3))) & keep);
                 }
             }
         }
@@ -469,7 +532,7 @@ int encode_launch(const EncodeJob *jobs, int count, int bs, bool f32_in, cudaStr
             continue;
         if (!j.w || !j.hole || !j.plug || !j.absmax)
             return kBadArg;
-        const bool aligned = aligned_to(j.hole, 8) && aligned_to(j.plug, 8) && aligned_to(j.absmax, 4);
+        const bool aligned = aligned_to(j.hole, 16) && aligned_to(j.plug, 16) && aligned_to(j.absmax, 4);
         if (!fast_bs || !aligned) {
             rc = f32_in ? launch_generic<float>(j, bs, st) : launch_generic<uint16_t>(j, bs, st);
             continue;

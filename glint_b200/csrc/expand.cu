@@ -6,16 +6,17 @@
  * multiply, then for BF16 a round to nearest even with the NaN rule
  * (u >> 16) | 0x40.
  *
- * Persistent CTAs of 8 consumer warps and one producer warp: the producer
- * streams 2 KB of each plane per 4096-weight unit into a 10-slot shared-memory
- * ring with cp.async.bulk; a consumer lane expands two groups of 8 weights per
- * unit, one 16-byte BF16 store each (512 contiguous bytes per warp store).  The
- * 256-entry f32 codebook sits in shared memory with one replica per lane
- * (32 KB), so the lookups never conflict.  absmax is read through the read-only
- * cache (one load per 8 weights, shared by the lanes of a block).  Blocksizes
- * that are not a power of two >= 8 and unaligned outputs go through a
- * one-thread-per-weight kernel; ragged last units and planes that are not
- * 16-byte aligned are read straight from global memory.
+ * One persistent CTA per SM: 16 consumer warps and a producer warp that streams
+ * each unit of 16384 weights (8 KB of each plane and the unit's absmax) into a
+ * 6-slot shared-memory ring with cp.async.bulk, and publishes a small descriptor
+ * of the unit (pointers, valid count) beside it.  A consumer lane expands four
+ * groups of 8 weights per unit, one 16-byte BF16 store each (512 contiguous
+ * bytes per warp store).  The 256-entry f32 codebook sits in shared memory with
+ * one replica per lane at a 256-byte entry stride, so each lookup address is one
+ * byte permute; the scale multiply runs two weights per f32x2 instruction.
+ * Blocksizes that are not a power of two in [8, 1024] and unaligned outputs go
+ * through a one-thread-per-weight kernel; ragged last units and unaligned planes
+ * are read straight from global memory.
  *
  * NaN absmax: the reference's host expand multiplies on x86, which returns the
  * NaN operand (quietened) unchanged, so the product carries absmax's bits.  The
@@ -35,15 +36,19 @@ __device__ int g_expand_error = 0;
 namespace {
 
 constexpr int kMaxItems = 32;
-constexpr int kUnitW = 4096;                 /* weights per ring slot */
-constexpr int kPlaneBytes = kUnitW / 2;      /* 2 KB of each plane per unit */
-constexpr int kSlotBytes = 2 * kPlaneBytes;  /* hole | plug */
-constexpr int kSlots = 10;
-constexpr int kConsumerWarps = 8;            /* 512 weights per warp per unit */
+constexpr int kConsumerWarps = 16;
+constexpr int kGroups = 4;                               /* 8-weight groups per lane per unit */
+constexpr int kUnitW = kConsumerWarps * 32 * 8 * kGroups; /* 16384 weights per ring slot */
+constexpr int kPlaneBytes = kUnitW / 2;                  /* 8 KB of each plane per unit */
+constexpr int kAmMax = kUnitW / 8 * 4;                   /* absmax bytes of a unit at bs = 8 */
+constexpr int kSlotBytes = 2 * kPlaneBytes + kAmMax;
+constexpr int kSlots = 6;
 constexpr int kExpThreads = (kConsumerWarps + 1) * 32;
-constexpr int kLutBytes = 256 * 32 * (int)sizeof(float);
-constexpr int kExpSmem = kLutBytes + kSlots * kSlotBytes + 2 * 8 * kSlots + 128;
-
+/* f32 codebook, one replica per lane, entry stride 256 B: a lookup address is one
+ * byte permute, (code << 8) | (lane << 2) */
+constexpr int kLutBytes = 256 * 256;
+constexpr int kMetaBytes = 48;
+constexpr int kExpSmem = kLutBytes + kSlots * kSlotBytes + kSlots * kMetaBytes + 2 * 8 * kSlots + 128;
 
 struct ExpandBatch {
     const uint8_t *hole[kMaxItems];
@@ -57,36 +62,67 @@ struct ExpandBatch {
     int bs_log2;
 };
 
+/* The producer's description of the unit in a slot (pointers offset to the unit). */
+struct UnitMeta {
+    const uint8_t *hole;
+    const uint8_t *plug;
+    const float *absmax;
+    void *out;
+    int valid;  /* weights in the unit */
+    int staged; /* planes and absmax sit in the slot */
+    int pad[2];
+};
+static_assert(sizeof(UnitMeta) == kMetaBytes, "slot descriptor layout");
+
 __device__ __forceinline__ float quiet_nan_of(float s) { return __uint_as_float(__float_as_uint(s) | 0x00400000u); }
 
-/* values of the 8 weights whose nibbles are in H and P (lo nibble first);
- * cells_lane = shared address of this lane's replica (entry stride 128 B) */
-__device__ __forceinline__ void dequant8(uint32_t cells_lane, uint32_t H, uint32_t P, float s, float v[8])
+__device__ __forceinline__ uint64_t pack2f(float lo, float hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2f(uint64_t v, float &lo, float &hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+__device__ __forceinline__ uint64_t mul2f(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+/* values of the 8 weights whose nibbles are in H and P (lo nibble first), one f32
+ * multiply each, two per instruction */
+__device__ __forceinline__ void dequant8(uint32_t lut_base, uint32_t lane4, uint32_t H, uint32_t P, float s, float v[8])
 {
     /* byte b of E holds the code of element 2b, byte b of O the code of element 2b+1 */
     const uint32_t E = ((H << 4) & 0xF0F0F0F0u) | (P & 0x0F0F0F0Fu);
     const uint32_t O = (H & 0xF0F0F0F0u) | ((P >> 4) & 0x0F0F0F0Fu);
+    const uint64_t s2 = pack2f(s, s);
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-        v[2 * b] = __uint_as_float(lds32(cells_lane + (((E >> (8 * b)) & 0xFFu) << 7))) * s;
-        v[2 * b + 1] = __uint_as_float(lds32(cells_lane + (((O >> (8 * b)) & 0xFFu) << 7))) * s;
+        const float c0 = __uint_as_float(lds32(lut_base + __byte_perm(E, lane4, 0x5504 | (b << 4))));
+        const float c1 = __uint_as_float(lds32(lut_base + __byte_perm(O, lane4, 0x5504 | (b << 4))));
+        unpack2f(mul2f(pack2f(c0, c1), s2), v[2 * b], v[2 * b + 1]);
     }
 }
 
 template <bool BF16>
-__global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __grid_constant__ ExpandBatch b)
+__global__ void __launch_bounds__(kExpThreads, 1) expand_stream_kernel(const __grid_constant__ ExpandBatch b)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    float *cells_rep = reinterpret_cast<float *>(smem);
+    float *lut = reinterpret_cast<float *>(smem);
     uint8_t *ring = smem + kLutBytes;
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + kSlots * kSlotBytes);
+    UnitMeta *meta = reinterpret_cast<UnitMeta *>(ring + kSlots * kSlotBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(meta + kSlots);
     uint64_t *empty = full + kSlots;
-    __shared__ int64_t unit_end[kMaxItems];
 
-    for (int i = threadIdx.x; i < 256 * 32; i += kExpThreads)
-        cells_rep[i] = (&g_cells[0][0])[i >> 5];
-    if (threadIdx.x < kMaxItems)
-        unit_end[threadIdx.x] = threadIdx.x < b.count ? b.unit_end[threadIdx.x] : INT64_MAX;
+    if (threadIdx.x < 256) {
+        const float c = (&g_cells[0][0])[threadIdx.x];
+        float4 *dst = reinterpret_cast<float4 *>(lut + threadIdx.x * 64);
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            dst[r] = make_float4(c, c, c, c);
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&full[s], 1);
@@ -97,7 +133,8 @@ __global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __g
     __syncthreads();
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = lane_id();
-    const int64_t total = unit_end[b.count - 1];
+    const int64_t total = b.unit_end[b.count - 1];
+    const int L2 = b.bs_log2;
 
     if (warp == kConsumerWarps) {
         if (lane == 0) {
@@ -109,13 +146,24 @@ __global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __g
                 const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
                 if (i >= kSlots && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_expand_error)))
                     break;
-                while (unit_end[it] <= u)
+                while (b.unit_end[it] <= u)
                     ++it;
-                const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * kUnitW;
-                if (b.n[it] - off >= kUnitW && !((b.direct >> it) & 1u)) {
-                    mbar_expect_tx(&full[s], kSlotBytes);
-                    bulk_g2s(ring + s * kSlotBytes, b.hole[it] + off / 2, kPlaneBytes, &full[s]);
-                    bulk_g2s(ring + s * kSlotBytes + kPlaneBytes, b.plug[it] + off / 2, kPlaneBytes, &full[s]);
+                const int64_t off = (u - (it ? b.unit_end[it - 1] : 0)) * kUnitW;
+                const int64_t left = b.n[it] - off;
+                const bool staged = left >= kUnitW && !((b.direct >> it) & 1u);
+                UnitMeta &m = meta[s];
+                m.hole = b.hole[it] + off / 2;
+                m.plug = b.plug[it] + off / 2;
+                m.absmax = b.absmax[it] + (off >> L2);
+                m.out = static_cast<char *>(b.out[it]) + off * (BF16 ? 2 : 4);
+                m.valid = left >= kUnitW ? kUnitW : (int)left;
+                m.staged = staged ? 1 : 0;
+                if (staged) {
+                    const uint32_t am_bytes = (uint32_t)(kUnitW >> L2) * 4u;
+                    mbar_expect_tx(&full[s], 2 * kPlaneBytes + am_bytes);
+                    bulk_g2s(ring + s * kSlotBytes, m.hole, kPlaneBytes, &full[s]);
+                    bulk_g2s(ring + s * kSlotBytes + kPlaneBytes, m.plug, kPlaneBytes, &full[s]);
+                    bulk_g2s(ring + s * kSlotBytes + 2 * kPlaneBytes, m.absmax, am_bytes, &full[s]);
                 } else {
                     mbar_arrive(&full[s]);
                 }
@@ -130,8 +178,7 @@ __global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __g
         return;
     }
 
-    const uint32_t cells_lane = saddr(cells_rep) + lane * 4u;
-    int it = 0;
+    const uint32_t lut_base = saddr(lut), lane4 = lane * 4u;
     int64_t i = 0;
     for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
         const int s = (int)(i % kSlots);
@@ -139,43 +186,40 @@ __global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __g
         const bool ok = lane == 0 ? mbar_wait_bounded(&full[s], ph, &g_expand_error) : true;
         if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
             break;
-        while (unit_end[it] <= u)
-            ++it;
-        const int64_t off = (u - (it ? unit_end[it - 1] : 0)) * kUnitW;
-        const int64_t n = b.n[it];
-        const bool staged = n - off >= kUnitW && !((b.direct >> it) & 1u);
-        uint32_t H[2], P[2];
-        float S[2];
-        int valid[2];
-        int64_t e0[2];
+        const UnitMeta m = meta[s];
+        const uint32_t slot = saddr(ring + s * kSlotBytes);
+        uint32_t H[kGroups], P[kGroups];
+        float S[kGroups];
+        int valid[kGroups], rel[kGroups];
 #pragma unroll
-        for (int grp = 0; grp < 2; ++grp) {
-            const int rel = warp * 512 + grp * 256 + (int)lane * 8;
-            e0[grp] = off + rel;
-            valid[grp] = n - e0[grp] >= 8 ? 8 : (n - e0[grp] > 0 ? (int)(n - e0[grp]) : 0);
-            H[grp] = P[grp] = 0;
-            S[grp] = 0.f;
-            if (staged) {
-                H[grp] = lds32(saddr(ring + s * kSlotBytes) + rel / 2);
-                P[grp] = lds32(saddr(ring + s * kSlotBytes + kPlaneBytes) + rel / 2);
+        for (int grp = 0; grp < kGroups; ++grp) {
+            rel[grp] = warp * (32 * 8 * kGroups) + grp * 256 + (int)lane * 8;
+            const int left = m.valid - rel[grp];
+            valid[grp] = left >= 8 ? 8 : (left > 0 ? left : 0);
+            if (m.staged) {
+                H[grp] = lds32(slot + rel[grp] / 2);
+                P[grp] = lds32(slot + kPlaneBytes + rel[grp] / 2);
+                S[grp] = __uint_as_float(lds32(slot + 2 * kPlaneBytes + (uint32_t)(rel[grp] >> L2) * 4u));
             } else {
+                H[grp] = P[grp] = 0;
+                S[grp] = 0.f;
                 for (int bb = 0; bb < (valid[grp] + 1) / 2; ++bb) {
-                    H[grp] |= (uint32_t)b.hole[it][(e0[grp] >> 1) + bb] << (8 * bb);
-                    P[grp] |= (uint32_t)b.plug[it][(e0[grp] >> 1) + bb] << (8 * bb);
+                    H[grp] |= (uint32_t)m.hole[rel[grp] / 2 + bb] << (8 * bb);
+                    P[grp] |= (uint32_t)m.plug[rel[grp] / 2 + bb] << (8 * bb);
                 }
+                if (valid[grp] > 0)
+                    S[grp] = __ldg(m.absmax + (rel[grp] >> L2));
             }
-            if (valid[grp] > 0)
-                S[grp] = __ldg(b.absmax[it] + (e0[grp] >> b.bs_log2));
         }
         __syncwarp();
         if (lane == 0)
-            mbar_arrive(&empty[s]); /* the planes are in registers now */
+            mbar_arrive(&empty[s]); /* the slot's data now lives in registers */
 #pragma unroll
-        for (int grp = 0; grp < 2; ++grp) {
+        for (int grp = 0; grp < kGroups; ++grp) {
             if (valid[grp] == 0)
                 continue;
             float v[8];
-            dequant8(cells_lane, H[grp], P[grp], S[grp], v);
+            dequant8(lut_base, lane4, H[grp], P[grp], S[grp], v);
             const bool nan_scale = isnan(S[grp]);
             if (BF16) {
                 uint32_t o[4];
@@ -191,7 +235,7 @@ __global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __g
                     for (int q = 0; q < 4; ++q)
                         o[q] = nb | (nb << 16);
                 }
-                uint16_t *dst = static_cast<uint16_t *>(b.out[it]) + e0[grp];
+                uint16_t *dst = static_cast<uint16_t *>(m.out) + rel[grp];
                 if (valid[grp] == 8) {
                     __stcs(reinterpret_cast<uint4 *>(dst), make_uint4(o[0], o[1], o[2], o[3]));
                 } else {
@@ -207,7 +251,7 @@ __global__ void __launch_bounds__(kExpThreads, 3) expand_stream_kernel(const __g
                     for (int j = 0; j < 8; ++j)
                         v[j] = qn;
                 }
-                float *dst = static_cast<float *>(b.out[it]) + e0[grp];
+                float *dst = static_cast<float *>(m.out) + rel[grp];
                 if (valid[grp] == 8) {
                     __stcs(reinterpret_cast<float4 *>(dst), make_float4(v[0], v[1], v[2], v[3]));
                     __stcs(reinterpret_cast<float4 *>(dst + 4), make_float4(v[4], v[5], v[6], v[7]));
@@ -246,7 +290,7 @@ int launch_fast(const ExpandBatch &b, cudaStream_t st)
     if (!ensure_smem((const void *)kern, kExpSmem))
         return kLaunch;
     const int64_t total = b.unit_end[b.count - 1];
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total, (int64_t)sm_count() * 3));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(total, (int64_t)sm_count()));
     kern<<<grid, kExpThreads, kExpSmem, st>>>(b);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
 }
@@ -284,9 +328,10 @@ int expand_launch(const ExpandJob *jobs, int count, int bs, OutKind out, cudaStr
             continue;
         if (!j.hole || !j.plug || !j.absmax || !j.out)
             return kBadArg;
-        /* fast path: a power-of-two blocksize >= 8 (8-weight groups inside one block,
-         * absmax index by shift) and a 16-byte aligned output */
-        const bool fast = l2 >= 3 && aligned_to(j.absmax, 4) && aligned_to(j.out, 16);
+        /* fast path: a power-of-two blocksize in [8, 1024] (8-weight groups inside one
+         * block, absmax index by shift, a unit's absmax a multiple of 16 bytes) and a
+         * 16-byte aligned output */
+        const bool fast = l2 >= 3 && l2 <= 10 && aligned_to(j.absmax, 4) && aligned_to(j.out, 16);
         if (!fast) {
             const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((j.n + 255) / 256, (int64_t)sm_count() * 8));
             if (bf16)
@@ -303,7 +348,7 @@ int expand_launch(const ExpandJob *jobs, int count, int bs, OutKind out, cudaStr
         b.out[k] = j.out;
         b.n[k] = j.n;
         b.unit_end[k] = (k ? b.unit_end[k - 1] : 0) + (j.n + kUnitW - 1) / kUnitW;
-        if (!aligned_to(j.hole, 16) || !aligned_to(j.plug, 16))
+        if (!aligned_to(j.hole, 16) || !aligned_to(j.plug, 16) || !aligned_to(j.absmax, 16))
             b.direct |= 1u << k;
         b.count = k + 1;
         if (b.count == kMaxItems)
