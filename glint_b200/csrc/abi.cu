@@ -510,4 +510,20 @@ int glint_htile_stream(const uint8_t *d_hole, const uint8_t *d_plug, const float
                         blocksize, mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
 }
 
+int glint_htile_stream_noalloc(const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
+                               const __nv_bfloat16 *d_x, void *d_y, int y_dtype, int M, int N, int K,
+                               int blocksize, int mode, cudaStream_t stream)
+{
+    if (!d_hole || !d_plug || !d_absmax || !d_x || !d_y)
+        return kBadArg;
+    if ((y_dtype != GLINT_Y_F32 && y_dtype != GLINT_Y_BF16) || (mode != GLINT_HTILE_PRECISE && mode != GLINT_HTILE_FAST))
+        return kBadArg;
+    if (blocksize <= 0)
+        return kBadBlocksize;
+    if (M <= 0 || N <= 0 || K <= 0 || !htile_decode_supported(d_hole, d_plug, d_absmax, d_x, M, N, K, blocksize))
+        return kBadArg;
+    return htile_decode_launch_noalloc(d_hole, d_plug, d_absmax, d_x, d_y, y_dtype == GLINT_Y_BF16 ? kOutBF16 : kOutF32,
+                                       M, N, K, mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
+}
+
 } /* extern "C" */

@@ -24,6 +24,7 @@ enum Status : int {
     kBadBlocksize = -2,
     kLaunch = -3,
     kCodebook = -4,
+    kScratch = -5, /* the fixed scratch area is too small for this call */
 };
 
 /* Encode lookup table: {threshold bits, base code} per grid cell, generated at

@@ -65,6 +65,10 @@ bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const floa
                             int M, int N, int K, int blocksize);
 int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
                         void *y, OutKind y_kind, int M, int N, int K, HtileMode mode, cudaStream_t stream);
+/* The same decode path on the library's fixed per-device scratch array (no allocation). */
+int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const float *absmax,
+                                const __nv_bfloat16 *x, void *y, OutKind y_kind, int M, int N, int K,
+                                HtileMode mode, cudaStream_t stream);
 
 /* SM count of the current device (cached per device). */
 int sm_count();

@@ -494,6 +494,84 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
     return bf ? launch_mt<false, true>(MT, maps, a, grid, st) : launch_mt<false, false>(MT, maps, a, grid, st);
 }
 
+/* ---- fixed-scratch variant ---------------------------------------------------
+ * Some callers cannot let a library allocate device memory: a serving process
+ * that hands all free HBM to its own cache pool up front, or an integration whose
+ * memory is budgeted before the first call and must not see cudaMalloc (which can
+ * fail under that budget and synchronises the device).  For them the decode path
+ * can run on a fixed scratch area compiled into this file instead of the
+ * per-stream workspace above: kNoAllocBytes per device, allocated with the
+ * library's device image when it is loaded on a device and held until the
+ * process exits.  The first kNoAllocCounterBytes hold the per (row block, warp)
+ * counters, the rest the split-K partial sums. */
+constexpr size_t kNoAllocBytes = size_t(4) << 20;   /* 4 MiB per device */
+constexpr size_t kNoAllocCounterBytes = 16 << 10;   /* 4096 counters: N <= 65536 */
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[64] = {};
+}
+
+int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
+                                void *y, OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
+{
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return kLaunch;
+    void *base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_addr[dev]) {
+            /* host code only sees a stand-in for the array: ask the runtime for its
+             * device address, once per device, with that device current */
+            void *p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+                cudaGetLastError();
+                return kLaunch;
+            }
+            g_noalloc_addr[dev] = p;
+        }
+        base = g_noalloc_addr[dev];
+    }
+    const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+    DecodeArgs a{};
+    a.x = x;
+    a.y = y;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.KU = K / kKU;
+    const int64_t rbs = (N + kRows - 1) / kRows;
+    a.units = rbs * a.KU;
+    const int grid = (int)std::min<int64_t>(a.units, sm_count());
+    const int64_t per_cta = std::max<int64_t>(1, a.units / grid);
+    a.max_parts = (int)std::min<int64_t>(grid, (a.KU + per_cta - 1) / per_cta + 1);
+    const size_t counter_bytes = (size_t)rbs * kConsumers * sizeof(int);
+    const size_t ws_bytes = (size_t)rbs * a.max_parts * kRows * 8 * MT * sizeof(float);
+    if (counter_bytes > kNoAllocCounterBytes || ws_bytes > kNoAllocBytes - kNoAllocCounterBytes)
+        return kScratch;
+    Maps maps;
+    if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
+                  4, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
+                  (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B))
+        return kLaunch;
+    /* the array keeps the previous call's contents: the counters must start at 0 */
+    a.counters = static_cast<int *>(base);
+    a.ws = reinterpret_cast<float *>(static_cast<unsigned char *>(base) + kNoAllocCounterBytes);
+    if (cudaMemsetAsync(a.counters, 0, counter_bytes, st) != cudaSuccess)
+        return kLaunch;
+    const bool bf = yk == kOutBF16;
+    if (mode == kPrecise)
+        return bf ? launch_mt<true, true>(MT, maps, a, grid, st) : launch_mt<true, false>(MT, maps, a, grid, st);
+    return bf ? launch_mt<false, true>(MT, maps, a, grid, st) : launch_mt<false, false>(MT, maps, a, grid, st);
+}
+
 /* This file's kernel error word (bounded waits that ran out); clear resets it. */
 int decode_error_word(bool clear)
 {

@@ -43,6 +43,24 @@ int glint_htile_stream(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
     const __nv_bfloat16 *d_x, void *d_y, int y_dtype,
     int M, int N, int K, int blocksize, int mode, cudaStream_t stream);
+
+/* Same contract as glint_htile_stream for decode shapes, for callers that cannot
+ * let a library allocate device memory (for example a serving process whose own
+ * allocator already owns all free HBM, or an integration whose memory budget is
+ * fixed before the first call).  No counterpart in the reference ABI.
+ * It allocates nothing: the split-K partial sums and counters live in one 4 MiB
+ * array compiled into the library, which every GPU that loads the library holds
+ * until the process exits.  The first call on a device looks the array's device
+ * address up; make that first call before any stream capture.  All calls share
+ * the array, so calls that overlap on the GPU (other streams, other threads) race
+ * and give wrong results; serialise them.  Limits: M <= 32, blocksize == 64,
+ * K % 256 == 0, 16-byte aligned pointers (-1 otherwise), N <= 65536 and the
+ * partial sums within the array (-5 GLINT_ERR_SCRATCH otherwise). */
+#define GLINT_ERR_SCRATCH (-5)
+int glint_htile_stream_noalloc(
+    const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
+    const __nv_bfloat16 *d_x, void *d_y, int y_dtype,
+    int M, int N, int K, int blocksize, int mode, cudaStream_t stream);
 #ifdef __cplusplus
 }
 #endif
