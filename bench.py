@@ -411,6 +411,12 @@ def profile_case(case: str, iters: int = 5):
     elif case == "expand":
         outs = [torch.empty_like(w) for w in ws]
         fn = lambda: D.expand_batch(planes, outs, BS)  # noqa: E731
+    elif case.startswith("gemm"):
+        M = int(case[4:] or 2048)
+        x = torch.randn((M, 4096), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, 14336), dtype=torch.float32, device="cuda")
+        n = 14336 * 4096
+        fn = lambda: D.htile(x, *planes[0], 14336, BS, mode="fast", out=y)  # noqa: E731
     elif case.startswith("gemv"):
         M = int(case[4:] or 1)
         x = torch.randn((M, 4096), generator=g, device="cuda").to(torch.bfloat16)
@@ -438,7 +444,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="glint_b200", choices=["glint_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", default=None, help="run one small kernel case (encode|expand|gemv<M>) for ncu")
+    ap.add_argument("--profile", default=None, help="run one small kernel case (encode|expand|gemv<M>|gemm<M>) for ncu")
     args = ap.parse_args()
     if args.profile:
         profile_case(args.profile)
