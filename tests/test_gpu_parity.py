@@ -421,7 +421,8 @@ def test_htile_matches_reference_library():
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 256, 4096), (300, 200, 128), (129, 264, 192),
-                                   (512, 512, 1024), (1024, 512, 4096), (256, 4096, 256)])
+                                   (512, 512, 1024), (1024, 512, 4096), (256, 4096, 256), (300, 200, 256),
+                                   (129, 264, 512), (640, 1000, 768), (2048, 384, 1024), (1100, 130, 2048)])
 def test_htile_prefill_tcgen05_vs_oracle(M, N, K):
     """Prefill shapes take the tcgen05 path in fast mode: within 1e-2 relative of the
     f32 dequant-then-matmul oracle, f32 and BF16 y, ragged M and N edges."""
