@@ -4,34 +4,40 @@
  *   y[m, n] = sum_k GLINT_CELLS[h][p] * absmax[(n*K + k) / bs] * x[m, k].
  * The reference runs scalar f32 FMAs, one output per thread.  Here the product
  * is computed transposed, y^T[n, m] = W[n, :] . x[m, :], so that the GLINT
- * weights are the UMMA's A operand and can live in tensor memory: dequantiser
- * warps write RN_bf16(cell * absmax) straight into TMEM with tcgen05.st, and
- * the weights never touch shared memory (no STS, no tensor-core smem reads of
- * W).  Only the activations stream through shared memory.
+ * weights are the UMMA's A operand and live in tensor memory: dequantiser warps
+ * write RN_bf16(cell * absmax) straight into TMEM with tcgen05.st, and the
+ * weights never pass through shared memory.  Only the activations do.
  *
- * Persistent CTAs (one per SM) walk tiles of 128 weight rows (n) x 256
- * activation rows (m); K steps of 64 (one absmax block) flow through a 4-stage
- * shared-memory ring and a 4-slot TMEM ring:
- *   warp 0      TMA producer: per K step the x tile [256 x 64] BF16 (128B
- *               swizzle) and the hole and plug tiles [128 rows x 32 B] (32B
- *               swizzle); every fourth step also an absmax box [128 rows x 4
- *               blocks].  Plain loads of this GPU's memory, no cluster multicast.
+ * CTA pairs (clusters of 2, tcgen05 cta_group::2) walk tiles of 256 weight rows
+ * (n) x 256 activation rows (m), persistently.  CTA r of a pair owns weight rows
+ * n0 + 128r .. +127 (its TMEM lanes: UMMA A rows and accumulator rows) and holds
+ * activation rows m0 + 128r .. +127 in its shared memory (its half of the UMMA
+ * B operand), so each SM streams half of the x tile and the plane rows of its
+ * own weights: 24.5 KB per K step for 128 x 256 x 64 multiply-adds.  K steps of
+ * 64 (one absmax block) flow through a 6-stage shared-memory ring and a 4-slot
+ * TMEM weight ring.  Roles per CTA:
+ *   warp 0      TMA producer: its x half [128 x 64] BF16 (128B swizzle; bytes
+ *               counted on the leader CTA's barrier), hole and plug tiles
+ *               [128 rows x 32 B] (32B swizzle) and, every fourth step, an absmax
+ *               box [128 rows x 4 blocks].  Plain loads of this GPU's memory; no
+ *               cluster multicast anywhere.
  *   warp 1      TMEM owner (512 columns: accumulator 0..255, weight ring
- *               256..383) and, in one lane, the UMMA issuer: per K step
- *               4 x (M=128, N=256, K=16) with A from TMEM, B = x from shared
- *               memory, then tcgen05.commit to release the stage and the slot;
- *   warps 2..9  dequantisers: warp w owns TMEM lanes 32*(w%4).. (weight rows)
- *               and half of the K step (32 weights per thread); codes are looked
- *               up in a per-lane replica of the codebook, scaled by the row's
- *               absmax in f32 and rounded to BF16 pairs;
+ *               256..383); in the leader CTA one lane issues the pair's UMMAs,
+ *               4 x (M=256, N=256, K=16) per K step, and commits them to both
+ *               CTAs' barriers;
+ *   warps 2-9   dequantisers: warp w owns TMEM lanes 32*(w%4).. (weight rows) and
+ *               32 weights of the K step; codes are looked up in a per-lane replica
+ *               of the codebook, scaled by the row's absmax in f32 (two weights per
+ *               f32x2 multiply) and rounded to BF16 pairs;
  *   warps 10-13 epilogue: tcgen05.ld of the accumulator (lane = weight row,
  *               column = activation row) to y.
  * Weights reach the MMA as RN_bf16(cell * absmax) (relative error <= 2^-9 per
  * weight), i.e. the GLINT_HTILE_FAST arithmetic.
  *
- * Every wait on an mbarrier is bounded (about one second of clock64 time); when
- * a wait runs out the kernel records an error in g_glint_kernel_error, stops,
- * waits (bounded) for its own TMA loads and UMMAs and releases TMEM.
+ * Every mbarrier wait is bounded (about one second of clock64 time) and suspends
+ * the warp between polls; when a wait runs out the kernel records an error in
+ * g_glint_kernel_error, stops, waits (bounded) for its own TMA loads and UMMAs,
+ * meets its peer CTA and releases TMEM.
  */
 #include <cudaTypedefs.h>
 
@@ -48,28 +54,80 @@ __device__ int g_glint_kernel_error = 0;
 
 namespace {
 
-constexpr int BN = 128;      /* weight rows per tile (UMMA M) */
-constexpr int BMX = 256;     /* activation rows per tile (UMMA N) */
-constexpr int BK = 64;       /* one absmax block */
-constexpr int STAGES = 4;    /* smem ring == TMEM weight ring depth */
-constexpr int kThreads = 14 * 32;
+constexpr int BN = 128;    /* weight rows per CTA (UMMA M = 2 x 128 per pair) */
+constexpr int BMX = 256;   /* activation rows per pair tile (UMMA N) */
+constexpr int BMH = 128;   /* activation rows held by one CTA */
+constexpr int BK = 64;     /* one absmax block */
+constexpr int STAGES = 6;  /* shared-memory ring */
+constexpr int WSLOTS = 4;  /* TMEM weight ring */
 constexpr int kDeqWarps = 8, kEpiWarps = 4;
-constexpr int kStageX = BMX * BK * 2;   /* 32 KB */
-constexpr int kPlaneBox = BN * BK / 2;  /* 4 KB: 128 rows x 32 B */
-constexpr int kAmBox = BN * 4 * 4;      /* 2 KB: 128 rows x 4 blocks */
-constexpr int kStageBytes = kStageX + 2 * kPlaneBox + kAmBox; /* 42 KB, a multiple of 1 KB */
-constexpr int kLutBytes = 256 * 32 * 4; /* f32 codebook, one replica per lane */
-constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kLutBytes + 256;
+constexpr int kDeq0 = 2, kEpi0 = kDeq0 + kDeqWarps; /* first warp of each role */
+constexpr int kThreads = (kEpi0 + kEpiWarps) * 32;
+constexpr int kWpt = BK * 4 / kDeqWarps;            /* 32 weights per dequantiser thread and K step */
+constexpr int kStageX = BMH * BK * 2;               /* 16 KB */
+constexpr int kPlaneBox = BN * BK / 2;              /* 4 KB: 128 rows x 32 B */
+constexpr int kAmBox = BN * 4 * 4;                  /* 2 KB: 128 rows x 4 blocks */
+constexpr int kStageBytes = kStageX + 2 * kPlaneBox + kAmBox; /* 26 KB, a multiple of 1 KB */
+/* f32 codebook, one replica per lane, 256-byte entry stride so that one byte
+ * permute forms (code << 8) | (lane << 2); the upper 128 bytes of each entry
+ * are not used */
+constexpr int kLutBytes = 256 * 256;
+constexpr int kSmemBytes = kLutBytes + 1024 + STAGES * kStageBytes + 512;
 constexpr uint32_t kAccCol = 0, kWCol = 256; /* TMEM column bases */
 constexpr uint32_t kTmemCols = 512;
 
+/* ---- cluster / pair primitives ------------------------------------------------ */
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+/* shared::cluster address of the same shared-memory offset in CTA `rank` */
+__device__ __forceinline__ uint32_t peer_addr(uint32_t a, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+/* arrive on an mbarrier given by its shared::cluster address (this CTA's or the
+ * peer's); default (CTA-scope) release: the data it publishes is tensor memory
+ * already completed by tcgen05.wait::st and fenced by tcgen05.fence */
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_test_suspend(uint64_t *bar, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}\n"
+                 : "=r"(ok)
+                 : "r"(saddr(bar)), "r"(parity), "r"(ns)
+                 : "memory");
+    return ok != 0;
+}
+/* bounded wait; arrivals may come from the peer CTA */
 __device__ __forceinline__ bool wait_or_fail(uint64_t *bar, uint32_t parity, bool &alive)
 {
     if (!alive)
         return false;
-    if (!mbar_wait_bounded(bar, parity, &g_glint_kernel_error))
-        alive = false;
-    return alive;
+    if (mbar_test_suspend(bar, parity, 0u))
+        return true;
+    const long long t0 = clock64();
+    while (!mbar_test_suspend(bar, parity, 20000u)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicOr(&g_glint_kernel_error, kErrTimeout);
+            alive = false;
+            return false;
+        }
+    }
+    return true;
 }
 /* lane 0 waits, the warp follows its verdict (keeps the warp converged) */
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, bool &alive)
@@ -79,20 +137,30 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, bool &
     alive = ok;
     return ok;
 }
+/* 2-D TMA load into this CTA's shared memory whose bytes are counted on the
+ * mbarrier at `bar_cluster` (the leader CTA's); no multicast */
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar_cluster, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4}], [%2];" ::"r"(saddr(dst)),
+                 "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
+                 : "memory");
+}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-/* D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (A and B both BF16) */
-__device__ __forceinline__ void umma_ts_bf16(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+/* D[tmem] (+)= A[tmem] * B[smem]^T over the CTA pair, kind::f16 (A and B both BF16) */
+__device__ __forceinline__ void umma_pair_ts_bf16(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc)
 {
     asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+                 "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
                  "r"(a), "l"(b), "r"(idesc), "r"(acc));
 }
-__device__ __forceinline__ void umma_commit(uint64_t *bar)
+/* arrive on the mbarrier at `cluster_addr` once this thread's UMMAs are done */
+__device__ __forceinline__ void umma_commit_to(uint32_t cluster_addr)
 {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
@@ -115,6 +183,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
                  "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
                  : "memory");
 }
+/* ring position: stage index and the parity of its current use */
+struct Ring {
+    int i = 0;
+    uint32_t ph = 0;
+    template <int N> __device__ __forceinline__ void next()
+    {
+        if (++i == N)
+            i = 0, ph ^= 1u;
+    }
+};
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -125,9 +203,16 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t sa)
     return (uint64_t)((sa >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-/* instruction descriptor: f32 accumulate, BF16 A and B, both K-major, M=128, N=256 */
+/* instruction descriptor: f32 accumulate, BF16 A and B, both K-major, M=256 (pair), N=256 */
 constexpr uint32_t kIdesc =
-    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BMX >> 3) << 17) | ((uint32_t)(BN >> 4) << 24);
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BMX >> 3) << 17) | ((uint32_t)((2 * BN) >> 4) << 24);
+
+__device__ __forceinline__ uint64_t pack2f(float lo, float hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
 
 /* (E, O) = codes of the even and odd weights of four plane bytes: code = h*16 + p */
 __device__ __forceinline__ void codes4(uint32_t h, uint32_t p, uint32_t &E, uint32_t &O)
@@ -147,174 +232,203 @@ struct Maps {
     CUtensorMap x, h, p, am;
 };
 
-__global__ void __launch_bounds__(kThreads, 1) htile_gemm_kernel(const __grid_constant__ Maps maps, const GemmArgs args)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    htile_gemm_kernel(const __grid_constant__ Maps maps, const GemmArgs args)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *lut = reinterpret_cast<float *>(smem + STAGES * kStageBytes);
-    uint64_t *load_full = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(lut) + kLutBytes);
-    uint64_t *load_empty = load_full + STAGES;
-    uint64_t *w_full = load_empty + STAGES;
-    uint64_t *w_empty = w_full + STAGES;
-    uint64_t *acc_full = w_empty + STAGES;
-    uint64_t *acc_empty = acc_full + 1;
+    float *lut = reinterpret_cast<float *>(smem_raw); /* at the start: its address folds into the loads */
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) &
+                                                ~uintptr_t(1023));
+    uint64_t *x_full = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
+    uint64_t *p_full = x_full + STAGES;  /* this CTA's planes landed */
+    uint64_t *empty = p_full + STAGES;   /* stage free: pair UMMAs + this CTA's dequantisers */
+    uint64_t *w_full = empty + STAGES;   /* leader: both CTAs' weight slots written */
+    uint64_t *w_empty = w_full + WSLOTS; /* weight slot read by the pair UMMAs */
+    uint64_t *acc_full = w_empty + WSLOTS;
+    uint64_t *acc_empty = acc_full + 1;  /* leader: both CTAs' epilogues drained */
     uint64_t *mma_done = acc_empty + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
 
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = lane_id();
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
     const int ksteps = args.K / BK;
     const int ntiles_total = args.mtiles * args.ntiles;
 
     for (int i = threadIdx.x; i < 256 * 32; i += kThreads)
-        lut[i] = (&g_cells[0][0])[i >> 5];
+        lut[(i >> 5) * 64 + (i & 31)] = (&g_cells[0][0])[i >> 5];
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&load_full[s], 1);
-            mbar_init(&load_empty[s], 1 + kDeqWarps); /* UMMA commit + dequantiser warps */
-            mbar_init(&w_full[s], kDeqWarps);
-            mbar_init(&w_empty[s], 1);
+            mbar_init(&x_full[s], 1);
+            mbar_init(&p_full[s], 1);
+            mbar_init(&empty[s], 1 + kDeqWarps);
+        }
+        for (int a = 0; a < WSLOTS; ++a) {
+            mbar_init(&w_full[a], 2 * kDeqWarps);
+            mbar_init(&w_empty[a], 1);
         }
         mbar_init(acc_full, 1);
-        mbar_init(acc_empty, kEpiWarps);
+        mbar_init(acc_empty, 2 * kEpiWarps);
         mbar_init(mma_done, 1);
         mbar_init_fence();
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
                      "r"(kTmemCols)
                      : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync(); /* both CTAs' barriers initialised and TMEM allocated */
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     bool alive = true;
 
     if (warp == 0) {
-        /* ---- TMA producer */
+        /* ---- TMA producer (both CTAs) */
         if (lane == 0) {
-            int64_t g = 0;
-            for (int tile = blockIdx.x; tile < ntiles_total && alive; tile += gridDim.x) {
-                const int m0 = (tile % args.mtiles) * BMX, n0 = (tile / args.mtiles) * BN;
-                for (int ks = 0; ks < ksteps && alive; ++ks, ++g) {
-                    const int s = (int)(g % STAGES);
-                    const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
-                    if (g >= STAGES && !wait_or_fail(&load_empty[s], ph ^ 1u, alive))
+            Ring st;
+            int64_t issued = 0;
+            for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
+                const int m0 = (tile % args.mtiles) * BMX, n0 = (tile / args.mtiles) * (2 * BN);
+                const int mr = m0 + (int)rank * BMH, nr = n0 + (int)rank * BN;
+                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<STAGES>()) {
+                    /* the first use of a stage waits on parity 1: returns at once */
+                    if (!wait_or_fail(&empty[st.i], st.ph ^ 1u, alive))
                         break;
-                    uint8_t *st = smem + s * kStageBytes;
+                    uint8_t *sb = smem + st.i * kStageBytes;
+                    if (leader)
+                        mbar_expect_tx(&x_full[st.i], 2 * kStageX);
+                    tma_load_2d_pair(sb, &maps.x, peer_addr(saddr(&x_full[st.i]), 0), ks * BK, mr);
                     const bool am = (ks & 3) == 0;
-                    mbar_expect_tx(&load_full[s], kStageX + 2 * kPlaneBox + (am ? kAmBox : 0));
-                    tma_load_2d(st, &maps.x, &load_full[s], ks * BK, m0);
-                    tma_load_2d(st + kStageX, &maps.h, &load_full[s], ks * (BK / 2), n0);
-                    tma_load_2d(st + kStageX + kPlaneBox, &maps.p, &load_full[s], ks * (BK / 2), n0);
+                    mbar_expect_tx(&p_full[st.i], 2 * kPlaneBox + (am ? kAmBox : 0));
+                    tma_load_2d(sb + kStageX, &maps.h, &p_full[st.i], ks * (BK / 2), nr);
+                    tma_load_2d(sb + kStageX + kPlaneBox, &maps.p, &p_full[st.i], ks * (BK / 2), nr);
                     if (am)
-                        tma_load_2d(st + kStageX + 2 * kPlaneBox, &maps.am, &load_full[s], ks, n0);
+                        tma_load_2d(sb + kStageX + 2 * kPlaneBox, &maps.am, &p_full[st.i], ks, nr);
+                    ++issued;
                 }
             }
             if (!alive) {
                 /* let the loads already issued land before the CTA exits */
                 bool drain = true;
-                for (int64_t j = g > STAGES ? g - STAGES : 0; j < g && drain; ++j)
-                    drain = mbar_wait_bounded(&load_full[(int)(j % STAGES)], (uint32_t)(j / STAGES) & 1u,
-                                              &g_glint_kernel_error);
+                for (int64_t j = issued > STAGES ? issued - STAGES : 0; j < issued && drain; ++j) {
+                    const int s = (int)(j % STAGES);
+                    const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
+                    drain = mbar_wait_bounded(&p_full[s], ph, &g_glint_kernel_error) &&
+                            (!leader || mbar_wait_bounded(&x_full[s], ph, &g_glint_kernel_error));
+                }
             }
         }
     } else if (warp == 1) {
-        /* ---- UMMA issuer */
-        if (lane == 0) {
-            int64_t g = 0;
+        /* ---- UMMA issuer (leader CTA only) */
+        if (leader && lane == 0) {
+            Ring st, ws;
             int t = 0;
-            for (int tile = blockIdx.x; tile < ntiles_total && alive; tile += gridDim.x, ++t) {
+            const uint32_t empty0 = peer_addr(saddr(&empty[0]), 0), empty1 = peer_addr(saddr(&empty[0]), 1);
+            const uint32_t wempty0 = peer_addr(saddr(&w_empty[0]), 0), wempty1 = peer_addr(saddr(&w_empty[0]), 1);
+            for (int tile = pair; tile < ntiles_total && alive; tile += npairs, ++t) {
                 if (t >= 1 && !wait_or_fail(acc_empty, (uint32_t)(t - 1) & 1u, alive))
                     break;
                 tc_fence_after();
-                for (int ks = 0; ks < ksteps && alive; ++ks, ++g) {
-                    const int s = (int)(g % STAGES);
-                    const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
-                    if (!wait_or_fail(&load_full[s], ph, alive) || !wait_or_fail(&w_full[s], ph, alive))
+                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<STAGES>(), ws.next<WSLOTS>()) {
+                    if (!wait_or_fail(&x_full[st.i], st.ph, alive) || !wait_or_fail(&w_full[ws.i], ws.ph, alive))
                         break;
                     tc_fence_after();
-                    const uint32_t xs = saddr(smem + s * kStageBytes);
-                    const uint32_t wa = tmem + kWCol + (uint32_t)s * (BK / 2);
+                    const uint32_t xs = saddr(smem + st.i * kStageBytes);
+                    const uint32_t wa = tmem + kWCol + (uint32_t)ws.i * (BK / 2);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
-                        umma_ts_bf16(tmem + kAccCol, wa + kk * 8, sw128_desc(xs + kk * 32), kIdesc,
-                                     (ks > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(&load_empty[s]); /* x tile consumed */
-                    umma_commit(&w_empty[s]);    /* weight slot consumed */
+                        umma_pair_ts_bf16(tmem + kAccCol, wa + kk * 8, sw128_desc(xs + kk * 32), kIdesc,
+                                          (ks > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit_to(empty0 + (uint32_t)st.i * 8u);
+                    umma_commit_to(empty1 + (uint32_t)st.i * 8u);
+                    umma_commit_to(wempty0 + (uint32_t)ws.i * 8u);
+                    umma_commit_to(wempty1 + (uint32_t)ws.i * 8u);
                 }
-                if (alive)
-                    umma_commit(acc_full);
+                if (alive) {
+                    umma_commit_to(peer_addr(saddr(acc_full), 0));
+                    umma_commit_to(peer_addr(saddr(acc_full), 1));
+                }
             }
             /* all UMMAs issued by this thread have completed before TMEM is released */
-            umma_commit(mma_done);
+            umma_commit_to(peer_addr(saddr(mma_done), 0));
             mbar_wait_bounded(mma_done, 0, &g_glint_kernel_error);
         }
         __syncwarp();
-    } else if (warp < 2 + kDeqWarps) {
-        /* ---- dequantisers: thread -> weight row r (TMEM lane), 32 weights (K half kh) */
-        const int q = warp & 3, kh = (warp - 2) >> 2;
+    } else if (warp < kEpi0) {
+        /* ---- dequantisers: thread -> weight row r (TMEM lane), 32 weights (K half kq) */
+        const int q = warp & 3, kq = (warp - kDeq0) >> 2;
         const int r = q * 32 + (int)lane;
-        const uint32_t cl = saddr(lut) + lane * 4u;
-        const uint32_t pofs = (uint32_t)r * 32u + ((uint32_t)(kh ^ ((r >> 2) & 1)) << 4); /* 32B swizzle */
-        const uint32_t tw = tmem + ((uint32_t)(q * 32) << 16) + kWCol + (uint32_t)kh * 16u;
+        const uint32_t lutb = saddr(lut), lane4 = lane * 4u;
+        /* byte offset of this thread's 16 plane bytes in the row; 32B swizzle of the
+         * plane rows: 16-byte chunk index ^= bit 2 of the row */
+        const uint32_t pofs = (uint32_t)r * 32u + ((uint32_t)(kq ^ ((r >> 2) & 1)) << 4);
+        const uint32_t tw = tmem + ((uint32_t)(q * 32) << 16) + kWCol + (uint32_t)kq * (kWpt / 2);
+        const uint32_t wfull0 = peer_addr(saddr(&w_full[0]), 0);
         float4 sc4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        int64_t g = 0;
-        for (int tile = blockIdx.x; tile < ntiles_total && alive; tile += gridDim.x) {
-            for (int ks = 0; ks < ksteps && alive; ++ks, ++g) {
-                const int s = (int)(g % STAGES);
-                const uint32_t ph = (uint32_t)(g / STAGES) & 1u;
-                if (!warp_wait(&load_full[s], ph, alive))
+        Ring st, ws;
+        for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
+            for (int ks = 0; ks < ksteps && alive; ++ks, st.next<STAGES>(), ws.next<WSLOTS>()) {
+                if (!warp_wait(&p_full[st.i], st.ph, alive))
                     break;
-                const uint32_t ps = saddr(smem + s * kStageBytes + kStageX);
+                const uint32_t ps = saddr(smem + st.i * kStageBytes + kStageX);
                 const uint4 H = lds128(ps + pofs);
                 const uint4 P = lds128(ps + kPlaneBox + pofs);
                 if ((ks & 3) == 0) {
-                    const uint4 a = lds128(ps + 2 * kPlaneBox + (uint32_t)r * 16u);
-                    sc4 = make_float4(__uint_as_float(a.x), __uint_as_float(a.y), __uint_as_float(a.z),
-                                      __uint_as_float(a.w));
+                    const uint4 a4 = lds128(ps + 2 * kPlaneBox + (uint32_t)r * 16u);
+                    sc4 = make_float4(__uint_as_float(a4.x), __uint_as_float(a4.y), __uint_as_float(a4.z),
+                                      __uint_as_float(a4.w));
                 }
                 const float sc = (ks & 3) == 0 ? sc4.x : (ks & 3) == 1 ? sc4.y : (ks & 3) == 2 ? sc4.z : sc4.w;
                 __syncwarp();
                 if (lane == 0)
-                    mbar_arrive(&load_empty[s]);
-                if (g >= STAGES && !warp_wait(&w_empty[s], ph ^ 1u, alive))
+                    mbar_arrive(&empty[st.i]);
+                /* the first use of a slot waits on parity 1: returns at once */
+                if (!warp_wait(&w_empty[ws.i], ws.ph ^ 1u, alive))
                     break;
                 tc_fence_after();
                 const uint32_t hw[4] = {H.x, H.y, H.z, H.w}, pw[4] = {P.x, P.y, P.z, P.w};
-                uint32_t o[16];
+                const uint64_t sc2 = pack2f(sc, sc);
+                uint32_t o[kWpt / 2];
 #pragma unroll
-                for (int wq = 0; wq < 4; ++wq) {
+                for (int wq = 0; wq < kWpt / 8; ++wq) {
                     uint32_t E, O;
                     codes4(hw[wq], pw[wq], E, O);
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
-                        const float v0 = __uint_as_float(lds32(cl + (((E >> (8 * b)) & 0xFFu) << 7))) * sc;
-                        const float v1 = __uint_as_float(lds32(cl + (((O >> (8 * b)) & 0xFFu) << 7))) * sc;
+                        /* (code << 8) | (lane << 2): entry `code`, this lane's replica */
+                        const float c0 = __uint_as_float(lds32(lutb + __byte_perm(E, lane4, 0x5504u | (b << 4))));
+                        const float c1 = __uint_as_float(lds32(lutb + __byte_perm(O, lane4, 0x5504u | (b << 4))));
+                        uint64_t d;
+                        float v0, v1;
+                        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack2f(c0, c1)), "l"(sc2));
+                        asm("mov.b64 {%0, %1}, %2;" : "=f"(v0), "=f"(v1) : "l"(d));
                         __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
                         o[wq * 4 + b] = *reinterpret_cast<uint32_t *>(&h2);
                     }
                 }
-                tmem_st16(tw + (uint32_t)s * (BK / 2), o);
+                tmem_st16(tw + (uint32_t)ws.i * (BK / 2), o);
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
-                    mbar_arrive(&w_full[s]);
+                    mbar_arrive_remote(wfull0 + (uint32_t)ws.i * 8u);
             }
         }
     } else {
         /* ---- epilogue: warp w reads TMEM lanes 32*(w%4): weight rows n, columns m */
         const int q = warp & 3;
+        const uint32_t accempty0 = peer_addr(saddr(acc_empty), 0);
         int t = 0;
-        for (int tile = blockIdx.x; tile < ntiles_total && alive; tile += gridDim.x, ++t) {
+        for (int tile = pair; tile < ntiles_total && alive; tile += npairs, ++t) {
             if (!warp_wait(acc_full, (uint32_t)t & 1u, alive))
                 break;
             tc_fence_after();
-            const int m0 = (tile % args.mtiles) * BMX, n0 = (tile / args.mtiles) * BN;
-            const int n = n0 + q * 32 + (int)lane;
+            const int m0 = (tile % args.mtiles) * BMX, n0 = (tile / args.mtiles) * (2 * BN);
+            const int n = n0 + (int)rank * BN + q * 32 + (int)lane;
             const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + kAccCol;
             const int mlim = min(BMX, args.M - m0);
 #pragma unroll 1
@@ -343,14 +457,15 @@ __global__ void __launch_bounds__(kThreads, 1) htile_gemm_kernel(const __grid_co
             tc_fence_before();
             __syncwarp();
             if (lane == 0)
-                mbar_arrive(acc_empty);
+                mbar_arrive_remote(accempty0);
         }
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync(); /* the peer no longer reads this CTA's TMEM or shared memory */
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
 }
 
@@ -396,6 +511,32 @@ bool encode_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64
     return enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+/* CTA pairs that fit on the device at once (one pair per two SMs at most) */
+int max_pairs()
+{
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return std::max(1, sm_count() / 2);
+    if (cached[dev] > 0)
+        return cached[dev];
+    int n = 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * std::max(1, sm_count() / 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void *)htile_gemm_kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = std::max(1, sm_count() / 2);
+    }
+    cached[dev] = n;
+    return n;
+}
 } // namespace
 
 int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
@@ -403,7 +544,7 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
 {
     (void)bs;
     Maps maps;
-    if (!encode_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BMX,
+    if (!encode_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BMH,
                     CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
                     BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_32B) ||
@@ -414,10 +555,10 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
         return kLaunch;
     if (!ensure_smem((const void *)htile_gemm_kernel, kSmemBytes))
         return kLaunch;
-    GemmArgs a{y, M, N, K, y_bf16 ? 1 : 0, (M + BMX - 1) / BMX, (N + BN - 1) / BN};
+    GemmArgs a{y, M, N, K, y_bf16 ? 1 : 0, (M + BMX - 1) / BMX, (N + 2 * BN - 1) / (2 * BN)};
     const int tiles = a.mtiles * a.ntiles;
-    const int grid = std::max(1, std::min(tiles, sm_count()));
-    htile_gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(maps, a);
+    const int pairs = std::max(1, std::min(tiles, max_pairs()));
+    htile_gemm_kernel<<<2 * pairs, kThreads, kSmemBytes, st>>>(maps, a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
 }
 

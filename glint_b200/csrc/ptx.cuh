@@ -59,6 +59,35 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     return true;
 }
 
+/* try_wait that lets the hardware suspend the warp until the phase completes or
+ * about `ns` nanoseconds pass, so waiting warps do not take issue slots from the
+ * warps that work. */
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}\n"
+                 : "=r"(ok)
+                 : "r"(saddr(bar)), "r"(parity), "r"(ns)
+                 : "memory");
+    return ok != 0;
+}
+/* Bounded wait as mbar_wait_bounded, suspending between polls. */
+__device__ __forceinline__ bool mbar_wait_suspend_bounded(uint64_t *bar, uint32_t parity, int *err_word)
+{
+    if (mbar_try_wait(bar, parity))
+        return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait_suspend(bar, parity, 20000u)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicOr(err_word, kErrTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
 /* 1-D bulk copy global -> this CTA's shared memory, completion on `bar`.
  * dst and src 16-byte aligned, bytes a multiple of 16. */
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
