@@ -14,15 +14,18 @@
  * activation rows m0 + 128r .. +127 in its shared memory (its half of the UMMA
  * B operand), so each SM streams half of the x tile and the plane rows of its
  * own weights: 24.5 KB per K step for 128 x 256 x 64 multiply-adds.  K steps of
- * 64 (one absmax block) flow through a 6-stage shared-memory ring and a 4-slot
- * TMEM weight ring.  Roles per CTA:
- *   warp 0      TMA producer: its x half [128 x 64] BF16 (128B swizzle; bytes
- *               counted on the leader CTA's barrier), hole and plug tiles
- *               [128 rows x 32 B] (32B swizzle) and, every fourth step, an absmax
- *               box [128 rows x 4 blocks].  Plain loads of this GPU's memory; no
- *               cluster multicast anywhere.
+ * 64 (one absmax block) flow through two shared-memory rings, activations
+ * (freed by the UMMAs) and planes (4 K steps per stage with 128-byte rows, so a
+ * TMA row request carries 128 bytes; freed by the dequantisers, so plane loads
+ * run ahead of the tensor cores), and an 8-slot TMEM weight ring.  Roles per CTA:
+ *   warp 0      activation producer: its x half [128 x 64] BF16 (128B swizzle;
+ *               bytes counted on the leader CTA's barrier);
+ *   warp 14     plane producer: per 4 K steps the hole and plug tiles [128 rows
+ *               x 128 B] (128B swizzle) and an absmax box [128 rows x 4 blocks].
+ *               All plain TMA loads of this GPU's memory; no cluster multicast
+ *               anywhere.
  *   warp 1      TMEM owner (512 columns: accumulator 0..255, weight ring
- *               256..383); in the leader CTA one lane issues the pair's UMMAs,
+ *               256..511); in the leader CTA one lane issues the pair's UMMAs,
  *               4 x (M=256, N=256, K=16) per K step, and commits them to both
  *               CTAs' barriers;
  *   warps 2-9   dequantisers: warp w owns TMEM lanes 32*(w%4).. (weight rows) and
@@ -58,22 +61,33 @@ constexpr int BN = 128;    /* weight rows per CTA (UMMA M = 2 x 128 per pair) */
 constexpr int BMX = 256;   /* activation rows per pair tile (UMMA N) */
 constexpr int BMH = 128;   /* activation rows held by one CTA */
 constexpr int BK = 64;     /* one absmax block */
-constexpr int STAGES = 6;  /* shared-memory ring */
-constexpr int WSLOTS = 4;  /* TMEM weight ring */
-constexpr int kDeqWarps = 8, kEpiWarps = 4;
+constexpr int XSTAGES = 5; /* shared-memory ring of activation tiles (freed by the UMMAs) */
+constexpr int PSTAGES = 2; /* shared-memory ring of plane tiles, 4 K steps each (freed by the dequantisers) */
+constexpr int PSTEPS = 4;  /* K steps per plane stage: 128-byte plane rows, one absmax box */
+constexpr int WSLOTS = 8;  /* TMEM weight ring */
+#ifndef GLINT_GEMM_DEQ_WARPS
+#define GLINT_GEMM_DEQ_WARPS 8
+#endif
+constexpr int kDeqWarps = GLINT_GEMM_DEQ_WARPS, kEpiWarps = 4;
+static_assert(kDeqWarps == 8 || kDeqWarps == 16, "2 or 4 dequantiser warps per TMEM lane quadrant");
+#ifndef GLINT_GEMM_DEFER_ST
+#define GLINT_GEMM_DEFER_ST 0
+#endif
 constexpr int kDeq0 = 2, kEpi0 = kDeq0 + kDeqWarps; /* first warp of each role */
-constexpr int kThreads = (kEpi0 + kEpiWarps) * 32;
-constexpr int kWpt = BK * 4 / kDeqWarps;            /* 32 weights per dequantiser thread and K step */
+constexpr int kPlaneWarp = kEpi0 + kEpiWarps;       /* plane producer */
+constexpr int kThreads = (kPlaneWarp + 1) * 32;
+constexpr int kWpt = BK * 4 / kDeqWarps;            /* weights per dequantiser thread and K step */
 constexpr int kStageX = BMH * BK * 2;               /* 16 KB */
-constexpr int kPlaneBox = BN * BK / 2;              /* 4 KB: 128 rows x 32 B */
-constexpr int kAmBox = BN * 4 * 4;                  /* 2 KB: 128 rows x 4 blocks */
-constexpr int kStageBytes = kStageX + 2 * kPlaneBox + kAmBox; /* 26 KB, a multiple of 1 KB */
+constexpr int kPlaneBox = BN * PSTEPS * BK / 2;     /* 16 KB: 128 rows x 128 B */
+constexpr int kAmBox = BN * PSTEPS * 4;             /* 2 KB: 128 rows x 4 blocks */
+constexpr int kPStage = 2 * kPlaneBox + kAmBox;     /* 34 KB, a multiple of 1 KB */
 /* f32 codebook, one replica per lane, 256-byte entry stride so that one byte
  * permute forms (code << 8) | (lane << 2); the upper 128 bytes of each entry
  * are not used */
 constexpr int kLutBytes = 256 * 256;
-constexpr int kSmemBytes = kLutBytes + 1024 + STAGES * kStageBytes + 512;
-constexpr uint32_t kAccCol = 0, kWCol = 256; /* TMEM column bases */
+constexpr int kSmemBytes = kLutBytes + 1024 + XSTAGES * kStageX + PSTAGES * kPStage + 512;
+constexpr uint32_t kAccCol = 0, kWCol = 256; /* TMEM column bases: accumulator, weight ring */
+static_assert(kWCol + WSLOTS * (BK / 2) <= 512, "TMEM columns");
 constexpr uint32_t kTmemCols = 512;
 
 /* ---- cluster / pair primitives ------------------------------------------------ */
@@ -175,7 +189,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
                    "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16])
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[8])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+/* kWpt/8 words of a plane row: 8 bytes (LDS.64) or 16 bytes (LDS.128) */
+__device__ __forceinline__ void lds_plane(uint32_t a, uint32_t (&w)[2])
+{
+    const uint2 v = lds64(a);
+    w[0] = v.x, w[1] = v.y;
+}
+__device__ __forceinline__ void lds_plane(uint32_t a, uint32_t (&w)[4])
+{
+    const uint4 v = lds128(a);
+    w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+}
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[16])
 {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
                  "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
@@ -239,10 +270,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     float *lut = reinterpret_cast<float *>(smem_raw); /* at the start: its address folds into the loads */
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) &
                                                 ~uintptr_t(1023));
-    uint64_t *x_full = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
-    uint64_t *p_full = x_full + STAGES;  /* this CTA's planes landed */
-    uint64_t *empty = p_full + STAGES;   /* stage free: pair UMMAs + this CTA's dequantisers */
-    uint64_t *w_full = empty + STAGES;   /* leader: both CTAs' weight slots written */
+    uint8_t *xring = smem, *pring = smem + XSTAGES * kStageX;
+    uint64_t *x_full = reinterpret_cast<uint64_t *>(pring + PSTAGES * kPStage); /* leader: both x halves */
+    uint64_t *x_empty = x_full + XSTAGES; /* x tile read by the pair UMMAs */
+    uint64_t *p_full = x_empty + XSTAGES; /* this CTA's planes landed */
+    uint64_t *p_empty = p_full + PSTAGES; /* planes read by this CTA's dequantisers */
+    uint64_t *w_full = p_empty + PSTAGES; /* leader: both CTAs' weight slots written */
     uint64_t *w_empty = w_full + WSLOTS; /* weight slot read by the pair UMMAs */
     uint64_t *acc_full = w_empty + WSLOTS;
     uint64_t *acc_empty = acc_full + 1;  /* leader: both CTAs' epilogues drained */
@@ -260,10 +293,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int i = threadIdx.x; i < 256 * 32; i += kThreads)
         lut[(i >> 5) * 64 + (i & 31)] = (&g_cells[0][0])[i >> 5];
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < XSTAGES; ++s) {
             mbar_init(&x_full[s], 1);
+            mbar_init(&x_empty[s], 1);
+        }
+        for (int s = 0; s < PSTAGES; ++s) {
             mbar_init(&p_full[s], 1);
-            mbar_init(&empty[s], 1 + kDeqWarps);
+            mbar_init(&p_empty[s], kDeqWarps);
         }
         for (int a = 0; a < WSLOTS; ++a) {
             mbar_init(&w_full[a], 2 * kDeqWarps);
@@ -287,39 +323,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool alive = true;
 
     if (warp == 0) {
-        /* ---- TMA producer (both CTAs) */
+        /* ---- activation producer (both CTAs): this CTA's half of the x tile */
         if (lane == 0) {
             Ring st;
             int64_t issued = 0;
             for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
-                const int m0 = (tile % args.mtiles) * BMX, n0 = (tile / args.mtiles) * (2 * BN);
-                const int mr = m0 + (int)rank * BMH, nr = n0 + (int)rank * BN;
-                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<STAGES>()) {
+                const int mr = (tile % args.mtiles) * BMX + (int)rank * BMH;
+                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<XSTAGES>()) {
                     /* the first use of a stage waits on parity 1: returns at once */
-                    if (!wait_or_fail(&empty[st.i], st.ph ^ 1u, alive))
+                    if (!wait_or_fail(&x_empty[st.i], st.ph ^ 1u, alive))
                         break;
-                    uint8_t *sb = smem + st.i * kStageBytes;
                     if (leader)
                         mbar_expect_tx(&x_full[st.i], 2 * kStageX);
-                    tma_load_2d_pair(sb, &maps.x, peer_addr(saddr(&x_full[st.i]), 0), ks * BK, mr);
-                    const bool am = (ks & 3) == 0;
-                    mbar_expect_tx(&p_full[st.i], 2 * kPlaneBox + (am ? kAmBox : 0));
-                    tma_load_2d(sb + kStageX, &maps.h, &p_full[st.i], ks * (BK / 2), nr);
-                    tma_load_2d(sb + kStageX + kPlaneBox, &maps.p, &p_full[st.i], ks * (BK / 2), nr);
-                    if (am)
-                        tma_load_2d(sb + kStageX + 2 * kPlaneBox, &maps.am, &p_full[st.i], ks, nr);
+                    tma_load_2d_pair(xring + st.i * kStageX, &maps.x, peer_addr(saddr(&x_full[st.i]), 0), ks * BK, mr);
+                    ++issued;
+                }
+            }
+            if (!alive && leader) {
+                /* let the loads already issued land before the CTA exits */
+                bool drain = true;
+                for (int64_t j = issued > XSTAGES ? issued - XSTAGES : 0; j < issued && drain; ++j)
+                    drain = mbar_wait_bounded(&x_full[(int)(j % XSTAGES)], (uint32_t)(j / XSTAGES) & 1u,
+                                              &g_glint_kernel_error);
+            }
+        }
+    } else if (warp == kPlaneWarp) {
+        /* ---- plane producer (both CTAs): hole, plug and absmax of this CTA's weight rows */
+        if (lane == 0) {
+            Ring st;
+            int64_t issued = 0;
+            for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
+                const int nr = (tile / args.mtiles) * (2 * BN) + (int)rank * BN;
+                for (int ks = 0; ks < ksteps && alive; ks += PSTEPS, st.next<PSTAGES>()) {
+                    if (!wait_or_fail(&p_empty[st.i], st.ph ^ 1u, alive))
+                        break;
+                    uint8_t *sb = pring + st.i * kPStage;
+                    mbar_expect_tx(&p_full[st.i], kPStage);
+                    tma_load_2d(sb, &maps.h, &p_full[st.i], ks * (BK / 2), nr);
+                    tma_load_2d(sb + kPlaneBox, &maps.p, &p_full[st.i], ks * (BK / 2), nr);
+                    tma_load_2d(sb + 2 * kPlaneBox, &maps.am, &p_full[st.i], ks, nr);
                     ++issued;
                 }
             }
             if (!alive) {
-                /* let the loads already issued land before the CTA exits */
                 bool drain = true;
-                for (int64_t j = issued > STAGES ? issued - STAGES : 0; j < issued && drain; ++j) {
-                    const int s = (int)(j % STAGES);
-                    const uint32_t ph = (uint32_t)(j / STAGES) & 1u;
-                    drain = mbar_wait_bounded(&p_full[s], ph, &g_glint_kernel_error) &&
-                            (!leader || mbar_wait_bounded(&x_full[s], ph, &g_glint_kernel_error));
-                }
+                for (int64_t j = issued > PSTAGES ? issued - PSTAGES : 0; j < issued && drain; ++j)
+                    drain = mbar_wait_bounded(&p_full[(int)(j % PSTAGES)], (uint32_t)(j / PSTAGES) & 1u,
+                                              &g_glint_kernel_error);
             }
         }
     } else if (warp == 1) {
@@ -327,17 +377,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (leader && lane == 0) {
             Ring st, ws;
             int t = 0;
-            const uint32_t empty0 = peer_addr(saddr(&empty[0]), 0), empty1 = peer_addr(saddr(&empty[0]), 1);
+            const uint32_t empty0 = peer_addr(saddr(&x_empty[0]), 0), empty1 = peer_addr(saddr(&x_empty[0]), 1);
             const uint32_t wempty0 = peer_addr(saddr(&w_empty[0]), 0), wempty1 = peer_addr(saddr(&w_empty[0]), 1);
             for (int tile = pair; tile < ntiles_total && alive; tile += npairs, ++t) {
                 if (t >= 1 && !wait_or_fail(acc_empty, (uint32_t)(t - 1) & 1u, alive))
                     break;
                 tc_fence_after();
-                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<STAGES>(), ws.next<WSLOTS>()) {
+                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<XSTAGES>(), ws.next<WSLOTS>()) {
                     if (!wait_or_fail(&x_full[st.i], st.ph, alive) || !wait_or_fail(&w_full[ws.i], ws.ph, alive))
                         break;
                     tc_fence_after();
-                    const uint32_t xs = saddr(smem + st.i * kStageBytes);
+                    const uint32_t xs = saddr(xring + st.i * kStageX);
                     const uint32_t wa = tmem + kWCol + (uint32_t)ws.i * (BK / 2);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
@@ -359,38 +409,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp < kEpi0) {
-        /* ---- dequantisers: thread -> weight row r (TMEM lane), 32 weights (K half kq) */
+        /* ---- dequantisers: thread -> weight row r (TMEM lane), kWpt weights (K part kq) */
         const int q = warp & 3, kq = (warp - kDeq0) >> 2;
         const int r = q * 32 + (int)lane;
         const uint32_t lutb = saddr(lut), lane4 = lane * 4u;
-        /* byte offset of this thread's 16 plane bytes in the row; 32B swizzle of the
-         * plane rows: 16-byte chunk index ^= bit 2 of the row */
-        const uint32_t pofs = (uint32_t)r * 32u + ((uint32_t)(kq ^ ((r >> 2) & 1)) << 4);
+        /* this thread's kWpt/2 plane bytes of K step j sit at byte j*32 + kq*kWpt/2 of
+         * the 128-byte row; 128B swizzle: 16-byte chunk index ^= row & 7 */
+        const uint32_t prow = (uint32_t)r * 128u, pswz = (uint32_t)(r & 7);
+        const uint32_t kb = (uint32_t)kq * (kWpt / 2);
         const uint32_t tw = tmem + ((uint32_t)(q * 32) << 16) + kWCol + (uint32_t)kq * (kWpt / 2);
         const uint32_t wfull0 = peer_addr(saddr(&w_full[0]), 0);
         float4 sc4 = make_float4(0.f, 0.f, 0.f, 0.f);
         Ring st, ws;
+        int pend = -1; /* weight slot whose tcgen05.st is issued but not yet published */
         for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
-            for (int ks = 0; ks < ksteps && alive; ++ks, st.next<STAGES>(), ws.next<WSLOTS>()) {
-                if (!warp_wait(&p_full[st.i], st.ph, alive))
+            for (int ks = 0; ks < ksteps && alive; ++ks, ws.next<WSLOTS>()) {
+                const int j = ks & (PSTEPS - 1);
+                if (j == 0 && !warp_wait(&p_full[st.i], st.ph, alive))
                     break;
-                const uint32_t ps = saddr(smem + st.i * kStageBytes + kStageX);
-                const uint4 H = lds128(ps + pofs);
-                const uint4 P = lds128(ps + kPlaneBox + pofs);
-                if ((ks & 3) == 0) {
+                const uint32_t ps = saddr(pring + st.i * kPStage);
+                const uint32_t kbj = (uint32_t)j * (BK / 2) + kb;
+                const uint32_t pofs = prow + ((((kbj >> 4) ^ pswz) << 4) | (kbj & 15u));
+                uint32_t hw[kWpt / 8], pw[kWpt / 8];
+                lds_plane(ps + pofs, hw);
+                lds_plane(ps + kPlaneBox + pofs, pw);
+                if (j == 0) {
                     const uint4 a4 = lds128(ps + 2 * kPlaneBox + (uint32_t)r * 16u);
                     sc4 = make_float4(__uint_as_float(a4.x), __uint_as_float(a4.y), __uint_as_float(a4.z),
                                       __uint_as_float(a4.w));
                 }
-                const float sc = (ks & 3) == 0 ? sc4.x : (ks & 3) == 1 ? sc4.y : (ks & 3) == 2 ? sc4.z : sc4.w;
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive(&empty[st.i]);
+                const float sc = j == 0 ? sc4.x : j == 1 ? sc4.y : j == 2 ? sc4.z : sc4.w;
+                if (j == PSTEPS - 1) {
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive(&p_empty[st.i]);
+                    st.next<PSTAGES>();
+                }
                 /* the first use of a slot waits on parity 1: returns at once */
                 if (!warp_wait(&w_empty[ws.i], ws.ph ^ 1u, alive))
                     break;
                 tc_fence_after();
-                const uint32_t hw[4] = {H.x, H.y, H.z, H.w}, pw[4] = {P.x, P.y, P.z, P.w};
                 const uint64_t sc2 = pack2f(sc, sc);
                 uint32_t o[kWpt / 2];
 #pragma unroll
@@ -410,13 +468,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         o[wq * 4 + b] = *reinterpret_cast<uint32_t *>(&h2);
                     }
                 }
-                tmem_st16(tw + (uint32_t)ws.i * (BK / 2), o);
-                tmem_st_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive_remote(wfull0 + (uint32_t)ws.i * 8u);
+                if (GLINT_GEMM_DEFER_ST) {
+                    /* publish the previous step's slot while this step's values are ready */
+                    if (pend >= 0) {
+                        tmem_st_wait();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            mbar_arrive_remote(wfull0 + (uint32_t)pend * 8u);
+                    }
+                    tmem_st(tw + (uint32_t)ws.i * (BK / 2), o);
+                    pend = ws.i;
+                } else {
+                    tmem_st(tw + (uint32_t)ws.i * (BK / 2), o);
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive_remote(wfull0 + (uint32_t)ws.i * 8u);
+                }
             }
+        }
+        if (pend >= 0) {
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (alive && lane == 0)
+                mbar_arrive_remote(wfull0 + (uint32_t)pend * 8u);
         }
     } else {
         /* ---- epilogue: warp w reads TMEM lanes 32*(w%4): weight rows n, columns m */
@@ -547,9 +625,9 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
     if (!encode_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BMH,
                     CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                    BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_32B) ||
+                    PSTEPS * BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                    BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_32B) ||
+                    PSTEPS * BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N,
                     (uint64_t)K / 64 * 4, 4, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
         return kLaunch;
