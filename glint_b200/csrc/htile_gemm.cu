@@ -46,6 +46,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "glint_internal.h"
@@ -65,18 +66,12 @@ constexpr int XSTAGES = 5; /* shared-memory ring of activation tiles (freed by t
 constexpr int PSTAGES = 2; /* shared-memory ring of plane tiles, 4 K steps each (freed by the dequantisers) */
 constexpr int PSTEPS = 4;  /* K steps per plane stage: 128-byte plane rows, one absmax box */
 constexpr int WSLOTS = 8;  /* TMEM weight ring */
-#ifndef GLINT_GEMM_DEQ_WARPS
-#define GLINT_GEMM_DEQ_WARPS 8
-#endif
-constexpr int kDeqWarps = GLINT_GEMM_DEQ_WARPS, kEpiWarps = 4;
-static_assert(kDeqWarps == 8 || kDeqWarps == 16, "2 or 4 dequantiser warps per TMEM lane quadrant");
-#ifndef GLINT_GEMM_DEFER_ST
-#define GLINT_GEMM_DEFER_ST 0
-#endif
+constexpr int kDeqWarps = 8, kEpiWarps = 4;
 constexpr int kDeq0 = 2, kEpi0 = kDeq0 + kDeqWarps; /* first warp of each role */
 constexpr int kPlaneWarp = kEpi0 + kEpiWarps;       /* plane producer */
 constexpr int kThreads = (kPlaneWarp + 1) * 32;
-constexpr int kWpt = BK * 4 / kDeqWarps;            /* weights per dequantiser thread and K step */
+constexpr int kWpt = BK * 4 / kDeqWarps;            /* 32 weights per dequantiser thread and K step */
+constexpr int kPartFloats = 8 * 32 * 32;            /* one epilogue warp's share of a partial tile */
 constexpr int kStageX = BMH * BK * 2;               /* 16 KB */
 constexpr int kPlaneBox = BN * PSTEPS * BK / 2;     /* 16 KB: 128 rows x 128 B */
 constexpr int kAmBox = BN * PSTEPS * 4;             /* 2 KB: 128 rows x 4 blocks */
@@ -189,23 +184,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
                    "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[8])
-{
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
-                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-                 : "memory");
-}
-/* kWpt/8 words of a plane row: 8 bytes (LDS.64) or 16 bytes (LDS.128) */
-__device__ __forceinline__ void lds_plane(uint32_t a, uint32_t (&w)[2])
-{
-    const uint2 v = lds64(a);
-    w[0] = v.x, w[1] = v.y;
-}
-__device__ __forceinline__ void lds_plane(uint32_t a, uint32_t (&w)[4])
-{
-    const uint4 v = lds128(a);
-    w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
-}
 __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[16])
 {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -257,11 +235,70 @@ struct GemmArgs {
     int M, N, K;
     int y_bf16;
     int mtiles, ntiles;
+    int G;        /* K groups (PSTEPS K steps) per tile */
+    int S;        /* tiles 0 .. S-1 are cut into units shared evenly by the pairs */
+    int R;        /* whole-tile rounds after that: pair p takes tiles S + p + r P, r < R */
+    int U;        /* units of the shared part: S x G */
+    int tiles;
+    float *ws;    /* partial tiles of split tiles: [pair][slot 2][rank 2][quadrant 4][kPartFloats] */
+    int *counters; /* per tile, rank and quadrant: contributors done (reset by the last) */
+};
+
+/* Work split (stream-K for the first S tiles, then data-parallel rounds): the
+ * units (tile, K group) of tiles 0 .. S-1 are cut into P equal ranges, pair p
+ * owning [unit_begin(p), unit_begin(p + 1)); the remaining R * P tiles go
+ * whole, round-robin.  S = tiles mod P + P (or all tiles when there are fewer
+ * than 2P), so every pair ends at the same time, a shared tile has at most a
+ * few contributors, and their sums are done while the whole tiles run. */
+__device__ __forceinline__ int unit_begin(const GemmArgs &a, int p, int P) { return (int)((int64_t)p * a.U / P); }
+__device__ __forceinline__ int pair_of(const GemmArgs &a, int u, int P)
+{
+    return (int)(((int64_t)(u + 1) * P - 1) / a.U);
+}
+/* Segments of one pair's work in order: tile T, K groups [ga, gb). */
+struct Segments {
+    int r = 0, u = 0, ue = 0;
+    __device__ __forceinline__ bool next(const GemmArgs &a, int pair, int P, int &T, int &ga, int &gb)
+    {
+        if (u < ue) {
+            T = u / a.G;
+            ga = u - T * a.G;
+            gb = min(a.G, ga + (ue - u));
+            u += gb - ga;
+            return true;
+        }
+        if (r < a.R && a.S + r * P + pair < a.tiles) {
+            T = a.S + r++ * P + pair, ga = 0, gb = a.G;
+            return true;
+        }
+        return false;
+    }
 };
 
 struct Maps {
     CUtensorMap x, h, p, am;
 };
+
+/* rows m0 .. m0+jl-1 of y at column n from 32 accumulator values (f32 bits) */
+__device__ __forceinline__ void store_y(const GemmArgs &args, const uint32_t (&v)[32], int m0, int jl, int n)
+{
+    if (n >= args.N)
+        return;
+    const size_t step = (size_t)args.N;
+    if (args.y_bf16) {
+        __nv_bfloat16 *yp = static_cast<__nv_bfloat16 *>(args.y) + (size_t)m0 * step + n;
+#pragma unroll
+        for (int j = 0; j < 32; ++j, yp += step)
+            if (j < jl)
+                *yp = __float2bfloat16_rn(__uint_as_float(v[j]));
+    } else {
+        float *yp = static_cast<float *>(args.y) + (size_t)m0 * step + n;
+#pragma unroll
+        for (int j = 0; j < 32; ++j, yp += step)
+            if (j < jl)
+                *yp = __uint_as_float(v[j]);
+    }
+}
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     htile_gemm_kernel(const __grid_constant__ Maps maps, const GemmArgs args)
@@ -287,8 +324,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
-    const int ksteps = args.K / BK;
-    const int ntiles_total = args.mtiles * args.ntiles;
+    const int G = args.G;
+    const int ub = unit_begin(args, pair, npairs), ue = unit_begin(args, pair + 1, npairs);
+    const Segments seg0{0, ub, ue};
+    int T, ga, gb;
 
     for (int i = threadIdx.x; i < 256 * 32; i += kThreads)
         lut[(i >> 5) * 64 + (i & 31)] = (&g_cells[0][0])[i >> 5];
@@ -327,9 +366,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             Ring st;
             int64_t issued = 0;
-            for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
-                const int mr = (tile % args.mtiles) * BMX + (int)rank * BMH;
-                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<XSTAGES>()) {
+            for (Segments sg = seg0; alive && sg.next(args, pair, npairs, T, ga, gb);) {
+                const int mr = (T % args.mtiles) * BMX + (int)rank * BMH;
+                for (int ks = ga * PSTEPS; ks < gb * PSTEPS && alive; ++ks, st.next<XSTAGES>()) {
                     /* the first use of a stage waits on parity 1: returns at once */
                     if (!wait_or_fail(&x_empty[st.i], st.ph ^ 1u, alive))
                         break;
@@ -352,9 +391,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             Ring st;
             int64_t issued = 0;
-            for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
-                const int nr = (tile / args.mtiles) * (2 * BN) + (int)rank * BN;
-                for (int ks = 0; ks < ksteps && alive; ks += PSTEPS, st.next<PSTAGES>()) {
+            for (Segments sg = seg0; alive && sg.next(args, pair, npairs, T, ga, gb);) {
+                const int nr = (T / args.mtiles) * (2 * BN) + (int)rank * BN;
+                for (int ks = ga * PSTEPS; ks < gb * PSTEPS && alive; ks += PSTEPS, st.next<PSTAGES>()) {
                     if (!wait_or_fail(&p_empty[st.i], st.ph ^ 1u, alive))
                         break;
                     uint8_t *sb = pring + st.i * kPStage;
@@ -379,11 +418,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int t = 0;
             const uint32_t empty0 = peer_addr(saddr(&x_empty[0]), 0), empty1 = peer_addr(saddr(&x_empty[0]), 1);
             const uint32_t wempty0 = peer_addr(saddr(&w_empty[0]), 0), wempty1 = peer_addr(saddr(&w_empty[0]), 1);
-            for (int tile = pair; tile < ntiles_total && alive; tile += npairs, ++t) {
+            for (Segments sg = seg0; alive && sg.next(args, pair, npairs, T, ga, gb); ++t) {
                 if (t >= 1 && !wait_or_fail(acc_empty, (uint32_t)(t - 1) & 1u, alive))
                     break;
                 tc_fence_after();
-                for (int ks = 0; ks < ksteps && alive; ++ks, st.next<XSTAGES>(), ws.next<WSLOTS>()) {
+                const int k0 = ga * PSTEPS;
+                for (int ks = k0; ks < gb * PSTEPS && alive; ++ks, st.next<XSTAGES>(), ws.next<WSLOTS>()) {
                     if (!wait_or_fail(&x_full[st.i], st.ph, alive) || !wait_or_fail(&w_full[ws.i], ws.ph, alive))
                         break;
                     tc_fence_after();
@@ -392,7 +432,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
                         umma_pair_ts_bf16(tmem + kAccCol, wa + kk * 8, sw128_desc(xs + kk * 32), kIdesc,
-                                          (ks > 0 || kk > 0) ? 1u : 0u);
+                                          (ks > k0 || kk > 0) ? 1u : 0u);
                     umma_commit_to(empty0 + (uint32_t)st.i * 8u);
                     umma_commit_to(empty1 + (uint32_t)st.i * 8u);
                     umma_commit_to(wempty0 + (uint32_t)ws.i * 8u);
@@ -421,18 +461,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const uint32_t wfull0 = peer_addr(saddr(&w_full[0]), 0);
         float4 sc4 = make_float4(0.f, 0.f, 0.f, 0.f);
         Ring st, ws;
-        int pend = -1; /* weight slot whose tcgen05.st is issued but not yet published */
-        for (int tile = pair; tile < ntiles_total && alive; tile += npairs) {
-            for (int ks = 0; ks < ksteps && alive; ++ks, ws.next<WSLOTS>()) {
+        for (Segments sg = seg0; alive && sg.next(args, pair, npairs, T, ga, gb);) {
+            for (int ks = ga * PSTEPS; ks < gb * PSTEPS && alive; ++ks, ws.next<WSLOTS>()) {
                 const int j = ks & (PSTEPS - 1);
                 if (j == 0 && !warp_wait(&p_full[st.i], st.ph, alive))
                     break;
                 const uint32_t ps = saddr(pring + st.i * kPStage);
                 const uint32_t kbj = (uint32_t)j * (BK / 2) + kb;
                 const uint32_t pofs = prow + ((((kbj >> 4) ^ pswz) << 4) | (kbj & 15u));
-                uint32_t hw[kWpt / 8], pw[kWpt / 8];
-                lds_plane(ps + pofs, hw);
-                lds_plane(ps + kPlaneBox + pofs, pw);
+                const uint4 H = lds128(ps + pofs), P = lds128(ps + kPlaneBox + pofs);
+                const uint32_t hw[4] = {H.x, H.y, H.z, H.w}, pw[4] = {P.x, P.y, P.z, P.w};
                 if (j == 0) {
                     const uint4 a4 = lds128(ps + 2 * kPlaneBox + (uint32_t)r * 16u);
                     sc4 = make_float4(__uint_as_float(a4.x), __uint_as_float(a4.y), __uint_as_float(a4.z),
@@ -468,74 +506,113 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         o[wq * 4 + b] = *reinterpret_cast<uint32_t *>(&h2);
                     }
                 }
-                if (GLINT_GEMM_DEFER_ST) {
-                    /* publish the previous step's slot while this step's values are ready */
-                    if (pend >= 0) {
-                        tmem_st_wait();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0)
-                            mbar_arrive_remote(wfull0 + (uint32_t)pend * 8u);
-                    }
-                    tmem_st(tw + (uint32_t)ws.i * (BK / 2), o);
-                    pend = ws.i;
-                } else {
-                    tmem_st(tw + (uint32_t)ws.i * (BK / 2), o);
-                    tmem_st_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0)
-                        mbar_arrive_remote(wfull0 + (uint32_t)ws.i * 8u);
-                }
+                tmem_st(tw + (uint32_t)ws.i * (BK / 2), o);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_remote(wfull0 + (uint32_t)ws.i * 8u);
             }
         }
-        if (pend >= 0) {
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (alive && lane == 0)
-                mbar_arrive_remote(wfull0 + (uint32_t)pend * 8u);
-        }
     } else {
-        /* ---- epilogue: warp w reads TMEM lanes 32*(w%4): weight rows n, columns m */
+        /* ---- epilogue: warp w reads TMEM lanes 32*(w%4): weight rows n, columns m.
+         * A whole tile goes straight to y.  A tile split between pairs: every
+         * contributor stores its f32 partial (L2 only) and counts itself in; the
+         * last one adds all partials in K order, so y does not depend on which
+         * pair finished last. */
         const int q = warp & 3;
         const uint32_t accempty0 = peer_addr(saddr(acc_empty), 0);
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + kAccCol;
         int t = 0;
-        for (int tile = pair; tile < ntiles_total && alive; tile += npairs, ++t) {
+        for (Segments sg = seg0; alive && sg.next(args, pair, npairs, T, ga, gb); ++t) {
             if (!warp_wait(acc_full, (uint32_t)t & 1u, alive))
                 break;
             tc_fence_after();
-            const int m0 = (tile % args.mtiles) * BMX, n0 = (tile / args.mtiles) * (2 * BN);
+            const int m0 = (T % args.mtiles) * BMX, n0 = (T / args.mtiles) * (2 * BN);
             const int n = n0 + (int)rank * BN + q * 32 + (int)lane;
-            const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + kAccCol;
             const int mlim = min(BMX, args.M - m0);
+            const bool whole = ga == 0 && gb == G;
+            if (whole) {
 #pragma unroll 1
-            for (int c = 0; c < BMX / 32 && c * 32 < mlim; ++c) {
+                for (int c = 0; c < BMX / 32 && c * 32 < mlim; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(tb + c * 32, v);
+                    tmem_ld_wait();
+                    store_y(args, v, m0 + c * 32, min(32, mlim - c * 32), n);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_remote(accempty0);
+                continue;
+            }
+            /* slot 0: the first segment of this pair's range, slot 1: its last */
+            const int slot = ub >= T * G ? 0 : 1;
+            float *mine = args.ws + ((((size_t)pair * 2 + slot) * 2 + rank) * 4 + q) * kPartFloats;
+#pragma unroll 1
+            for (int c = 0; c < BMX / 32; ++c) {
                 uint32_t v[32];
                 tmem_ld32(tb + c * 32, v);
                 tmem_ld_wait();
-                if (n < args.N) {
-                    const int jl = min(32, mlim - c * 32);
-                    const size_t step = (size_t)args.N;
-                    if (args.y_bf16) {
-                        __nv_bfloat16 *yp = static_cast<__nv_bfloat16 *>(args.y) + (size_t)(m0 + c * 32) * step + n;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j, yp += step)
-                            if (j < jl)
-                                *yp = __float2bfloat16_rn(__uint_as_float(v[j]));
-                    } else {
-                        float *yp = static_cast<float *>(args.y) + (size_t)(m0 + c * 32) * step + n;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j, yp += step)
-                            if (j < jl)
-                                *yp = __uint_as_float(v[j]);
-                    }
-                }
+                for (int j = 0; j < 32; ++j)
+                    __stcg(mine + (c * 32 + j) * 32 + lane, __uint_as_float(v[j]));
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0)
-                mbar_arrive_remote(accempty0);
+                mbar_arrive_remote(accempty0); /* accumulator free: the rest works from memory */
+            __threadfence();
+            __syncwarp();
+            int *cnt = args.counters + ((size_t)T * 2 + rank) * 4 + q;
+            const int pf = pair_of(args, T * G, npairs), pl = pair_of(args, (T + 1) * G - 1, npairs);
+            int prev = 0;
+            if (lane == 0)
+                prev = atomicAdd(cnt, 1);
+            prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
+            if (prev != pl - pf)
+                continue;
+            /* last contributor: sum the partials in K order, loading up to four
+             * contributors' values before adding them */
+            __threadfence();
+            if (lane == 0)
+                *cnt = 0;
+#pragma unroll 1
+            for (int c = 0; c < BMX / 32 && c * 32 < mlim; ++c) {
+                uint32_t v[32];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float acc[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        acc[j] = 0.f;
+#pragma unroll 1
+                    for (int p0 = pf; p0 <= pl; p0 += 4) {
+                        float part[4][16];
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int pq = min(p0 + b, pl);
+                            const int sq = unit_begin(args, pq, npairs) >= T * G ? 0 : 1;
+                            const float *src = args.ws + ((((size_t)pq * 2 + sq) * 2 + rank) * 4 + q) * kPartFloats +
+                                               c * 1024 + h * 512 + lane;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                part[b][j] = __ldcg(src + j * 32);
+                        }
+#pragma unroll
+                        for (int b = 0; b < 4; ++b)
+                            if (p0 + b <= pl) {
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    acc[j] += part[b][j];
+                            }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        v[h * 16 + j] = __float_as_uint(acc[j]);
+                }
+                store_y(args, v, m0 + c * 32, min(32, mlim - c * 32), n);
+            }
         }
     }
     tc_fence_before();
@@ -589,6 +666,50 @@ bool encode_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64
     return enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+/* Per (device, stream) scratch for split tiles: partial sums and per-tile
+ * counters (zeroed once; the last contributor of a tile zeroes its counter). */
+struct GemmScratch {
+    float *ws = nullptr;
+    size_t ws_floats = 0;
+    int *counters = nullptr;
+    size_t n_counters = 0;
+};
+std::mutex g_gemm_scratch_mu;
+std::unordered_map<uint64_t, GemmScratch> g_gemm_scratch;
+
+bool gemm_scratch(cudaStream_t st, size_t ws_floats, size_t n_counters, float **ws, int **counters)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return false;
+    const uint64_t key = (reinterpret_cast<uint64_t>(st) << 8) ^ (uint64_t)dev;
+    std::lock_guard<std::mutex> lk(g_gemm_scratch_mu);
+    GemmScratch &S = g_gemm_scratch[key];
+    if (S.ws_floats < ws_floats) {
+        if (S.ws)
+            cudaFree(S.ws);
+        S.ws = nullptr, S.ws_floats = 0;
+        if (cudaMalloc(&S.ws, ws_floats * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        S.ws_floats = ws_floats;
+    }
+    if (S.n_counters < n_counters) {
+        if (S.counters)
+            cudaFree(S.counters);
+        S.counters = nullptr, S.n_counters = 0;
+        if (cudaMalloc(&S.counters, n_counters * sizeof(int)) != cudaSuccess ||
+            cudaMemset(S.counters, 0, n_counters * sizeof(int)) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        S.n_counters = n_counters;
+    }
+    *ws = S.ws, *counters = S.counters;
+    return true;
+}
+
 /* CTA pairs that fit on the device at once (one pair per two SMs at most) */
 int max_pairs()
 {
@@ -633,9 +754,24 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
         return kLaunch;
     if (!ensure_smem((const void *)htile_gemm_kernel, kSmemBytes))
         return kLaunch;
-    GemmArgs a{y, M, N, K, y_bf16 ? 1 : 0, (M + BMX - 1) / BMX, (N + 2 * BN - 1) / (2 * BN)};
+    GemmArgs a{};
+    a.y = y, a.M = M, a.N = N, a.K = K, a.y_bf16 = y_bf16 ? 1 : 0;
+    a.mtiles = (M + BMX - 1) / BMX, a.ntiles = (N + 2 * BN - 1) / (2 * BN);
+    a.G = K / (PSTEPS * BK);
     const int tiles = a.mtiles * a.ntiles;
-    const int pairs = std::max(1, std::min(tiles, max_pairs()));
+    /* whole tiles only, unless the last data-parallel round would leave more than
+     * 2% of the pairs' time idle and there are at least two rounds, so that the
+     * shared tiles' sums overlap whole tiles */
+    const int maxp = max_pairs();
+    const int rounds = (tiles + maxp - 1) / maxp;
+    const bool split = tiles >= 2 * maxp && (double)(rounds * maxp - tiles) > 0.02 * rounds * maxp;
+    const int pairs = split ? maxp : std::max(1, std::min(tiles, maxp));
+    a.tiles = tiles;
+    a.R = split ? tiles / pairs - 1 : (tiles + pairs - 1) / pairs;
+    a.S = split ? tiles - a.R * pairs : 0;
+    a.U = a.S * a.G;
+    if (!gemm_scratch(st, (size_t)pairs * 2 * 2 * 4 * kPartFloats, (size_t)tiles * 8, &a.ws, &a.counters))
+        return kLaunch;
     htile_gemm_kernel<<<2 * pairs, kThreads, kSmemBytes, st>>>(maps, a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
 }

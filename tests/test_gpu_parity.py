@@ -422,10 +422,12 @@ def test_htile_matches_reference_library():
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 256, 4096), (300, 200, 128), (129, 264, 192),
                                    (512, 512, 1024), (1024, 512, 4096), (256, 4096, 256), (300, 200, 256),
-                                   (129, 264, 512), (640, 1000, 768), (2048, 384, 1024), (1100, 130, 2048)])
+                                   (129, 264, 512), (640, 1000, 768), (2048, 384, 1024), (1100, 130, 2048),
+                                   (256, 512, 4096), (384, 4608, 1280)])
 def test_htile_prefill_tcgen05_vs_oracle(M, N, K):
     """Prefill shapes take the tcgen05 path in fast mode: within 1e-2 relative of the
-    f32 dequant-then-matmul oracle, f32 and BF16 y, ragged M and N edges."""
+    f32 dequant-then-matmul oracle, f32 and BF16 y, ragged M and N edges, tiles
+    split between 1 to 16 CTA pairs, and bit-identical repeated calls."""
     from glint_b200 import glint_cuda
     L = glint_cuda.load()
     assert L.glint_kernel_error(1) == 0
@@ -435,9 +437,12 @@ def test_htile_prefill_tcgen05_vs_oracle(M, N, K):
     ref = O.htile(ho, po, ao, x, M, N, K, 64).astype(np.float64)
     dev = [torch.from_numpy(a).cuda() for a in (ho, po, ao)]
     dx = to_dev_bf16(x).view(M, K)
-    yf = D().htile(dx, *dev, N, 64, mode="fast").cpu().numpy()
+    yt = D().htile(dx, *dev, N, 64, mode="fast")
+    yt2 = D().htile(dx, *dev, N, 64, mode="fast")
+    yf = yt.cpu().numpy()
     yb = D().htile(dx, *dev, N, 64, mode="fast", out_dtype=torch.bfloat16).float().cpu().numpy()
     assert L.glint_kernel_error(1) == 0
+    assert torch.equal(yt, yt2)  # split tiles are summed in a fixed order
     assert np.all(np.isfinite(yf))
     assert rel_err(yf, ref) <= FAST_TOL, rel_err(yf, ref)
     assert rel_err(yb, ref) <= FAST_TOL, rel_err(yb, ref)
