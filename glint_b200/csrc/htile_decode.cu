@@ -52,9 +52,15 @@ __device__ int g_decode_error = 0;
 namespace {
 
 constexpr int kRows = 256;                 /* weight rows per unit */
-constexpr int kKU = 128;                   /* k per unit */
-constexpr int kPlaneTile = kRows * kKU / 2; /* 16 KB per plane (64 B per row, 64B swizzle) */
-constexpr int kAmTile = kRows * 4 * 4;     /* 256 rows x 4 blocks x f32: this unit's 2 blocks + its neighbour's */
+/* k per unit: 256 (128-byte plane rows, 128B swizzle, two ring slots) while the
+ * activation slice is small, else 128 (64-byte rows, 64B swizzle, three slots).
+ * Wide rows matter: a TMA row request carries the row, and the bytes in flight
+ * per SM grow with it. */
+template <int MT>
+constexpr int ku_of() { return MT <= 2 ? 256 : 128; }
+template <int MT>
+constexpr int plane_tile() { return kRows * ku_of<MT>() / 2; } /* 32 or 16 KB */
+constexpr int kAmTile = kRows * 4 * 4; /* 256 rows x 4 blocks x f32: the unit's blocks (k 256) or its pair's (k 128) */
 constexpr int kConsumers = 16;             /* 16 rows each */
 constexpr int kThreads = (kConsumers + 1) * 32;
 /* codebook hi|lo pairs, one replica per lane, entry stride 256 B: the lookup address
@@ -62,11 +68,11 @@ constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kLutBytes = 256 * 256;
 /* x tile of a unit: 2 boxes of 64 k x 8*MT rows (128B swizzle), 1 KB per 8 rows */
 template <int MT>
-constexpr int x_tile() { return 2 * 8 * MT * 128; }
+constexpr int x_tile() { return (ku_of<MT>() / 64) * 8 * MT * 128; }
 template <int MT>
-constexpr int slot_bytes() { return 2 * kPlaneTile + kAmTile + x_tile<MT>(); }
+constexpr int slot_bytes() { return 2 * plane_tile<MT>() + kAmTile + x_tile<MT>(); }
 template <int MT>
-constexpr int n_slots() { return 3; }
+constexpr int n_slots() { return ku_of<MT>() == 256 ? 2 : 3; } /* as many as fit in 227 KB */
 template <int MT>
 constexpr int smem_bytes() { return kLutBytes + 1024 + n_slots<MT>() * slot_bytes<MT>() + 2 * 8 * n_slots<MT>() + 64; }
 
@@ -117,6 +123,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 {
     constexpr int kSlots = n_slots<MT>();
     constexpr int kSlotBytes = slot_bytes<MT>();
+    constexpr int kKU = ku_of<MT>(), kPlaneTile = plane_tile<MT>();
+    static_assert(smem_bytes<MT>() <= 232448, "shared memory");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem_raw);
     uint8_t *ring = reinterpret_cast<uint8_t *>(
@@ -124,21 +132,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + kSlots * kSlotBytes);
     uint64_t *empty = full + kSlots;
 
-    /* codebook as BF16 hi/lo pairs, one replica per lane (first 128 B of each 256-B
-     * entry row): each thread converts one entry and writes its 32 replicas */
-    if (threadIdx.x < 256) {
-        const uint32_t e = split_pair(g_cells[threadIdx.x >> 4][threadIdx.x & 15]);
-        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 64);
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-            dst[r] = make_uint4(e, e, e, e);
-    }
+    /* barriers first, so the producer can start streaming while the consumers
+     * build the codebook */
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumers);
         }
         mbar_init_fence();
+    }
+    if (threadIdx.x == kConsumers * 32) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&hmap) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&pmap) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&amap) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
     }
     __syncthreads();
 
@@ -149,24 +156,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kConsumers) {
         if (lane == 0) {
+            auto load_x = [&](int64_t u, int s) {
+                const int ku = (int)(u % a.KU);
+                uint8_t *slot = ring + s * kSlotBytes;
+#pragma unroll
+                for (int c = 0; c < kKU / 64; ++c)
+                    tma_load_2d(slot + 2 * kPlaneTile + kAmTile + c * (8 * MT * 128), &xmap, &full[s],
+                                ku * kKU + c * 64, 0);
+            };
             int64_t i = 0;
             bool ok = true;
             for (int64_t u = u0; u < u1; ++u, ++i) {
                 const int s = (int)(i % kSlots);
                 const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
-                if (i >= kSlots && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_decode_error)))
+                if (i >= kSlots && !(ok = mbar_wait_suspend_bounded(&empty[s], ph ^ 1u, &g_decode_error)))
                     break;
                 const int rb = (int)(u / a.KU), ku = (int)(u % a.KU);
                 uint8_t *slot = ring + s * kSlotBytes;
                 mbar_expect_tx(&full[s], kSlotBytes);
                 tma_load_2d(slot, &hmap, &full[s], ku * (kKU / 2), rb * kRows);
                 tma_load_2d(slot + kPlaneTile, &pmap, &full[s], ku * (kKU / 2), rb * kRows);
-                /* absmax box at an even unit so the x coordinate stays 16-byte aligned */
-                tma_load_2d(slot + 2 * kPlaneTile, &amap, &full[s], (ku >> 1) * 4, rb * kRows);
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    tma_load_2d(slot + 2 * kPlaneTile + kAmTile + c * (8 * MT * 128), &xmap, &full[s], ku * kKU + c * 64, 0);
+                /* absmax box of 4 blocks: the unit's own (k 256) or, for k 128, taken at an
+                 * even unit so the x coordinate stays 16-byte aligned */
+                tma_load_2d(slot + 2 * kPlaneTile, &amap, &full[s], kKU == 256 ? ku * 4 : (ku >> 1) * 4, rb * kRows);
+                if (i >= kSlots) {
+                    load_x(u, s);
+                } else if (i == kSlots - 1 || u == u1 - 1) {
+                    /* The weights do not depend on earlier kernels, the activations may:
+                     * under programmatic dependent launch the first slots' weights are
+                     * already streaming while the previous kernel finishes (a no-op
+                     * otherwise). */
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    for (int64_t j = 0; j <= i; ++j)
+                        load_x(u0 + j, (int)j);
+                }
             }
+            /* all loads issued: the next kernel in the stream may start launching */
+            asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
             if (!ok) {
                 const int64_t issued = i;
                 for (int64_t j = issued > kSlots ? issued - kSlots : 0; j < issued; ++j)
@@ -176,6 +202,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return;
     }
+
+    /* codebook as BF16 hi/lo pairs, one replica per lane (first 128 B of each 256-B
+     * entry row): each thread converts one entry and writes its 32 replicas; the
+     * consumer warps then meet on named barrier 1 (the producer is not in it) */
+    if (threadIdx.x < 256) {
+        const uint32_t e = split_pair(g_cells[threadIdx.x >> 4][threadIdx.x & 15]);
+        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 64);
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            dst[r] = make_uint4(e, e, e, e);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    /* y, the workspace and its counters are touched only after the previous kernel
+     * in the stream is complete (no-op without programmatic dependent launch) */
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     /* consumer warp: rows r0 + g and r0 + g + 8 of each unit's 128 */
     const int g = (int)(lane >> 2), t = (int)(lane & 3);
@@ -190,8 +231,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     /* Publish this warp's sums for its 16 rows of row block rb (k units [k0, k1) of
      * the block): straight to y when this CTA covered the whole block, otherwise
-     * to the workspace; the last of the block's parts to arrive (a per row block
-     * and warp counter) adds the parts in k order and writes y. */
+     * to the workspace.  A CTA has at most two such partial blocks (the first and
+     * the last of its range); their counters are bumped at the end, after one
+     * fence, so the stores never stall the stream: the last of a block's parts
+     * to arrive (a per row block and warp counter) adds the parts in k order and
+     * writes y. */
+    int pend_rb[2] = {-1, -1}, pend_parts[2] = {0, 0}, npend = 0;
     auto flush = [&](int rb, int k0, int k1) {
         constexpr int MP = 8 * MT;
         const bool whole = k0 == 0 && k1 == a.KU;
@@ -220,19 +265,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (whole)
             return;
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0)
-            last = atomicAdd(&a.counters[rb * kConsumers + warp], 1) == parts - 1;
-        if (!__shfl_sync(0xFFFFFFFFu, last, 0))
+        pend_rb[npend] = rb, pend_parts[npend] = parts, ++npend;
+    };
+    auto finish = [&]() {
+        constexpr int MP = 8 * MT;
+        if (npend == 0)
             return;
         __threadfence();
+        __syncwarp();
+        /* acquire-release count: the last arrival sees every part's stores (its
+         * lanes read them from L2 after the count) */
+        int prev[2] = {0, 0};
+        if (lane == 0)
+            for (int j = 0; j < npend; ++j)
+                asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                             : "=r"(prev[j])
+                             : "l"(&a.counters[pend_rb[j] * kConsumers + warp])
+                             : "memory");
+        for (int j = 0; j < npend; ++j) {
+        const int rb = pend_rb[j], parts = pend_parts[j];
+        float *wsp = a.ws + ((int64_t)rb * a.max_parts) * kRows * MP;
+        if (__shfl_sync(0xFFFFFFFFu, prev[j], 0) != parts - 1)
+            continue;
+#pragma unroll
         for (int e = (int)lane; e < 16 * MP; e += 32) {
             const int row = r0 + e / MP, col = e % MP;
+            /* parts in k order; eight loads in flight at a time */
             float v = 0.f;
-            for (int pp = 0; pp < parts; ++pp)
-                v += __ldcg(wsp + ((int64_t)pp * kRows + row) * MP + col);
+            for (int p0 = 0; p0 < parts; p0 += 8) {
+                float t[8];
+#pragma unroll
+                for (int b = 0; b < 8; ++b)
+                    t[b] = p0 + b < parts ? __ldcg(wsp + ((int64_t)(p0 + b) * kRows + row) * MP + col) : 0.f;
+#pragma unroll
+                for (int b = 0; b < 8; ++b)
+                    if (p0 + b < parts)
+                        v += t[b];
+            }
             const int n = rb * kRows + row;
             if (n < a.N && col < a.M) {
                 if (BF16OUT)
@@ -243,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0)
             a.counters[rb * kConsumers + warp] = 0; /* ready for the next call */
+        }
     };
 
     int64_t i = 0;
@@ -259,25 +329,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int s = (int)(i % kSlots);
         const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
-        const bool ok = lane == 0 ? mbar_wait_bounded(&full[s], ph, &g_decode_error) : true;
+        const bool ok = lane == 0 ? mbar_wait_suspend_bounded(&full[s], ph, &g_decode_error) : true;
         if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0)) {
             cur_rb = -1; /* give up: no partial results are published */
             break;
         }
         const uint32_t slot = saddr(ring + s * kSlotBytes);
         const uint32_t xs = slot + 2 * kPlaneTile + kAmTile;
-        const uint32_t am_col = (uint32_t)(ku & 1) * 2;
+        const uint32_t am_col = kKU == 256 ? 0u : (uint32_t)(ku & 1) * 2;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < kKU / 64; ++c) {
             /* packed nibbles of rows g and g+8: 8 bytes at k-byte c*32 + t*8 of the
-             * row's 64 B (64B swizzle: 16-byte chunk j sits at j ^ ((row >> 1) & 3)) */
+             * row's kKU/2 bytes (16-byte chunk j sits at j ^ (row & 7) with the 128B
+             * swizzle, at j ^ ((row >> 1) & 3) with the 64B one) */
             uint32_t E[2][2], O[2][2];
             float sc[2];
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 const int row = r0 + g + 8 * r;
-                const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)((row >> 1) & 3);
-                const uint32_t off = (uint32_t)row * 64u + (chunk << 4) + (uint32_t)(t & 1) * 8u;
+                const uint32_t chunk =
+                    (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(kKU == 256 ? (row & 7) : ((row >> 1) & 3));
+                const uint32_t off = (uint32_t)row * (uint32_t)(kKU / 2) + (chunk << 4) + (uint32_t)(t & 1) * 8u;
                 const uint2 hw = lds64(slot + off), pw = lds64(slot + kPlaneTile + off);
                 const uint32_t hv[2] = {hw.x, hw.y}, pv[2] = {pw.x, pw.y};
 #pragma unroll
@@ -345,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (cur_rb >= 0)
         flush(cur_rb, seg_k0, (int)(u1 - 1 - (int64_t)cur_rb * a.KU) + 1);
+    finish();
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder()
@@ -426,24 +499,42 @@ struct Maps {
     CUtensorMap h, p, am, x;
 };
 
+/* Launched with programmatic stream serialisation (PDL): the kernel may start
+ * while the previous kernel in the stream drains; it streams weights at once and
+ * waits (griddepcontrol.wait) before reading activations or touching y and its
+ * workspace.  `pdl` is off for the fixed-scratch entry, whose counters are reset
+ * by a memset just before the launch. */
 template <int MT, bool SPLIT, bool BF16OUT>
-int launch_t(const Maps &m, const DecodeArgs &a, int grid, cudaStream_t st)
+int launch_t(const Maps &m, const DecodeArgs &a, int grid, cudaStream_t st, bool pdl)
 {
     auto kern = htile_decode_kernel<MT, SPLIT, BF16OUT>;
     if (!ensure_smem((const void *)kern, smem_bytes<MT>()))
         return kLaunch;
-    kern<<<grid, kThreads, smem_bytes<MT>(), st>>>(m.h, m.p, m.am, m.x, a);
-    return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes<MT>();
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, m.h, m.p, m.am, m.x, a) != cudaSuccess) {
+        cudaGetLastError();
+        return kLaunch;
+    }
+    return kOk;
 }
 
 template <bool SPLIT, bool BF16OUT>
-int launch_mt(int MT, const Maps &m, const DecodeArgs &a, int grid, cudaStream_t st)
+int launch_mt(int MT, const Maps &m, const DecodeArgs &a, int grid, cudaStream_t st, bool pdl)
 {
     if (MT == 1)
-        return launch_t<1, SPLIT, BF16OUT>(m, a, grid, st);
+        return launch_t<1, SPLIT, BF16OUT>(m, a, grid, st, pdl);
     if (MT == 2)
-        return launch_t<2, SPLIT, BF16OUT>(m, a, grid, st);
-    return launch_t<4, SPLIT, BF16OUT>(m, a, grid, st);
+        return launch_t<2, SPLIT, BF16OUT>(m, a, grid, st, pdl);
+    return launch_t<4, SPLIT, BF16OUT>(m, a, grid, st, pdl);
 }
 
 } // namespace
@@ -456,19 +547,28 @@ bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const floa
            aligned_to(am, 16) && aligned_to(x, 16) && N >= 1 && encoder() != nullptr;
 }
 
+/* tensor maps of one call: plane rows of kKU/2 bytes (64B or 128B swizzle) */
+bool decode_maps(Maps &maps, const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, int M,
+                 int N, int K, int MT)
+{
+    const int ku = MT <= 2 ? ku_of<1>() : ku_of<4>();
+    const CUtensorMapSwizzle sw = ku == 256 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    return make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                    (uint32_t)ku / 2, kRows, sw) &&
+           make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                    (uint32_t)ku / 2, kRows, sw) &&
+           make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
+                    4, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
+                    (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
                         OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
 {
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
     Maps maps;
-    if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
-                  4, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
-                  (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!decode_maps(maps, hole, plug, am, x, M, N, K, MT))
         return kLaunch;
     DecodeArgs a{};
     a.x = x;
@@ -476,7 +576,7 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
     a.M = M;
     a.N = N;
     a.K = K;
-    a.KU = K / kKU;
+    a.KU = K / (MT <= 2 ? ku_of<1>() : ku_of<4>());
     const int64_t rbs = (N + kRows - 1) / kRows;
     a.units = rbs * a.KU;
     const int grid = (int)std::min<int64_t>(a.units, sm_count());
@@ -490,8 +590,8 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
     a.counters = S.counters;
     const bool bf = yk == kOutBF16;
     if (mode == kPrecise)
-        return bf ? launch_mt<true, true>(MT, maps, a, grid, st) : launch_mt<true, false>(MT, maps, a, grid, st);
-    return bf ? launch_mt<false, true>(MT, maps, a, grid, st) : launch_mt<false, false>(MT, maps, a, grid, st);
+        return bf ? launch_mt<true, true>(MT, maps, a, grid, st, true) : launch_mt<true, false>(MT, maps, a, grid, st, true);
+    return bf ? launch_mt<false, true>(MT, maps, a, grid, st, true) : launch_mt<false, false>(MT, maps, a, grid, st, true);
 }
 
 /* ---- fixed-scratch variant ---------------------------------------------------
@@ -541,7 +641,7 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
     a.M = M;
     a.N = N;
     a.K = K;
-    a.KU = K / kKU;
+    a.KU = K / (MT <= 2 ? ku_of<1>() : ku_of<4>());
     const int64_t rbs = (N + kRows - 1) / kRows;
     a.units = rbs * a.KU;
     const int grid = (int)std::min<int64_t>(a.units, sm_count());
@@ -552,14 +652,7 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
     if (counter_bytes > kNoAllocCounterBytes || ws_bytes > kNoAllocBytes - kNoAllocCounterBytes)
         return kScratch;
     Maps maps;
-    if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
-                  kKU / 2, kRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
-                  4, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
-                  (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!decode_maps(maps, hole, plug, am, x, M, N, K, MT))
         return kLaunch;
     /* the array keeps the previous call's contents: the counters must start at 0 */
     a.counters = static_cast<int *>(base);
@@ -568,8 +661,8 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
         return kLaunch;
     const bool bf = yk == kOutBF16;
     if (mode == kPrecise)
-        return bf ? launch_mt<true, true>(MT, maps, a, grid, st) : launch_mt<true, false>(MT, maps, a, grid, st);
-    return bf ? launch_mt<false, true>(MT, maps, a, grid, st) : launch_mt<false, false>(MT, maps, a, grid, st);
+        return bf ? launch_mt<true, true>(MT, maps, a, grid, st, false) : launch_mt<true, false>(MT, maps, a, grid, st, false);
+    return bf ? launch_mt<false, true>(MT, maps, a, grid, st, false) : launch_mt<false, false>(MT, maps, a, grid, st, false);
 }
 
 /* This file's kernel error word (bounded waits that ran out); clear resets it. */
