@@ -31,6 +31,10 @@ sys.path.insert(0, str(ROOT))
 
 BS = 64
 ENC_BYTES_PER_W = 2 + 0.5 + 0.5 + 4 / 64        # 3.0625: BF16 in, hole + plug out, absmax out
+# DRAM read+write bytes per weight of encode_stream_kernel from one ncu capture of
+# `bench.py --profile encode` (4 x 14336x4096 tensors, one launch): 686.1 MB for
+# 234,881,024 weights; scaled to the bench's launches by their weights
+ENC_DRAM_BYTES_PER_W = 2.92
 EXP_BYTES_PER_W = 0.5 + 0.5 + 4 / 64 + 2        # 3.0625: planes + absmax in, BF16 out
 
 
@@ -190,10 +194,12 @@ def bench_glint(args):
     barrier(world)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("encode_timed")  # ncu --nvtx-include "encode_timed/" selects these launches
     t0.record()
     for k in range(args.steps):
         encode_step(ev[k])
     t1.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     clk = clocks.stop()
@@ -212,7 +218,9 @@ def bench_glint(args):
                    "weights_per_rank": weights, "blocksize": BS, "parallelism": f"per-tensor LPT x{world}, no collective",
                    "l2": "inputs (15 GB per rank) far larger than L2; no flush needed"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "traffic": round(weights / len(groups) * ENC_DRAM_BYTES_PER_W),
+                     "traffic_note": "DRAM bytes per launch: ncu bytes/weight of the profile case x mean weights per launch",
                      "peak_source": pk["source"], "bytes_per_weight": ENC_BYTES_PER_W},
         "clocks": clk,
         "gpu_launches": args.steps * len(groups),
@@ -228,10 +236,12 @@ def bench_glint(args):
         expand_step()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("expand_timed")
     a.record()
     for _ in range(args.steps):
         expand_step()
     b.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ems = max_over_ranks(world, a.elapsed_time(b)) / args.steps
     eg = weights * EXP_BYTES_PER_W / (ems / 1e3) / 1e9
@@ -247,7 +257,8 @@ def bench_glint(args):
 
     # ---- decode GEMV and prefill GEMM (per GPU)
     result["htile"] = bench_htile(args, pk)
-    result["gpu_launches"] += args.steps * len(groups)
+    # gpu_launches counts the headline's timed region (encode); the sub-results carry their own counts
+    result["expand"]["launches"] = args.steps * len(groups)
     barrier(world)
     if world > 1:
         import torch.distributed as dist
@@ -288,55 +299,76 @@ def e2e_encode(ws, args, world):
             "sample": f"{len(hosts)} tensors ({nbytes / 1e9:.2f} GB BF16) per rank"}
 
 
-def flush_l2(buf):
-    buf.add_(1)
+def graph_time_us(fn, n_launch: int, reps: int = 5) -> float:
+    """Median device time of one launch: `n_launch` calls captured back to back in
+    a CUDA graph (no host gaps inside the timed region), replayed `reps` times."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):  # first calls on the capture stream allocate its workspace
+        for i in range(n_launch):
+            fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n_launch):
+                fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3 / n_launch)
+    del g
+    return statistics.median(ts)
 
 
 def bench_htile(args, pk):
+    """Decode GEMV and prefill GEMM on one GPU, fast mode.
+    Every launch reads a different copy of the GLINT planes (4 copies for the
+    GEMV: 250 MB > L2, so each launch streams its weights from HBM; 2 for the
+    GEMM), and launches run back to back in a CUDA graph, so the numbers are
+    device time with no host gaps.  The decode kernel uses programmatic
+    dependent launch: in the graph a launch's weight stream starts while the
+    previous one drains, as in a decode step of consecutive linears."""
     import torch
     from glint_b200 import device as D
     res = {}
-    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2
     cases = [(m, 4096, 14336) for m in (1, 4, 16)] + [(m, 14336, 4096) for m in (1, 4, 16)]
     gemm = [(m, 4096, n) for m in (512, 2048, 8192) for n in (4096, 14336)]
     g = torch.Generator(device="cuda")
     g.manual_seed(7)
-    planes_cache = {}
-
-    def planes_for(N, K):
-        if (N, K) not in planes_cache:
-            w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
-            planes_cache[(N, K)] = D.encode(w, BS)
-        return planes_cache[(N, K)]
-
-    iters = 50
+    launches = 0
     for (M, K, N) in cases + gemm:
-        hole, plug, am = planes_for(N, K)
+        w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        base = D.encode(w, BS)
+        del w
+        ncopy = 4 if M <= 16 else 2
+        copies = [base] + [tuple(t.clone() for t in base) for _ in range(ncopy - 1)]
         x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
         y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-        mode = "fast"
-        for _ in range(3):
-            D.htile(x, hole, plug, am, N, BS, mode=mode, out=y)
-        times = []
-        for _ in range(iters if M <= 16 else 10):
-            flush_l2(flush)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            D.htile(x, hole, plug, am, N, BS, mode=mode, out=y)
-            b.record()
-            torch.cuda.synchronize()
-            times.append(a.elapsed_time(b))
-        t = statistics.median(times) / 1e3
-        flops = 2.0 * M * N * K
+        n_launch = 16 if M <= 16 else 6
+        t = graph_time_us(lambda i: D.htile(x, *copies[i % ncopy], N, BS, mode="fast", out=y), n_launch) / 1e6
+        launches += n_launch * (5 + 2)
         if M <= 16:
             byt = N * K * (1 + 4 / 64) + M * K * 2 + M * N * 4
             gbs = byt / t / 1e9
             res[f"gemv_m{M}_k{K}_n{N}"] = {"us": round(t * 1e6, 2), "hbm_gbs": round(gbs, 1),
-                                            "frac": round(gbs / pk["hbm_gbs"], 4), "mode": mode}
+                                            "frac": round(gbs / pk["hbm_gbs"], 4), "mode": "fast"}
         else:
-            tf = flops / t / 1e12
+            tf = 2.0 * M * N * K / t / 1e12
             res[f"gemm_m{M}_k{K}_n{N}"] = {"us": round(t * 1e6, 1), "tflops": round(tf, 1),
-                                            "frac": round(tf / pk["bf16_tflops"], 4), "mode": mode}
+                                            "frac": round(tf / pk["bf16_tflops"], 4), "mode": "fast"}
+        del copies, base, x, y
+    torch.cuda.empty_cache()
+    res["timing"] = ("CUDA graph of back-to-back launches over rotating plane copies; median of 5 replays; "
+                     "fractions of MEASURED_PEAKS hbm_gbs / bf16_tflops")
+    res["launches"] = launches
     return res
 
 
