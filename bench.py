@@ -105,7 +105,7 @@ def dist_init(args):
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
@@ -257,6 +257,8 @@ def bench_glint(args):
 
     # ---- decode GEMV and prefill GEMM (per GPU)
     result["htile"] = bench_htile(args, pk)
+    # ---- column-parallel decode of a 70B layer over the ranks (NCCL all-gathers when world > 1)
+    result["tp_decode"] = bench_tp_decode(args, world, rank, pk)
     # gpu_launches counts the headline's timed region (encode); the sub-results carry their own counts
     result["expand"]["launches"] = args.steps * len(groups)
     barrier(world)
@@ -370,6 +372,84 @@ def bench_htile(args, pk):
                      "fractions of MEASURED_PEAKS hbm_gbs / bf16_tflops")
     res["launches"] = launches
     return res
+
+
+def bench_tp_decode(args, world, rank, pk, M: int = 1):
+    """configs[4]-style decode step of one Llama-3-70B layer, column-parallel over
+    the ranks (glint_b200/tp.py): every rank holds 1/world of each linear's packed
+    rows and runs the decode kernel on them; all-gathers (NCCL) reassemble the
+    o_proj and down_proj inputs and outputs, the only places a consumer needs whole
+    rows (q/k/v and gate/up consumers work on their column shards).  The layer is
+    captured once in a CUDA graph (kernels and collectives), replayed, timed with
+    CUDA events, max over ranks; tokens/s assumes the 80 identical layers."""
+    import torch
+    from glint_b200 import device as D
+    from glint_b200 import shard as SH
+    from glint_b200 import tp
+    g = torch.Generator(device="cuda")
+    g.manual_seed(99 + rank)
+    lin = {nm: (N, K) for nm, N, K in SH.LLAMA3_70B_LAYER}
+    shards = {}
+    local_bytes = 0
+    for nm, (N, K) in lin.items():
+        n0, n1 = SH.column_shard(N, world, rank)
+        w = (torch.randn((n1 - n0) * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        h, p, a = D.encode(w, BS)
+        del w
+        shards[nm] = tp.ColumnShard(n0, n1, N, K, BS, h, p, a)
+        local_bytes += (n1 - n0) * K * (1 + 4 / 64)
+    x = torch.randn((M, 8192), generator=g, device="cuda").to(torch.bfloat16)
+    attn = torch.randn((M, 8192), generator=g, device="cuda").to(torch.bfloat16)
+    act_full = torch.randn((M, 28672), generator=g, device="cuda").to(torch.bfloat16)
+
+    def layer():
+        outs = []
+        for nm in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj"):
+            outs.append(tp.column_parallel(x, shards[nm], world, rank, gather=False))
+        # o_proj: gather its input shard (the attention output), then its output
+        o_in = tp.gather_columns(attn[:, shards["o_proj"].n0:shards["o_proj"].n1].float(), 8192, world, rank)
+        o = tp.column_parallel(o_in.to(torch.bfloat16), shards["o_proj"], world, rank)
+        # down_proj: gather the activation shard, then the output
+        n0, n1 = SH.column_shard(28672, world, rank)
+        d_in = tp.gather_columns(act_full[:, n0:n1].float(), 28672, world, rank)
+        d = tp.column_parallel(d_in.to(torch.bfloat16), shards["down_proj"], world, rank)
+        return outs, o, d
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            layer()
+    torch.cuda.synchronize()
+    barrier(world)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(gr, stream=s):
+            layer()
+    torch.cuda.synchronize()
+    barrier(world)
+    reps = 50
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        gr.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = max_over_ranks(world, a.elapsed_time(b) * 1e3 / reps)
+    barrier(world)
+    del gr  # graphs holding NCCL calls go before the process group does
+    torch.cuda.synchronize()
+    gathers = 4 if world > 1 else 0
+    return {"model": "Llama-3-70B layer (configs[4] shapes)", "tp": world, "batch": M,
+            "us_per_layer": round(us, 2), "tokens_per_s_80_layers": round(M / (80 * us * 1e-6), 1),
+            "weight_bytes_per_gpu_per_layer": int(local_bytes),
+            "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
+            "all_gathers_per_layer": gathers, "kernels_per_layer": 7,
+            "timing": "one layer in a CUDA graph (decode kernels + NCCL all-gathers), replayed; max over ranks"}
 
 
 # ------------------------------------------------------------------ CPU baselines
