@@ -95,7 +95,7 @@ struct DecodeArgs {
     const __nv_bfloat16 *x;
     void *y;
     float *ws;          /* partial sums: [row block][part][128][8*MT] */
-    int *counters;      /* per row block and consumer warp, zero between calls */
+    int *flags;         /* per row block, part and consumer warp: part published; zero between calls */
     int M, N, K;
     int KU;             /* units per row block (K / 256) */
     int64_t units;      /* row blocks * KU */
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             dst[r] = make_uint4(e, e, e, e);
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
-    /* y, the workspace and its counters are touched only after the previous kernel
+    /* y, the workspace and its flags are touched only after the previous kernel
      * in the stream is complete (no-op without programmatic dependent launch) */
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -230,88 +230,83 @@ __global__ void __launch_bounds__(kThreads, 1)
     int cur_rb = -1, seg_k0 = 0;
 
     /* Publish this warp's sums for its 16 rows of row block rb (k units [k0, k1) of
-     * the block): straight to y when this CTA covered the whole block, otherwise
-     * to the workspace.  A CTA has at most two such partial blocks (the first and
-     * the last of its range); their counters are bumped at the end, after one
-     * fence, so the stores never stall the stream: the last of a block's parts
-     * to arrive (a per row block and warp counter) adds the parts in k order and
-     * writes y. */
-    int pend_rb[2] = {-1, -1}, pend_parts[2] = {0, 0}, npend = 0;
+     * the block).  A whole block goes straight to y.  A block split between CTAs
+     * has a fixed owner, part 0: the CTA holding the block's first k unit, which
+     * reaches it at the end of its range.  Every other part is the first segment of
+     * its CTA's range (or the whole range): it stores its sums in the workspace and
+     * sets its flag with a release add that nothing waits for.  The owner waits for
+     * the flags (bounded; parts never wait on anything, so they complete as soon as
+     * their CTAs run), adds the parts to its own sums in k order (results do not
+     * depend on timing), resets the flags for the next call and writes y. */
     auto flush = [&](int rb, int k0, int k1) {
         constexpr int MP = 8 * MT;
-        const bool whole = k0 == 0 && k1 == a.KU;
-        const int64_t first = cta_of((int64_t)rb * a.KU, a.units, ctas);
-        const int part = whole ? 0 : (int)(blockIdx.x - first);
-        const int parts = whole ? 1 : (int)(cta_of((int64_t)rb * a.KU + a.KU - 1, a.units, ctas) - first + 1);
-        float *wsp = a.ws + ((int64_t)rb * a.max_parts) * kRows * MP;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int row = r0 + g + (q >> 1) * 8;
-                const int col = mt * 8 + 2 * t + (q & 1);
-                const int n = rb * kRows + row;
-                if (whole) {
-                    if (n < a.N && col < a.M) {
-                        if (BF16OUT)
-                            static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(acc[mt][q]);
-                        else
-                            static_cast<float *>(a.y)[(int64_t)col * a.N + n] = acc[mt][q];
-                    }
-                } else {
-                    wsp[((int64_t)part * kRows + row) * MP + col] = acc[mt][q];
-                }
-            }
-        }
-        if (whole)
-            return;
-        pend_rb[npend] = rb, pend_parts[npend] = parts, ++npend;
-    };
-    auto finish = [&]() {
-        constexpr int MP = 8 * MT;
-        if (npend == 0)
-            return;
-        __threadfence();
-        __syncwarp();
-        /* acquire-release count: the last arrival sees every part's stores (its
-         * lanes read them from L2 after the count) */
-        int prev[2] = {0, 0};
-        if (lane == 0)
-            for (int j = 0; j < npend; ++j)
-                asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                             : "=r"(prev[j])
-                             : "l"(&a.counters[pend_rb[j] * kConsumers + warp])
-                             : "memory");
-        for (int j = 0; j < npend; ++j) {
-        const int rb = pend_rb[j], parts = pend_parts[j];
-        float *wsp = a.ws + ((int64_t)rb * a.max_parts) * kRows * MP;
-        if (__shfl_sync(0xFFFFFFFFu, prev[j], 0) != parts - 1)
-            continue;
-#pragma unroll
-        for (int e = (int)lane; e < 16 * MP; e += 32) {
-            const int row = r0 + e / MP, col = e % MP;
-            /* parts in k order; eight loads in flight at a time */
-            float v = 0.f;
-            for (int p0 = 0; p0 < parts; p0 += 8) {
-                float t[8];
-#pragma unroll
-                for (int b = 0; b < 8; ++b)
-                    t[b] = p0 + b < parts ? __ldcg(wsp + ((int64_t)(p0 + b) * kRows + row) * MP + col) : 0.f;
-#pragma unroll
-                for (int b = 0; b < 8; ++b)
-                    if (p0 + b < parts)
-                        v += t[b];
-            }
-            const int n = rb * kRows + row;
+        auto put_y = [&](int n, int col, float v) {
             if (n < a.N && col < a.M) {
                 if (BF16OUT)
                     static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(v);
                 else
                     static_cast<float *>(a.y)[(int64_t)col * a.N + n] = v;
             }
+        };
+        if (k0 == 0 && k1 == a.KU) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    put_y(rb * kRows + r0 + g + (q >> 1) * 8, mt * 8 + 2 * t + (q & 1), acc[mt][q]);
+            return;
         }
-        if (lane == 0)
-            a.counters[rb * kConsumers + warp] = 0; /* ready for the next call */
+        const int64_t first = cta_of((int64_t)rb * a.KU, a.units, ctas);
+        const int part = (int)(blockIdx.x - first);
+        const int parts = (int)(cta_of((int64_t)rb * a.KU + a.KU - 1, a.units, ctas) - first + 1);
+        const float *wsp = a.ws + ((int64_t)rb * a.max_parts) * kRows * MP;
+        int *flg = a.flags + ((int64_t)rb * a.max_parts) * kConsumers + warp;
+        if (part != 0) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    __stcg(const_cast<float *>(wsp) + ((int64_t)part * kRows + r0 + g + (q >> 1) * 8) * MP + mt * 8 +
+                               2 * t + (q & 1),
+                           acc[mt][q]);
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(flg + part * kConsumers) : "memory");
+            return;
+        }
+        bool ok = true;
+        if (lane == 0) {
+            for (int pp = 1; pp < parts && ok; ++pp) {
+                int *f = flg + pp * kConsumers;
+                const long long t0 = clock64();
+                uint32_t v = 0;
+                while (true) {
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                    if (v)
+                        break;
+                    if (clock64() - t0 > kWaitCycles) {
+                        atomicOr(&g_decode_error, kErrTimeout);
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+                *f = 0; /* consumed: zero for the next call */
+            }
+        }
+        __syncwarp();
+        if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
+            return;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int row = r0 + g + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
+                float v = acc[mt][q];
+                for (int pp = 1; pp < parts; ++pp)
+                    v += __ldcg(wsp + ((int64_t)pp * kRows + row) * MP + col);
+                put_y(rb * kRows + row, col, v);
+            }
         }
     };
 
@@ -417,7 +412,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (cur_rb >= 0)
         flush(cur_rb, seg_k0, (int)(u1 - 1 - (int64_t)cur_rb * a.KU) + 1);
-    finish();
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder()
@@ -450,7 +444,7 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-/* Per (device, stream) scratch: partial sums and row-block counters. */
+/* Per (device, stream) scratch: partial sums and split-block flags. */
 struct Scratch {
     float *ws = nullptr;
     size_t ws_floats = 0;
@@ -502,7 +496,7 @@ struct Maps {
 /* Launched with programmatic stream serialisation (PDL): the kernel may start
  * while the previous kernel in the stream drains; it streams weights at once and
  * waits (griddepcontrol.wait) before reading activations or touching y and its
- * workspace.  `pdl` is off for the fixed-scratch entry, whose counters are reset
+ * workspace.  `pdl` is off for the fixed-scratch entry, whose flags are reset
  * by a memset just before the launch. */
 template <int MT, bool SPLIT, bool BF16OUT>
 int launch_t(const Maps &m, const DecodeArgs &a, int grid, cudaStream_t st, bool pdl)
@@ -584,10 +578,10 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
     const int64_t per_cta = std::max<int64_t>(1, a.units / grid);
     a.max_parts = (int)std::min<int64_t>(grid, (a.KU + per_cta - 1) / per_cta + 1);
     Scratch S;
-    if (!get_scratch(st, (size_t)rbs * a.max_parts * kRows * 8 * MT, (size_t)rbs * kConsumers, S))
+    if (!get_scratch(st, (size_t)rbs * a.max_parts * kRows * 8 * MT, (size_t)rbs * a.max_parts * kConsumers, S))
         return kLaunch;
     a.ws = S.ws;
-    a.counters = S.counters;
+    a.flags = S.counters;
     const bool bf = yk == kOutBF16;
     if (mode == kPrecise)
         return bf ? launch_mt<true, true>(MT, maps, a, grid, st, true) : launch_mt<true, false>(MT, maps, a, grid, st, true);
@@ -602,10 +596,10 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
  * can run on a fixed scratch area compiled into this file instead of the
  * per-stream workspace above: kNoAllocBytes per device, allocated with the
  * library's device image when it is loaded on a device and held until the
- * process exits.  The first kNoAllocCounterBytes hold the per (row block, warp)
- * counters, the rest the split-K partial sums. */
+ * process exits.  The first kNoAllocCounterBytes hold the per (row block, part,
+ * warp) split-block flags, the rest the split-K partial sums. */
 constexpr size_t kNoAllocBytes = size_t(4) << 20;   /* 4 MiB per device */
-constexpr size_t kNoAllocCounterBytes = 16 << 10;   /* 4096 counters: N <= 65536 */
+constexpr size_t kNoAllocCounterBytes = 64 << 10;   /* 16384 flags (row blocks x parts x warps) */
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 namespace {
@@ -647,17 +641,17 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
     const int grid = (int)std::min<int64_t>(a.units, sm_count());
     const int64_t per_cta = std::max<int64_t>(1, a.units / grid);
     a.max_parts = (int)std::min<int64_t>(grid, (a.KU + per_cta - 1) / per_cta + 1);
-    const size_t counter_bytes = (size_t)rbs * kConsumers * sizeof(int);
+    const size_t counter_bytes = (size_t)rbs * a.max_parts * kConsumers * sizeof(int);
     const size_t ws_bytes = (size_t)rbs * a.max_parts * kRows * 8 * MT * sizeof(float);
     if (counter_bytes > kNoAllocCounterBytes || ws_bytes > kNoAllocBytes - kNoAllocCounterBytes)
         return kScratch;
     Maps maps;
     if (!decode_maps(maps, hole, plug, am, x, M, N, K, MT))
         return kLaunch;
-    /* the array keeps the previous call's contents: the counters must start at 0 */
-    a.counters = static_cast<int *>(base);
+    /* the array keeps the previous call's contents: the flags must start at 0 */
+    a.flags = static_cast<int *>(base);
     a.ws = reinterpret_cast<float *>(static_cast<unsigned char *>(base) + kNoAllocCounterBytes);
-    if (cudaMemsetAsync(a.counters, 0, counter_bytes, st) != cudaSuccess)
+    if (cudaMemsetAsync(a.flags, 0, counter_bytes, st) != cudaSuccess)
         return kLaunch;
     const bool bf = yk == kOutBF16;
     if (mode == kPrecise)
