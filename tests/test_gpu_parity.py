@@ -425,9 +425,10 @@ def test_htile_matches_reference_library():
                                    (129, 264, 512), (640, 1000, 768), (2048, 384, 1024), (1100, 130, 2048),
                                    (256, 512, 4096), (384, 4608, 1280)])
 def test_htile_prefill_tcgen05_vs_oracle(M, N, K):
-    """Prefill shapes take the tcgen05 path in fast mode: within 1e-2 relative of the
-    f32 dequant-then-matmul oracle, f32 and BF16 y, ragged M and N edges, tiles
-    split between 1 to 16 CTA pairs, and bit-identical repeated calls."""
+    """Prefill shapes take the tcgen05 path: fast mode within 1e-2 relative of the f32
+    dequant-then-matmul oracle, precise mode (and the reference ABI) within 1e-5, f32 and
+    BF16 y, ragged M and N edges, tiles split between 1 to 16 CTA pairs, bit-identical
+    repeated calls."""
     from glint_b200 import glint_cuda
     L = glint_cuda.load()
     assert L.glint_kernel_error(1) == 0
@@ -446,6 +447,15 @@ def test_htile_prefill_tcgen05_vs_oracle(M, N, K):
     assert np.all(np.isfinite(yf))
     assert rel_err(yf, ref) <= FAST_TOL, rel_err(yf, ref)
     assert rel_err(yb, ref) <= FAST_TOL, rel_err(yb, ref)
+    # precise mode (hi + lo halves on the tensor cores) and the reference ABI, which is precise
+    yp = D().htile(dx, *dev, N, 64, mode="precise")
+    yp2 = D().htile(dx, *dev, N, 64, mode="precise")
+    yr = D().htile_reference_abi(dx, *dev, N, 64)
+    torch.cuda.synchronize()
+    assert L.glint_kernel_error(1) == 0
+    assert torch.equal(yp, yp2)
+    assert rel_err(yp.cpu().numpy(), ref) <= PRECISE_TOL, rel_err(yp.cpu().numpy(), ref)
+    assert rel_err(yr.cpu().numpy(), ref) <= PRECISE_TOL, rel_err(yr.cpu().numpy(), ref)
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 100, 256), (3, 1000, 512), (16, 4096, 14336), (17, 384, 2048), (32, 200, 4096),
