@@ -12,10 +12,11 @@
  *     register pressure; full/empty mbarriers hand the slots over;
  *   - a consumer lane owns 16 consecutive weights (two 16-byte shared loads), so
  *     a block of bs weights is bs/16 adjacent lanes and its absmax a shuffle-max
- *     over them.  The maximum is taken on |w|'s bits with packed 16-bit integer
- *     max, where NaN sorts above inf, so the same pass tells whether the block
- *     holds a NaN; such blocks recompute absmax with fmaxf, which skips NaN as
- *     the reference's `a > m` does;
+ *     over them.  The maximum is taken with the packed BF16 max of absolute
+ *     values that propagates NaN (for f32 input: integer max of |w|'s bits, where
+ *     NaN sorts above inf), so the same pass tells whether the block holds a NaN;
+ *     such blocks recompute absmax with fmaxf, which skips NaN as the reference's
+ *     `a > m` does;
  *   - v = RN(w / s) comes from one correctly rounded reciprocal per block and
  *     Markstein's correction per weight (glint_codec.cuh), evaluated two weights
  *     per instruction with the f32x2 forms; blocks with a NaN, with s == 0 or
@@ -36,7 +37,10 @@
  * two-kernel path, which follows the reference's structure (absmax, then one
  * thread per output byte) with the same arithmetic.
  */
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -57,7 +61,11 @@ constexpr int kSlots = 3;
 constexpr int kWpl = 32;                                                /* weights per consumer lane */
 
 
+
 struct EncodeBatch {
+    /* BF16 inputs viewed as rows of 32 weights (64 B) for 2-D TMA with the 64-byte
+     * swizzle; used for the full units of the items in `tma` */
+    CUtensorMap wmap[kMaxItems];
     const void *w[kMaxItems];
     uint8_t *hole[kMaxItems];
     uint8_t *plug[kMaxItems];
@@ -65,6 +73,7 @@ struct EncodeBatch {
     int64_t n[kMaxItems];
     int64_t unit_end[kMaxItems]; /* inclusive prefix sum of ceil(n / unit weights) */
     uint32_t direct;             /* bit i: item i is read straight from global (input not 16-B aligned) */
+    uint32_t tma;                /* bit i: item i's full units are staged through wmap[i] */
     int count;
 };
 
@@ -76,7 +85,9 @@ constexpr int consumer_warps() { return unit_w<In>() / (32 * kWpl); }
 template <typename In>
 constexpr int enc_threads() { return (consumer_warps<In>() + 1) * 32; }
 constexpr int kMetaBytes = 48;
-constexpr int kEncSmem = kLutBytes + kSlots * kSlotBytes + kSlots * kMetaBytes + 2 * 8 * kSlots + 128;
+constexpr int kRingOff = (kLutBytes + 1023) / 1024 * 1024; /* the ring starts on a 1 KB boundary (TMA swizzle) */
+constexpr int kEncSmem = kRingOff + kSlots * kSlotBytes + kSlots * kMetaBytes + 2 * 8 * kSlots + 128;
+constexpr int kTmaRows = 256; /* rows of 32 BF16 weights per TMA box: 16 KB, 3 boxes per unit */
 
 /* What the producer tells the consumers about the unit in a slot: pointers already
  * offset to the unit's first element, how many weights it holds, and whether its
@@ -88,7 +99,8 @@ struct UnitMeta {
     float *absmax;
     int valid;
     int staged;
-    int pad[2];
+    int swz; /* staged through TMA with the 64-byte swizzle (else a linear bulk copy) */
+    int pad;
 };
 static_assert(sizeof(UnitMeta) == kMetaBytes, "slot descriptor layout");
 
@@ -118,28 +130,30 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
     return d;
 }
-__device__ __forceinline__ uint32_t umax16x2(uint32_t a, uint32_t b)
-{
-    uint32_t d;
-    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
 
 /* 16 weights of one lane as f32, and the lane's |w| bit maximum (NaN above inf) */
 struct Lane16 {
     float w[16];
     uint32_t mag; /* max over the lane of |w| as an order-preserving integer */
 };
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t a, uint32_t b)
+{
+    uint32_t d; /* per half: max(|a|, |b|) (sign = xor, ignored), NaN if either is NaN */
+    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
 __device__ __forceinline__ void from_words(const uint16_t *, const uint32_t (&u)[8], Lane16 &L)
 {
+    /* BF16 max on |w| with NaN propagation: one instruction per two weights; a NaN
+     * comes out as the canonical 0x7FFF, which as f32 bits sorts above inf */
     uint32_t m = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         L.w[2 * i] = __uint_as_float(u[i] << 16);
         L.w[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
-        m = umax16x2(m, u[i] & 0x7FFF7FFFu);
+        m = absmax_bf16x2(m, u[i]);
     }
-    L.mag = max(m & 0xFFFFu, m >> 16) << 16; /* as f32 bits */
+    L.mag = (absmax_bf16x2(m, m >> 16) & 0x7FFFu) << 16; /* as f32 bits */
 }
 __device__ __forceinline__ void from_words(const float *, const uint32_t (&u)[16], Lane16 &L)
 {
@@ -266,7 +280,7 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
     constexpr int G = BS_LOG2 >= 5 ? (1 << BS_LOG2) / kWpl : 1;
     extern __shared__ __align__(128) uint8_t smem[];
     uint2 *lut = reinterpret_cast<uint2 *>(smem);
-    uint8_t *ring = smem + kLutBytes;
+    uint8_t *ring = smem + kRingOff;
     UnitMeta *meta = reinterpret_cast<UnitMeta *>(ring + kSlots * kSlotBytes);
     uint64_t *full = reinterpret_cast<uint64_t *>(meta + kSlots);
     uint64_t *empty = full + kSlots;
@@ -309,7 +323,18 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
                 m.absmax = b.absmax[it] + (off >> BS_LOG2);
                 m.valid = left >= UW ? UW : (int)left;
                 m.staged = staged ? 1 : 0;
-                if (staged) {
+                m.swz = staged && sizeof(In) == 2 && ((b.tma >> it) & 1u) ? 1 : 0;
+                if (m.swz) {
+                    /* three boxes of 256 rows x 64 B, each 16-byte chunk c of row r landing at
+                     * chunk c ^ ((r >> 1) & 3): a quarter-warp's 16-byte reads of eight rows
+                     * then cover all 32 banks */
+                    mbar_expect_tx(&full[s], kSlotBytes);
+                    const int row0 = (int)(off / 32);
+#pragma unroll
+                    for (int bx = 0; bx < kSlotBytes / (kTmaRows * 64); ++bx)
+                        tma_load_2d(ring + s * kSlotBytes + bx * kTmaRows * 64, &b.wmap[it], &full[s], 0,
+                                    row0 + bx * kTmaRows);
+                } else if (staged) {
                     mbar_expect_tx(&full[s], kSlotBytes);
                     bulk_g2s(ring + s * kSlotBytes, m.src, kSlotBytes, &full[s]);
                 } else {
@@ -341,7 +366,20 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
         const int valid = m.valid - rel >= kWpl ? kWpl : (m.valid - rel > 0 ? m.valid - rel : 0);
         const In *src = static_cast<const In *>(m.src);
         uint32_t wa[Words<In>::N], wb[Words<In>::N];
-        if (m.staged) {
+        if (m.swz) {
+            /* row rel/32 of the slot, chunk j at j ^ ((row >> 1) & 3) (BF16 only) */
+            const uint32_t row = (uint32_t)rel / 32u, sw = (row >> 1) & 3u;
+            const uint32_t a = saddr(ring + s * kSlotBytes) + row * 64u;
+            uint32_t q[16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint4 v = lds128(a + (((uint32_t)j ^ sw) << 4));
+                q[4 * j] = v.x, q[4 * j + 1] = v.y, q[4 * j + 2] = v.z, q[4 * j + 3] = v.w;
+            }
+#pragma unroll
+            for (int j = 0; j < Words<In>::N; ++j)
+                wa[j] = q[j], wb[j] = q[j + Words<In>::N];
+        } else if (m.staged) {
             const uint32_t a = saddr(ring + s * kSlotBytes) + rel * (int)sizeof(In);
             smem_words(src, a, wa);
             smem_words(src, a + 16 * (int)sizeof(In), wb);
@@ -501,6 +539,38 @@ int launch_fast(const EncodeBatch &b, int bs_log2, cudaStream_t st)
     }
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+/* BF16 tensor of n weights as [n / 32 rows][32] for 64-byte-swizzled TMA boxes of
+ * 256 rows; false when the driver entry point is missing or the map is refused */
+bool bf16_row_map(CUtensorMap *m, const void *w, int64_t n)
+{
+    auto enc = tensor_map_encoder();
+    if (!enc || n < 32)
+        return false;
+    cuuint64_t dims[2] = {32, (cuuint64_t)(n / 32)};
+    cuuint64_t strides[1] = {64};
+    cuuint32_t box[2] = {32, kTmaRows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int log2_if_pow2(int bs)
 {
     for (int l = 0; l < 31; ++l)
@@ -547,6 +617,8 @@ int encode_launch(const EncodeJob *jobs, int count, int bs, bool f32_in, cudaStr
         b.unit_end[k] = (k ? b.unit_end[k - 1] : 0) + (j.n + uw - 1) / uw;
         if (!aligned_to(j.w, 16))
             b.direct |= 1u << k;
+        else if (!f32_in && j.n >= uw && bf16_row_map(&b.wmap[k], j.w, j.n))
+            b.tma |= 1u << k;
         b.count = k + 1;
         if (b.count == kMaxItems)
             rc = flush();
