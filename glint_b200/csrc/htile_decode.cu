@@ -115,6 +115,89 @@ __device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t ctas
     return c;
 }
 
+/* One 64-k absmax block of a 16-row weight tile against the activations:
+ * acc[mt] += absmax * (W[rows r0+g, r0+g+8][block] . x[mt*8+g'][block]).
+ * `hole`/`plug`: plane tiles with ROWB-byte rows (128: 128B swizzle, 16-byte chunk j
+ * of row r at j ^ (r & 7); 64: 64B swizzle, j ^ ((r >> 1) & 3)), the block at byte
+ * 32*c of a row; `am`: absmax rows of 16 bytes, this block in column am_col; `xbox`:
+ * the block's activation box, 8*MT rows x 128 B, 128B swizzle.  Swap-AB
+ * mma.sync.m16n8k16: weights are the A operand (lane (g, t) holds rows g and g+8),
+ * activations the B operand read with the same k map, so the dot product is exact
+ * whatever the k order; hi (and lo in precise mode) BF16 halves of the codebook. */
+template <int MT, bool SPLIT, int ROWB>
+__device__ __forceinline__ void tile_block(uint32_t hole, uint32_t plug, uint32_t am, uint32_t am_col, uint32_t xbox,
+                                           int c, int r0, int g, int t, uint32_t lut_base, uint32_t lane4,
+                                           float (&acc)[MT][4])
+{
+    uint32_t E[2][2], O[2][2];
+    float sc[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int row = r0 + g + 8 * r;
+        const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(ROWB == 128 ? (row & 7) : ((row >> 1) & 3));
+        const uint32_t off = (uint32_t)row * (uint32_t)ROWB + (chunk << 4) + (uint32_t)(t & 1) * 8u;
+        const uint2 hw = lds64(hole + off), pw = lds64(plug + off);
+        const uint32_t hv[2] = {hw.x, hw.y}, pv[2] = {pw.x, pw.y};
+#pragma unroll
+        for (int wd = 0; wd < 2; ++wd) {
+            E[r][wd] = ((hv[wd] << 4) & 0xF0F0F0F0u) | (pv[wd] & 0x0F0F0F0Fu);
+            O[r][wd] = (hv[wd] & 0xF0F0F0F0u) | ((pv[wd] >> 4) & 0x0F0F0F0Fu);
+        }
+        sc[r] = __uint_as_float(lds32(am + (uint32_t)row * 16u + am_col * 4u));
+    }
+    /* x fragments: row m = mt*8 + g of the box, 16 consecutive k at 32*t bytes
+     * (16-byte chunks 2t and 2t+1, 128B swizzle: chunk ^ (m & 7)) */
+    uint4 xb[MT][2];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        const uint32_t rowb = xbox + (uint32_t)(mt * 8 + g) * 128u;
+        xb[mt][0] = lds128(rowb + ((uint32_t)((2 * t) ^ g) << 4));
+        xb[mt][1] = lds128(rowb + ((uint32_t)((2 * t + 1) ^ g) << 4));
+    }
+    /* two accumulators (even and odd MMA steps) keep the chains independent */
+    float part[2][MT][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+            part[h][mt][0] = part[h][mt][1] = part[h][mt][2] = part[h][mt][3] = 0.f;
+#pragma unroll
+    for (int st = 0; st < 4; ++st) {
+        const int wd = st >> 1, b0 = (st & 1) * 2;
+        uint32_t e[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            /* address = (code << 8) | (lane << 2): byte b0 or b0+1 of E / O into byte 1 */
+            e[r][0] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | (b0 << 4)));
+            e[r][1] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | (b0 << 4)));
+            e[r][2] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
+            e[r][3] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
+        }
+        const uint32_t ahi[4] = {__byte_perm(e[0][0], e[0][1], 0x5410), __byte_perm(e[1][0], e[1][1], 0x5410),
+                                 __byte_perm(e[0][2], e[0][3], 0x5410), __byte_perm(e[1][2], e[1][3], 0x5410)};
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
+            mma_bf16_16816(part[st & 1][mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+        }
+        if (SPLIT) {
+            const uint32_t alo[4] = {__byte_perm(e[0][0], e[0][1], 0x7632), __byte_perm(e[1][0], e[1][1], 0x7632),
+                                     __byte_perm(e[0][2], e[0][3], 0x7632), __byte_perm(e[1][2], e[1][3], 0x7632)};
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
+                mma_bf16_16816(part[st & 1][mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            acc[mt][q] = fmaf(sc[q >> 1], part[0][mt][q] + part[1][mt][q], acc[mt][q]);
+    }
+}
+
 template <int MT, bool SPLIT, bool BF16OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     htile_decode_kernel(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap pmap,
@@ -333,85 +416,234 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t xs = slot + 2 * kPlaneTile + kAmTile;
         const uint32_t am_col = kKU == 256 ? 0u : (uint32_t)(ku & 1) * 2;
 #pragma unroll
-        for (int c = 0; c < kKU / 64; ++c) {
-            /* packed nibbles of rows g and g+8: 8 bytes at k-byte c*32 + t*8 of the
-             * row's kKU/2 bytes (16-byte chunk j sits at j ^ (row & 7) with the 128B
-             * swizzle, at j ^ ((row >> 1) & 3) with the 64B one) */
-            uint32_t E[2][2], O[2][2];
-            float sc[2];
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int row = r0 + g + 8 * r;
-                const uint32_t chunk =
-                    (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(kKU == 256 ? (row & 7) : ((row >> 1) & 3));
-                const uint32_t off = (uint32_t)row * (uint32_t)(kKU / 2) + (chunk << 4) + (uint32_t)(t & 1) * 8u;
-                const uint2 hw = lds64(slot + off), pw = lds64(slot + kPlaneTile + off);
-                const uint32_t hv[2] = {hw.x, hw.y}, pv[2] = {pw.x, pw.y};
-#pragma unroll
-                for (int wd = 0; wd < 2; ++wd) {
-                    E[r][wd] = ((hv[wd] << 4) & 0xF0F0F0F0u) | (pv[wd] & 0x0F0F0F0Fu);
-                    O[r][wd] = (hv[wd] & 0xF0F0F0F0u) | ((pv[wd] >> 4) & 0x0F0F0F0Fu);
-                }
-                sc[r] = __uint_as_float(lds32(slot + 2 * kPlaneTile + (uint32_t)row * 16u + (am_col + c) * 4u));
-            }
-            /* x fragments: row m = mt*8 + g of the 64-k box c, 16 consecutive k at 32*t bytes
-             * (16-byte chunks 2t and 2t+1, 128B swizzle: chunk ^ (m & 7)) */
-            uint4 xb[MT][2];
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                const uint32_t rowb = xs + (uint32_t)c * (8 * MT * 128) + (uint32_t)(mt * 8 + g) * 128u;
-                xb[mt][0] = lds128(rowb + ((uint32_t)((2 * t) ^ g) << 4));
-                xb[mt][1] = lds128(rowb + ((uint32_t)((2 * t + 1) ^ g) << 4));
-            }
-            /* two accumulators (even and odd MMA steps) keep the chains independent */
-            float part[2][MT][4];
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-                    part[h][mt][0] = part[h][mt][1] = part[h][mt][2] = part[h][mt][3] = 0.f;
-#pragma unroll
-            for (int st = 0; st < 4; ++st) {
-                const int wd = st >> 1, b0 = (st & 1) * 2;
-                uint32_t e[2][4];
-#pragma unroll
-                for (int r = 0; r < 2; ++r) {
-                    /* address = (code << 8) | (lane << 2): byte b0 or b0+1 of E / O into byte 1 */
-                    e[r][0] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | (b0 << 4)));
-                    e[r][1] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | (b0 << 4)));
-                    e[r][2] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
-                    e[r][3] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
-                }
-                const uint32_t ahi[4] = {__byte_perm(e[0][0], e[0][1], 0x5410), __byte_perm(e[1][0], e[1][1], 0x5410),
-                                         __byte_perm(e[0][2], e[0][3], 0x5410), __byte_perm(e[1][2], e[1][3], 0x5410)};
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-                    mma_bf16_16816(part[st & 1][mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
-                }
-                if (SPLIT) {
-                    const uint32_t alo[4] = {__byte_perm(e[0][0], e[0][1], 0x7632), __byte_perm(e[1][0], e[1][1], 0x7632),
-                                             __byte_perm(e[0][2], e[0][3], 0x7632), __byte_perm(e[1][2], e[1][3], 0x7632)};
-#pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-                        mma_bf16_16816(part[st & 1][mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
-                    }
-                }
-            }
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    acc[mt][q] = fmaf(sc[q >> 1], part[0][mt][q] + part[1][mt][q], acc[mt][q]);
-            }
-        }
+        for (int c = 0; c < kKU / 64; ++c)
+            tile_block<MT, SPLIT, kKU / 2>(slot, slot + kPlaneTile, slot + 2 * kPlaneTile, am_col + c,
+                                           xs + (uint32_t)c * (8 * MT * 128), c, r0, g, t, lut_base, lane4, acc);
         __syncwarp();
         if (lane == 0)
             mbar_arrive(&empty[s]);
     }
     if (cur_rb >= 0)
         flush(cur_rb, seg_k0, (int)(u1 - 1 - (int64_t)cur_rb * a.KU) + 1);
+}
+
+/* ---- row-owned decode for wide layers ------------------------------------------
+ * When every SM can own at least 16 rows (N >= 16 x SMs), CTA c takes the rows
+ * [c*R, (c+1)*R), R = ceil(N / ctas), over the whole K, so no row is split between
+ * CTAs: no workspace, no cross-CTA sums, and the per-SM work differs by at most
+ * one row.  Its rows go in row blocks of RB <= 112 (7 tiles of 16); the units are
+ * (row block, 256 k): hole and plug tiles [RB rows x 128 B] (128B swizzle), an
+ * absmax box [RB rows x 4 blocks] and the activation slice, through a TMA ring.
+ * Consumer warp w works on tile w / KH and a KH-th of every unit's four 64-k
+ * blocks; at the end of a row block the KH partial sums of a tile are added in k
+ * order through shared memory (bounded mbarrier handshakes) and written to y. */
+constexpr int kRowBlockMax = 112;
+constexpr int kRPlane = kRowBlockMax * 128; /* 14 KB per plane tile */
+constexpr int kRAm = 2048;                  /* absmax box, >= 112 rows x 16 B */
+template <int MT>
+constexpr int r_xtile() { return 4 * 8 * MT * 128; }
+template <int MT>
+constexpr int r_stage() { return 2 * kRPlane + kRAm + r_xtile<MT>(); }
+template <int MT>
+constexpr int r_stages() { return MT == 1 ? 4 : 3; }
+/* partial sums exchanged at a row block's end: T * (KH - 1) <= 12 warps x 32 lanes */
+template <int MT>
+constexpr int r_scratch_floats() { return (MT <= 2 ? 12 : 7) * 32 * 4 * MT; }
+template <int MT>
+constexpr int r_smem_bytes()
+{
+    return kLutBytes + 1024 + r_stages<MT>() * r_stage<MT>() + r_scratch_floats<MT>() * 4 + 8 * (2 * r_stages<MT>() + 2) +
+           64;
+}
+
+struct RowArgs {
+    void *y;
+    int M, N, K;
+    int KU; /* 256-k units per row */
+    int R;  /* rows per CTA */
+    int nb; /* row blocks per CTA */
+    int RB; /* rows per row block (the TMA box height) */
+    int T;  /* 16-row tiles per row block */
+    int KH; /* consumer warps per tile (each a KH-th of a unit's k) */
+};
+
+template <int MT, bool SPLIT, bool BF16OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    htile_rows_kernel(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap pmap,
+                      const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap xmap, const RowArgs a)
+{
+    constexpr int S = r_stages<MT>();
+    constexpr int kStage = r_stage<MT>();
+    static_assert(r_smem_bytes<MT>() <= 232448, "shared memory");
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint32_t *lut = reinterpret_cast<uint32_t *>(smem_raw);
+    uint8_t *ring = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) & ~uintptr_t(1023));
+    float *scratch = reinterpret_cast<float *>(ring + S * kStage);
+    uint64_t *full = reinterpret_cast<uint64_t *>(scratch + r_scratch_floats<MT>());
+    uint64_t *empty = full + S;
+    uint64_t *cmb_full = empty + S;  /* a row block's KH-1 partials per tile are in scratch */
+    uint64_t *cmb_empty = cmb_full + 1; /* the tile owners have read them */
+
+    const int active = a.T * a.KH;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], active);
+        }
+        mbar_init(cmb_full, a.KH > 1 ? a.T * (a.KH - 1) : 1);
+        mbar_init(cmb_empty, a.T);
+        mbar_init_fence();
+    }
+    if (threadIdx.x == kConsumers * 32) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&hmap) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&pmap) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&amap) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5;
+    const uint32_t lane = lane_id();
+    const int n_begin = blockIdx.x * a.R, n_end = min(a.N, n_begin + a.R);
+    const int units = a.nb * a.KU;
+    const uint32_t box_bytes = (uint32_t)(2 * a.RB * 128 + a.RB * 16 + r_xtile<MT>());
+
+    if (warp == kConsumers) {
+        if (lane == 0) {
+            auto load_x = [&](int u, int s) {
+                const int ku = u % a.KU;
+                uint8_t *st = ring + s * kStage + 2 * kRPlane + kRAm;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tma_load_2d(st + c * (8 * MT * 128), &xmap, &full[s], ku * 256 + c * 64, 0);
+            };
+            bool ok = true;
+            int i = 0;
+            for (; i < units; ++i) {
+                const int s = i % S;
+                const uint32_t ph = (uint32_t)(i / S) & 1u;
+                if (i >= S && !(ok = mbar_wait_suspend_bounded(&empty[s], ph ^ 1u, &g_decode_error)))
+                    break;
+                const int blk = i / a.KU, ku = i % a.KU;
+                const int nb0 = n_begin + blk * a.RB;
+                uint8_t *st = ring + s * kStage;
+                mbar_expect_tx(&full[s], box_bytes);
+                tma_load_2d(st, &hmap, &full[s], ku * 128, nb0);
+                tma_load_2d(st + kRPlane, &pmap, &full[s], ku * 128, nb0);
+                tma_load_2d(st + 2 * kRPlane, &amap, &full[s], ku * 4, nb0);
+                if (i >= S) {
+                    load_x(i, s);
+                } else if (i == S - 1 || i == units - 1) {
+                    /* weights stream before the previous kernel is done, activations after
+                     * (programmatic dependent launch; a no-op otherwise) */
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    for (int j = 0; j <= i; ++j)
+                        load_x(j, j);
+                }
+            }
+            asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+            if (!ok) {
+                for (int j = i > S ? i - S : 0; j < i; ++j)
+                    if (!mbar_wait_bounded(&full[j % S], (uint32_t)(j / S) & 1u, &g_decode_error))
+                        break;
+            }
+        }
+        return;
+    }
+
+    if (threadIdx.x < 256) {
+        const uint32_t e = split_pair(g_cells[threadIdx.x >> 4][threadIdx.x & 15]);
+        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 64);
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            dst[r] = make_uint4(e, e, e, e);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (warp >= active)
+        return;
+
+    /* warp kh takes blocks [kh*4/KH, (kh+1)*4/KH) of each unit */
+    const int tile = warp / a.KH, kh = warp % a.KH, nblk = 4 / a.KH, c0 = kh * nblk;
+    const int g = (int)(lane >> 2), t = (int)(lane & 3), r0 = tile * 16;
+    const uint32_t lut_base = saddr(lut), lane4 = lane * 4u;
+    float acc[MT][4];
+    bool alive = true;
+    int i = 0;
+    for (int blk = 0; blk < a.nb && alive; ++blk) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+            acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+        for (int ku = 0; ku < a.KU; ++ku, ++i) {
+            const int s = i % S;
+            const uint32_t ph = (uint32_t)(i / S) & 1u;
+            bool ok = lane == 0 ? mbar_wait_suspend_bounded(&full[s], ph, &g_decode_error) : true;
+            if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0)) {
+                alive = false;
+                break;
+            }
+            const uint32_t st = saddr(ring + s * kStage);
+            for (int c = c0; c < c0 + nblk; ++c)
+                tile_block<MT, SPLIT, 128>(st, st + kRPlane, st + 2 * kRPlane, (uint32_t)c,
+                                           st + 2 * kRPlane + kRAm + (uint32_t)c * (8 * MT * 128), c, r0, g, t,
+                                           lut_base, lane4, acc);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&empty[s]);
+        }
+        if (!alive)
+            break;
+        /* add the tile's KH partial sums in k order (kh 0, 1, ...), then y */
+        if (a.KH > 1) {
+            if (kh > 0) {
+                bool ok = true;
+                if (blk > 0 && lane == 0)
+                    ok = mbar_wait_suspend_bounded(cmb_empty, (uint32_t)(blk - 1) & 1u, &g_decode_error);
+                if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
+                    break;
+                float *dst = scratch + ((tile * (a.KH - 1) + kh - 1) * 32 + (int)lane) * 4 * MT;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        dst[mt * 4 + q] = acc[mt][q];
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(cmb_full);
+                continue;
+            }
+            bool ok = lane == 0 ? mbar_wait_suspend_bounded(cmb_full, (uint32_t)blk & 1u, &g_decode_error) : true;
+            if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
+                break;
+            for (int kk = 1; kk < a.KH; ++kk) {
+                const float *src = scratch + ((tile * (a.KH - 1) + kk - 1) * 32 + (int)lane) * 4 * MT;
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        acc[mt][q] += src[mt * 4 + q];
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(cmb_empty);
+        }
+        const int nb0 = n_begin + blk * a.RB;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int row = r0 + g + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
+                const int n = nb0 + row;
+                if (row < a.RB && n < n_end && col < a.M) {
+                    if (BF16OUT)
+                        static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(acc[mt][q]);
+                    else
+                        static_cast<float *>(a.y)[(int64_t)col * a.N + n] = acc[mt][q];
+                }
+            }
+        }
+    }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder()
@@ -531,6 +763,75 @@ int launch_mt(int MT, const Maps &m, const DecodeArgs &a, int grid, cudaStream_t
     return launch_t<4, SPLIT, BF16OUT>(m, a, grid, st, pdl);
 }
 
+template <int MT, bool SPLIT, bool BF16OUT>
+int launch_rows_t(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bool pdl)
+{
+    auto kern = htile_rows_kernel<MT, SPLIT, BF16OUT>;
+    if (!ensure_smem((const void *)kern, r_smem_bytes<MT>()))
+        return kLaunch;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = r_smem_bytes<MT>();
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, m.h, m.p, m.am, m.x, a) != cudaSuccess) {
+        cudaGetLastError();
+        return kLaunch;
+    }
+    return kOk;
+}
+
+/* the row-owned kernel for N >= 16 x SMs: no workspace, no split rows */
+int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st, bool pdl)
+{
+    const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+    const int sms = sm_count();
+    const int g0 = std::max(1, std::min(sms, (N + 15) / 16));
+    RowArgs a{};
+    a.y = y, a.M = M, a.N = N, a.K = K, a.KU = K / 256;
+    a.R = (N + g0 - 1) / g0;
+    const int grid = (N + a.R - 1) / a.R;
+    a.nb = (a.R + kRowBlockMax - 1) / kRowBlockMax;
+    a.RB = (a.R + a.nb - 1) / a.nb;
+    a.T = (a.RB + 15) / 16;
+    const int khmax = MT <= 2 ? 4 : 2;
+    a.KH = 1;
+    while (a.KH * 2 <= khmax && a.T * a.KH * 2 <= kConsumers)
+        a.KH *= 2;
+    Maps maps;
+    if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
+                  (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
+                  (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
+                  4, (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
+                  (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B))
+        return kLaunch;
+    const bool bf = yk == kOutBF16, pr = mode == kPrecise;
+#define GLINT_ROWS_CASE(mt)                                                                                            \
+    if (MT == mt)                                                                                                      \
+        return pr ? (bf ? launch_rows_t<mt, true, true>(maps, a, grid, st, pdl)                                         \
+                        : launch_rows_t<mt, true, false>(maps, a, grid, st, pdl))                                       \
+                  : (bf ? launch_rows_t<mt, false, true>(maps, a, grid, st, pdl)                                        \
+                        : launch_rows_t<mt, false, false>(maps, a, grid, st, pdl));
+    GLINT_ROWS_CASE(1)
+    GLINT_ROWS_CASE(2)
+    GLINT_ROWS_CASE(4)
+#undef GLINT_ROWS_CASE
+    return kLaunch;
+}
+
+/* wide enough for every SM to own >= 16 rows, and narrow enough for <= 2 row
+ * blocks per CTA (beyond that stream-K keeps more warps busy) */
+bool rows_supported(int N) { return N >= 16 * sm_count() && N <= 2 * kRowBlockMax * sm_count(); }
+
 } // namespace
 
 bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
@@ -560,6 +861,8 @@ bool decode_maps(Maps &maps, const uint8_t *hole, const uint8_t *plug, const flo
 int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
                         OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
 {
+    if (rows_supported(N))
+        return launch_rows(hole, plug, am, x, y, yk, M, N, K, mode, st, true);
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
     Maps maps;
     if (!decode_maps(maps, hole, plug, am, x, M, N, K, MT))
@@ -600,6 +903,7 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
  * warp) split-block flags, the rest the split-K partial sums. */
 constexpr size_t kNoAllocBytes = size_t(4) << 20;   /* 4 MiB per device */
 constexpr size_t kNoAllocCounterBytes = 64 << 10;   /* 16384 flags (row blocks x parts x warps) */
+constexpr int kNoAllocMaxN = 65536;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 namespace {
@@ -610,6 +914,11 @@ void *g_noalloc_addr[64] = {};
 int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
                                 void *y, OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
 {
+    /* the documented limit of this entry point, whichever kernel runs */
+    if (N > kNoAllocMaxN)
+        return kScratch;
+    if (rows_supported(N)) /* needs no scratch at all */
+        return launch_rows(hole, plug, am, x, y, yk, M, N, K, mode, st, false);
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return kLaunch;
