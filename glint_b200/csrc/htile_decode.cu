@@ -123,10 +123,12 @@ __device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t ctas
  * the block's activation box, 8*MT rows x 128 B, 128B swizzle.  Swap-AB
  * mma.sync.m16n8k16: weights are the A operand (lane (g, t) holds rows g and g+8),
  * activations the B operand read with the same k map, so the dot product is exact
- * whatever the k order; hi (and lo in precise mode) BF16 halves of the codebook. */
+ * whatever the k order; hi (and lo in precise mode) BF16 halves of the codebook.
+ * Lanes whose activation row mt*8+g is >= M (rows the TMA box fills with zeros)
+ * take zeros without reading shared memory. */
 template <int MT, bool SPLIT, int ROWB>
 __device__ __forceinline__ void tile_block(uint32_t hole, uint32_t plug, uint32_t am, uint32_t am_col, uint32_t xbox,
-                                           int c, int r0, int g, int t, uint32_t lut_base, uint32_t lane4,
+                                           int c, int r0, int g, int t, uint32_t lut_base, uint32_t lane4, int M,
                                            float (&acc)[MT][4])
 {
     uint32_t E[2][2], O[2][2];
@@ -151,8 +153,9 @@ __device__ __forceinline__ void tile_block(uint32_t hole, uint32_t plug, uint32_
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
         const uint32_t rowb = xbox + (uint32_t)(mt * 8 + g) * 128u;
-        xb[mt][0] = lds128(rowb + ((uint32_t)((2 * t) ^ g) << 4));
-        xb[mt][1] = lds128(rowb + ((uint32_t)((2 * t + 1) ^ g) << 4));
+        const bool live = mt * 8 + g < M;
+        xb[mt][0] = lds128_if(rowb + ((uint32_t)((2 * t) ^ g) << 4), live);
+        xb[mt][1] = lds128_if(rowb + ((uint32_t)((2 * t + 1) ^ g) << 4), live);
     }
     /* two accumulators (even and odd MMA steps) keep the chains independent */
     float part[2][MT][4];
@@ -418,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < kKU / 64; ++c)
             tile_block<MT, SPLIT, kKU / 2>(slot, slot + kPlaneTile, slot + 2 * kPlaneTile, am_col + c,
-                                           xs + (uint32_t)c * (8 * MT * 128), c, r0, g, t, lut_base, lane4, acc);
+                                           xs + (uint32_t)c * (8 * MT * 128), c, r0, g, t, lut_base, lane4, a.M, acc);
         __syncwarp();
         if (lane == 0)
             mbar_arrive(&empty[s]);
@@ -587,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = c0; c < c0 + nblk; ++c)
                 tile_block<MT, SPLIT, 128>(st, st + kRPlane, st + 2 * kRPlane, (uint32_t)c,
                                            st + 2 * kRPlane + kRAm + (uint32_t)c * (8 * MT * 128), c, r0, g, t,
-                                           lut_base, lane4, acc);
+                                           lut_base, lane4, a.M, acc);
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(&empty[s]);

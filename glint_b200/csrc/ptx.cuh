@@ -120,6 +120,17 @@ __device__ __forceinline__ uint4 lds128(uint32_t a)
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
+/* 16-byte shared load issued only where `p` holds (zeros elsewhere): lanes that
+ * skip it take no shared-memory bandwidth. */
+__device__ __forceinline__ uint4 lds128_if(uint32_t a, bool p)
+{
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %5, 0;\n\t"
+                 "@q ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n\t}\n"
+                 : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+                 : "r"(a), "r"(p ? 1u : 0u));
+    return v;
+}
 __device__ __forceinline__ uint32_t lds32(uint32_t a)
 {
     uint32_t v;
