@@ -115,13 +115,27 @@ __device__ __forceinline__ int64_t cta_of(int64_t u, int64_t units, int64_t ctas
     return c;
 }
 
+/* Physical row (within its group of 8) behind mma fragment row g.  A half-warp
+ * holds fragment rows 0-3 (or 4-7); the map spreads them over rows whose swizzled
+ * 16-byte chunks of a 64-k block are all different, so its 8-byte plane loads
+ * cover the 32 banks once (the identity map reads 4 chunks twice: 2-way
+ * conflicts).  128-byte rows: rows 0,2,4,6 | 1,3,5,7 (chunk ^ (row & 7)); 64-byte
+ * rows: rows 0,1,4,5 | 2,3,6,7 (chunk ^ ((row >> 1) & 3), row parity picks the
+ * bank half). */
+template <int ROWB>
+__device__ __forceinline__ int frag_row(int g)
+{
+    return ROWB == 128 ? (((g & 3) << 1) | (g >> 2)) : ((g & 1) | (((g >> 1) & 1) << 2) | ((g >> 2) << 1));
+}
+
 /* One 64-k absmax block of a 16-row weight tile against the activations:
  * acc[mt] += absmax * (W[rows r0+g, r0+g+8][block] . x[mt*8+g'][block]).
  * `hole`/`plug`: plane tiles with ROWB-byte rows (128: 128B swizzle, 16-byte chunk j
  * of row r at j ^ (r & 7); 64: 64B swizzle, j ^ ((r >> 1) & 3)), the block at byte
  * 32*c of a row; `am`: absmax rows of 16 bytes, this block in column am_col; `xbox`:
  * the block's activation box, 8*MT rows x 128 B, 128B swizzle.  Swap-AB
- * mma.sync.m16n8k16: weights are the A operand (lane (g, t) holds rows g and g+8),
+ * mma.sync.m16n8k16: weights are the A operand (lane (g, t) holds rows
+ * frag_row(g) and frag_row(g)+8),
  * activations the B operand read with the same k map, so the dot product is exact
  * whatever the k order; hi (and lo in precise mode) BF16 halves of the codebook.
  * Lanes whose activation row mt*8+g is >= M (rows the TMA box fills with zeros)
@@ -135,7 +149,7 @@ __device__ __forceinline__ void tile_block(uint32_t hole, uint32_t plug, uint32_
     float sc[2];
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-        const int row = r0 + g + 8 * r;
+        const int row = r0 + frag_row<ROWB>(g) + 8 * r;
         const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(ROWB == 128 ? (row & 7) : ((row >> 1) & 3));
         const uint32_t off = (uint32_t)row * (uint32_t)ROWB + (chunk << 4) + (uint32_t)(t & 1) * 8u;
         const uint2 hw = lds64(hole + off), pw = lds64(plug + off);
@@ -304,9 +318,9 @@ __global__ void __launch_bounds__(kThreads, 1)
      * in the stream is complete (no-op without programmatic dependent launch) */
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    /* consumer warp: rows r0 + g and r0 + g + 8 of each unit's 128 */
+    /* consumer warp: rows r0 + pg and r0 + pg + 8 of each unit's 128 */
     const int g = (int)(lane >> 2), t = (int)(lane & 3);
-    const int r0 = warp * 16;
+    const int r0 = warp * 16, pg = frag_row<kKU / 2>(g);
     const uint32_t lut_base = saddr(lut);
     const uint32_t lane4 = lane * 4u;
     float acc[MT][4];
@@ -339,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    put_y(rb * kRows + r0 + g + (q >> 1) * 8, mt * 8 + 2 * t + (q & 1), acc[mt][q]);
+                    put_y(rb * kRows + r0 + pg + (q >> 1) * 8, mt * 8 + 2 * t + (q & 1), acc[mt][q]);
             return;
         }
         const int64_t first = cta_of((int64_t)rb * a.KU, a.units, ctas);
@@ -352,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    __stcg(const_cast<float *>(wsp) + ((int64_t)part * kRows + r0 + g + (q >> 1) * 8) * MP + mt * 8 +
+                    __stcg(const_cast<float *>(wsp) + ((int64_t)part * kRows + r0 + pg + (q >> 1) * 8) * MP + mt * 8 +
                                2 * t + (q & 1),
                            acc[mt][q]);
             __syncwarp();
@@ -387,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const int row = r0 + g + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
+                const int row = r0 + pg + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
                 float v = acc[mt][q];
                 for (int pp = 1; pp < parts; ++pp)
                     v += __ldcg(wsp + ((int64_t)pp * kRows + row) * MP + col);
@@ -470,7 +484,7 @@ struct RowArgs {
     int KH; /* consumer warps per tile (each a KH-th of a unit's k) */
 };
 
-template <int MT, bool SPLIT, bool BF16OUT>
+template <int MT, bool SPLIT, bool BF16OUT, int KH>
 __global__ void __launch_bounds__(kThreads, 1)
     htile_rows_kernel(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap pmap,
                       const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap xmap, const RowArgs a)
@@ -488,13 +502,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *cmb_full = empty + S;  /* a row block's KH-1 partials per tile are in scratch */
     uint64_t *cmb_empty = cmb_full + 1; /* the tile owners have read them */
 
-    const int active = a.T * a.KH;
+    const int active = a.T * KH;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], active);
         }
-        mbar_init(cmb_full, a.KH > 1 ? a.T * (a.KH - 1) : 1);
+        mbar_init(cmb_full, KH > 1 ? a.T * (KH - 1) : 1);
         mbar_init(cmb_empty, a.T);
         mbar_init_fence();
     }
@@ -567,9 +581,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp >= active)
         return;
 
-    /* warp kh takes blocks [kh*4/KH, (kh+1)*4/KH) of each unit */
-    const int tile = warp / a.KH, kh = warp % a.KH, nblk = 4 / a.KH, c0 = kh * nblk;
-    const int g = (int)(lane >> 2), t = (int)(lane & 3), r0 = tile * 16;
+    /* warp kh takes blocks [kh*4/KH, (kh+1)*4/KH) of each unit (unrolled, so the
+     * blocks' shared loads and MMAs interleave) */
+    constexpr int nblk = 4 / KH;
+    const int tile = warp / KH, kh = warp % KH, c0 = kh * nblk;
+    const int g = (int)(lane >> 2), t = (int)(lane & 3), r0 = tile * 16, pg = frag_row<128>(g);
     const uint32_t lut_base = saddr(lut), lane4 = lane * 4u;
     float acc[MT][4];
     bool alive = true;
@@ -587,10 +603,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             const uint32_t st = saddr(ring + s * kStage);
-            for (int c = c0; c < c0 + nblk; ++c)
+#pragma unroll
+            for (int j = 0; j < nblk; ++j) {
+                const int c = c0 + j;
                 tile_block<MT, SPLIT, 128>(st, st + kRPlane, st + 2 * kRPlane, (uint32_t)c,
                                            st + 2 * kRPlane + kRAm + (uint32_t)c * (8 * MT * 128), c, r0, g, t,
                                            lut_base, lane4, a.M, acc);
+            }
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(&empty[s]);
@@ -598,14 +617,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!alive)
             break;
         /* add the tile's KH partial sums in k order (kh 0, 1, ...), then y */
-        if (a.KH > 1) {
+        if (KH > 1) {
             if (kh > 0) {
                 bool ok = true;
                 if (blk > 0 && lane == 0)
                     ok = mbar_wait_suspend_bounded(cmb_empty, (uint32_t)(blk - 1) & 1u, &g_decode_error);
                 if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
                     break;
-                float *dst = scratch + ((tile * (a.KH - 1) + kh - 1) * 32 + (int)lane) * 4 * MT;
+                float *dst = scratch + ((tile * (KH - 1) + kh - 1) * 32 + (int)lane) * 4 * MT;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -619,8 +638,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = lane == 0 ? mbar_wait_suspend_bounded(cmb_full, (uint32_t)blk & 1u, &g_decode_error) : true;
             if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
                 break;
-            for (int kk = 1; kk < a.KH; ++kk) {
-                const float *src = scratch + ((tile * (a.KH - 1) + kk - 1) * 32 + (int)lane) * 4 * MT;
+            for (int kk = 1; kk < KH; ++kk) {
+                const float *src = scratch + ((tile * (KH - 1) + kk - 1) * 32 + (int)lane) * 4 * MT;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -636,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const int row = r0 + g + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
+                const int row = r0 + pg + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
                 const int n = nb0 + row;
                 if (row < a.RB && n < n_end && col < a.M) {
                     if (BF16OUT)
@@ -766,10 +785,10 @@ int launch_mt(int MT, const Maps &m, const DecodeArgs &a, int grid, cudaStream_t
     return launch_t<4, SPLIT, BF16OUT>(m, a, grid, st, pdl);
 }
 
-template <int MT, bool SPLIT, bool BF16OUT>
-int launch_rows_t(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bool pdl)
+template <int MT, bool SPLIT, bool BF16OUT, int KH>
+int launch_rows_kh(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bool pdl)
 {
-    auto kern = htile_rows_kernel<MT, SPLIT, BF16OUT>;
+    auto kern = htile_rows_kernel<MT, SPLIT, BF16OUT, KH>;
     if (!ensure_smem((const void *)kern, r_smem_bytes<MT>()))
         return kLaunch;
     cudaLaunchConfig_t cfg = {};
@@ -787,6 +806,15 @@ int launch_rows_t(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bo
         return kLaunch;
     }
     return kOk;
+}
+template <int MT, bool SPLIT, bool BF16OUT>
+int launch_rows_t(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bool pdl)
+{
+    if (a.KH == 2)
+        return launch_rows_kh<MT, SPLIT, BF16OUT, 2>(m, a, grid, st, pdl);
+    if (MT <= 2 && a.KH == 4)
+        return launch_rows_kh<MT, SPLIT, BF16OUT, MT <= 2 ? 4 : 2>(m, a, grid, st, pdl);
+    return kLaunch;
 }
 
 /* the row-owned kernel for N >= 16 x SMs: no workspace, no split rows */
