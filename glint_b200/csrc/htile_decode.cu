@@ -448,59 +448,67 @@ __global__ void __launch_bounds__(kThreads, 1)
  * When every SM can own at least 16 rows (N >= 16 x SMs), CTA c takes the rows
  * [c*R, (c+1)*R), R = ceil(N / ctas), over the whole K, so no row is split between
  * CTAs: no workspace, no cross-CTA sums, and the per-SM work differs by at most
- * one row.  Its rows go in row blocks of RB <= 112 (7 tiles of 16); the units are
- * (row block, 256 k): hole and plug tiles [RB rows x 128 B] (128B swizzle), an
- * absmax box [RB rows x 4 blocks] and the activation slice, through a TMA ring.
- * Consumer warp w works on tile w / KH and a KH-th of every unit's four 64-k
- * blocks; at the end of a row block the KH partial sums of a tile are added in k
- * order through shared memory (bounded mbarrier handshakes) and written to y. */
+ * one row.  Its rows go in row blocks of RB <= 112 (7 tiles of 16).  A unit is
+ * (row block, UB x 256 k): per 256 k, hole and plug tiles [RB rows x 128 B] (128B
+ * swizzle), an absmax box [RB rows x 4 blocks] and the activation slice (only the
+ * M rows that exist), through a TMA ring whose stage size follows RB, so narrow
+ * row blocks take two 256-k slices per stage and more stages: the bytes in flight
+ * per SM stay near the same whatever RB is.  Consumer warp w works on tile w / KH
+ * and NB = 4*UB/KH of every unit's 64-k blocks (unrolled, so the blocks' shared
+ * loads and MMAs interleave); at the end of a row block the KH partial sums of a
+ * tile are added in k order through shared memory (bounded mbarrier handshakes)
+ * and written to y. */
 constexpr int kRowBlockMax = 112;
-constexpr int kRPlane = kRowBlockMax * 128; /* 14 KB per plane tile */
-constexpr int kRAm = 2048;                  /* absmax box, >= 112 rows x 16 B */
+constexpr int kRMaxStages = 8;
 template <int MT>
-constexpr int r_xtile() { return 4 * 8 * MT * 128; }
+constexpr int r_xsub() { return 4 * 8 * MT * 128; } /* activation boxes of 256 k, 1 KB apart per 8 rows */
+/* ring capacity: 4 (MT 1) or 3 stages of the widest row block and one 256-k slice */
 template <int MT>
-constexpr int r_stage() { return 2 * kRPlane + kRAm + r_xtile<MT>(); }
+constexpr int r_ring() { return (MT == 1 ? 4 : 3) * (2 * kRowBlockMax * 128 + 2048 + r_xsub<MT>()); }
+/* partial sums exchanged at a row block's end: T * (KH - 1) <= 14 warps x 32 lanes */
 template <int MT>
-constexpr int r_stages() { return MT == 1 ? 4 : 3; }
-/* partial sums exchanged at a row block's end: T * (KH - 1) <= 12 warps x 32 lanes */
-template <int MT>
-constexpr int r_scratch_floats() { return (MT <= 2 ? 12 : 7) * 32 * 4 * MT; }
+constexpr int r_scratch_floats() { return (MT <= 2 ? 14 : 7) * 32 * 4 * MT; }
 template <int MT>
 constexpr int r_smem_bytes()
 {
-    return kLutBytes + 1024 + r_stages<MT>() * r_stage<MT>() + r_scratch_floats<MT>() * 4 + 8 * (2 * r_stages<MT>() + 2) +
-           64;
+    return kLutBytes + 1024 + r_ring<MT>() + r_scratch_floats<MT>() * 4 + 8 * (2 * kRMaxStages + 2) + 64;
 }
 
 struct RowArgs {
     void *y;
     int M, N, K;
-    int KU; /* 256-k units per row */
+    int KU; /* units per row (K / (256 UB)) */
+    int UB; /* 256-k slices per unit */
     int R;  /* rows per CTA */
     int nb; /* row blocks per CTA */
     int RB; /* rows per row block (the TMA box height) */
     int T;  /* 16-row tiles per row block */
-    int KH; /* consumer warps per tile (each a KH-th of a unit's k) */
+    int KH; /* consumer warps per tile */
+    int S;  /* ring stages */
+    int pt; /* bytes of a plane tile (RB x 128, 1 KB aligned) */
+    int at; /* bytes of an absmax tile (RB x 16, 1 KB aligned) */
+    int sub;   /* bytes of a 256-k slice: 2 pt + at + activation boxes */
+    int xrows; /* activation rows per box: min(M, 8 MT) */
+    uint32_t tx; /* TMA bytes per stage */
 };
 
-template <int MT, bool SPLIT, bool BF16OUT, int KH>
+template <int MT, bool SPLIT, bool BF16OUT, int NB>
 __global__ void __launch_bounds__(kThreads, 1)
     htile_rows_kernel(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap pmap,
                       const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap xmap, const RowArgs a)
 {
-    constexpr int S = r_stages<MT>();
-    constexpr int kStage = r_stage<MT>();
     static_assert(r_smem_bytes<MT>() <= 232448, "shared memory");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem_raw);
     uint8_t *ring = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) & ~uintptr_t(1023));
-    float *scratch = reinterpret_cast<float *>(ring + S * kStage);
+    float *scratch = reinterpret_cast<float *>(ring + r_ring<MT>());
     uint64_t *full = reinterpret_cast<uint64_t *>(scratch + r_scratch_floats<MT>());
-    uint64_t *empty = full + S;
-    uint64_t *cmb_full = empty + S;  /* a row block's KH-1 partials per tile are in scratch */
-    uint64_t *cmb_empty = cmb_full + 1; /* the tile owners have read them */
+    uint64_t *empty = full + kRMaxStages;
+    uint64_t *cmb_full = empty + kRMaxStages; /* a row block's KH-1 partials per tile are in scratch */
+    uint64_t *cmb_empty = cmb_full + 1;       /* the tile owners have read them */
+    const int S = a.S, KH = a.KH;
+    const int stage_bytes = a.UB * a.sub;
 
     const int active = a.T * KH;
     if (threadIdx.x == 0) {
@@ -524,40 +532,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane = lane_id();
     const int n_begin = blockIdx.x * a.R, n_end = min(a.N, n_begin + a.R);
     const int units = a.nb * a.KU;
-    const uint32_t box_bytes = (uint32_t)(2 * a.RB * 128 + a.RB * 16 + r_xtile<MT>());
 
     if (warp == kConsumers) {
         if (lane == 0) {
-            auto load_x = [&](int u, int s) {
-                const int ku = u % a.KU;
-                uint8_t *st = ring + s * kStage + 2 * kRPlane + kRAm;
+            auto load_x = [&](int ku, int s) {
+                for (int sb = 0; sb < a.UB; ++sb) {
+                    uint8_t *xs = ring + s * stage_bytes + sb * a.sub + 2 * a.pt + a.at;
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    tma_load_2d(st + c * (8 * MT * 128), &xmap, &full[s], ku * 256 + c * 64, 0);
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_2d(xs + c * (8 * MT * 128), &xmap, &full[s], (ku * a.UB + sb) * 256 + c * 64, 0);
+                }
             };
             bool ok = true;
-            int i = 0;
+            int i = 0, s = 0, blk = 0, ku = 0;
+            uint32_t ph = 0;
             for (; i < units; ++i) {
-                const int s = i % S;
-                const uint32_t ph = (uint32_t)(i / S) & 1u;
                 if (i >= S && !(ok = mbar_wait_suspend_bounded(&empty[s], ph ^ 1u, &g_decode_error)))
                     break;
-                const int blk = i / a.KU, ku = i % a.KU;
                 const int nb0 = n_begin + blk * a.RB;
-                uint8_t *st = ring + s * kStage;
-                mbar_expect_tx(&full[s], box_bytes);
-                tma_load_2d(st, &hmap, &full[s], ku * 128, nb0);
-                tma_load_2d(st + kRPlane, &pmap, &full[s], ku * 128, nb0);
-                tma_load_2d(st + 2 * kRPlane, &amap, &full[s], ku * 4, nb0);
+                uint8_t *st = ring + s * stage_bytes;
+                mbar_expect_tx(&full[s], a.tx);
+                for (int sb = 0; sb < a.UB; ++sb) {
+                    uint8_t *ss = st + sb * a.sub;
+                    const int k256 = ku * a.UB + sb;
+                    tma_load_2d(ss, &hmap, &full[s], k256 * 128, nb0);
+                    tma_load_2d(ss + a.pt, &pmap, &full[s], k256 * 128, nb0);
+                    tma_load_2d(ss + 2 * a.pt, &amap, &full[s], k256 * 4, nb0);
+                }
                 if (i >= S) {
-                    load_x(i, s);
+                    load_x(ku, s);
                 } else if (i == S - 1 || i == units - 1) {
                     /* weights stream before the previous kernel is done, activations after
                      * (programmatic dependent launch; a no-op otherwise) */
                     asm volatile("griddepcontrol.wait;" ::: "memory");
                     for (int j = 0; j <= i; ++j)
-                        load_x(j, j);
+                        load_x(j % a.KU, j);
                 }
+                if (++ku == a.KU)
+                    ku = 0, ++blk;
+                if (++s == S)
+                    s = 0, ph ^= 1u;
             }
             asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
             if (!ok) {
@@ -581,38 +595,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp >= active)
         return;
 
-    /* warp kh takes blocks [kh*4/KH, (kh+1)*4/KH) of each unit (unrolled, so the
-     * blocks' shared loads and MMAs interleave) */
-    constexpr int nblk = 4 / KH;
-    const int tile = warp / KH, kh = warp % KH, c0 = kh * nblk;
+    /* warp kh takes the unit's 64-k blocks [kh*NB, (kh+1)*NB) (block b: slice b/4, block b%4) */
+    const int tile = warp / KH, kh = warp % KH, b0 = kh * NB;
     const int g = (int)(lane >> 2), t = (int)(lane & 3), r0 = tile * 16, pg = frag_row<128>(g);
     const uint32_t lut_base = saddr(lut), lane4 = lane * 4u;
     float acc[MT][4];
     bool alive = true;
-    int i = 0;
+    int s = 0;
+    uint32_t ph = 0;
     for (int blk = 0; blk < a.nb && alive; ++blk) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
             acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-        for (int ku = 0; ku < a.KU; ++ku, ++i) {
-            const int s = i % S;
-            const uint32_t ph = (uint32_t)(i / S) & 1u;
+        for (int ku = 0; ku < a.KU; ++ku) {
             bool ok = lane == 0 ? mbar_wait_suspend_bounded(&full[s], ph, &g_decode_error) : true;
             if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0)) {
                 alive = false;
                 break;
             }
-            const uint32_t st = saddr(ring + s * kStage);
+            const uint32_t st = saddr(ring + s * stage_bytes);
 #pragma unroll
-            for (int j = 0; j < nblk; ++j) {
-                const int c = c0 + j;
-                tile_block<MT, SPLIT, 128>(st, st + kRPlane, st + 2 * kRPlane, (uint32_t)c,
-                                           st + 2 * kRPlane + kRAm + (uint32_t)c * (8 * MT * 128), c, r0, g, t,
+            for (int j = 0; j < NB; ++j) {
+                const int b = b0 + j, c = b & 3;
+                const uint32_t ss = st + (uint32_t)((b >> 2) * a.sub);
+                tile_block<MT, SPLIT, 128>(ss, ss + a.pt, ss + 2 * a.pt, (uint32_t)c,
+                                           ss + 2 * a.pt + a.at + (uint32_t)c * (8 * MT * 128), c, r0, g, t,
                                            lut_base, lane4, a.M, acc);
             }
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(&empty[s]);
+            if (++s == S)
+                s = 0, ph ^= 1u;
         }
         if (!alive)
             break;
@@ -785,10 +799,10 @@ int launch_mt(int MT, const Maps &m, const DecodeArgs &a, int grid, cudaStream_t
     return launch_t<4, SPLIT, BF16OUT>(m, a, grid, st, pdl);
 }
 
-template <int MT, bool SPLIT, bool BF16OUT, int KH>
-int launch_rows_kh(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bool pdl)
+template <int MT, bool SPLIT, bool BF16OUT, int NB>
+int launch_rows_nb(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bool pdl)
 {
-    auto kern = htile_rows_kernel<MT, SPLIT, BF16OUT, KH>;
+    auto kern = htile_rows_kernel<MT, SPLIT, BF16OUT, NB>;
     if (!ensure_smem((const void *)kern, r_smem_bytes<MT>()))
         return kLaunch;
     cudaLaunchConfig_t cfg = {};
@@ -810,12 +824,15 @@ int launch_rows_kh(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, b
 template <int MT, bool SPLIT, bool BF16OUT>
 int launch_rows_t(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bool pdl)
 {
-    if (a.KH == 2)
-        return launch_rows_kh<MT, SPLIT, BF16OUT, 2>(m, a, grid, st, pdl);
-    if (MT <= 2 && a.KH == 4)
-        return launch_rows_kh<MT, SPLIT, BF16OUT, MT <= 2 ? 4 : 2>(m, a, grid, st, pdl);
+    const int nb = 4 * a.UB / a.KH;
+    if (nb == 2)
+        return launch_rows_nb<MT, SPLIT, BF16OUT, 2>(m, a, grid, st, pdl);
+    if (nb == 1)
+        return launch_rows_nb<MT, SPLIT, BF16OUT, 1>(m, a, grid, st, pdl);
     return kLaunch;
 }
+
+constexpr int align1k(int v) { return (v + 1023) & ~1023; }
 
 /* the row-owned kernel for N >= 16 x SMs: no workspace, no split rows */
 int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
@@ -825,16 +842,40 @@ int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const
     const int sms = sm_count();
     const int g0 = std::max(1, std::min(sms, (N + 15) / 16));
     RowArgs a{};
-    a.y = y, a.M = M, a.N = N, a.K = K, a.KU = K / 256;
+    a.y = y, a.M = M, a.N = N, a.K = K;
     a.R = (N + g0 - 1) / g0;
     const int grid = (N + a.R - 1) / a.R;
     a.nb = (a.R + kRowBlockMax - 1) / kRowBlockMax;
     a.RB = (a.R + a.nb - 1) / a.nb;
     a.T = (a.RB + 15) / 16;
-    const int khmax = MT <= 2 ? 4 : 2;
-    a.KH = 1;
-    while (a.KH * 2 <= khmax && a.T * a.KH * 2 <= kConsumers)
-        a.KH *= 2;
+    /* warps per tile and 256-k slices per unit: as many consumer warps as the 16
+     * allow, two blocks per warp and unit where that still fills them (MT 4: one,
+     * for registers), two slices per unit for row blocks of <= 4 tiles */
+    a.UB = (a.T <= 4 && MT <= 2 && K % 512 == 0) ? 2 : 1;
+    const int blocks = 4 * a.UB, scratch_warps = MT <= 2 ? 14 : 7;
+    int nbk = MT <= 2 ? 2 : 1;
+    a.KH = blocks / nbk;
+    while ((a.T * a.KH > kConsumers || a.T * (a.KH - 1) > scratch_warps) && nbk < blocks) {
+        nbk *= 2;
+        a.KH = blocks / nbk;
+    }
+    if (a.T * a.KH < kConsumers / 2 && nbk > 1 && a.T * a.KH * 2 <= kConsumers &&
+        a.T * (a.KH * 2 - 1) <= scratch_warps) {
+        nbk /= 2;
+        a.KH = blocks / nbk;
+    }
+    if (a.T * a.KH > kConsumers || a.T * (a.KH - 1) > scratch_warps || nbk > 2)
+        return kLaunch;
+    a.KU = K / (256 * a.UB);
+    a.xrows = std::min(M, 8 * MT);
+    a.pt = align1k(a.RB * 128);
+    a.at = align1k(a.RB * 16);
+    a.sub = 2 * a.pt + a.at + (MT == 1 ? r_xsub<1>() : MT == 2 ? r_xsub<2>() : r_xsub<4>());
+    const int ring = MT == 1 ? r_ring<1>() : MT == 2 ? r_ring<2>() : r_ring<4>();
+    a.S = std::min(kRMaxStages, ring / (a.UB * a.sub));
+    if (a.S < 2)
+        return kLaunch;
+    a.tx = (uint32_t)(a.UB * (2 * a.RB * 128 + a.RB * 16 + 4 * a.xrows * 128));
     Maps maps;
     if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
                   (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -843,7 +884,7 @@ int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const
         !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
                   4, (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
-                  (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B))
+                  (uint32_t)a.xrows, CU_TENSOR_MAP_SWIZZLE_128B))
         return kLaunch;
     const bool bf = yk == kOutBF16, pr = mode == kPrecise;
 #define GLINT_ROWS_CASE(mt)                                                                                            \
