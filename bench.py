@@ -259,6 +259,9 @@ def bench_glint(args):
     result["htile"] = bench_htile(args, pk)
     # ---- column-parallel decode of a 70B layer over the ranks (NCCL all-gathers when world > 1)
     result["tp_decode"] = bench_tp_decode(args, world, rank, pk)
+    # ---- plugs in host memory, streamed through the two-slot ring (one GPU's PCIe link)
+    if world == 1:
+        result["plug_stream"] = bench_plug_stream(pk)
     # gpu_launches counts the headline's timed region (encode); the sub-results carry their own counts
     result["expand"]["launches"] = args.steps * len(groups)
     barrier(world)
@@ -450,6 +453,87 @@ def bench_tp_decode(args, world, rank, pk, M: int = 1):
             "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
             "all_gathers_per_layer": gathers, "kernels_per_layer": 7,
             "timing": "one layer in a CUDA graph (decode kernels + NCCL all-gathers), replayed; max over ranks"}
+
+
+def bench_plug_stream(pk, passes: int = 3):
+    """System-RAM residency (include/glint_plug_streamer.h): a Llama-3-8B decode
+    pass (32 layers x 7 linears, M = 1) with hole planes and absmax resident and
+    each layer's plug planes (109 MB) streamed from pinned host memory through the
+    two-slot ring while the previous layer computes.  Reported beside the same
+    pass with plugs resident and a plain pinned host->device copy of one layer's
+    plugs (the PCIe ceiling the streamed pass is bound by)."""
+    import torch
+    from glint_b200 import device as D
+    from glint_b200 import shard as SH
+    from glint_b200.streamer import PlugStreamer, device_bytes
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    lins = []
+    off = 0
+    for nm, N, K in SH.LLAMA3_8B_LAYER:
+        w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        h, p, a = D.encode(w, BS)
+        del w
+        lins.append((N, K, h, p, a, off))
+        off += p.numel()
+    layer_plug = off
+    n_layers = SH.LLAMA3_8B_LAYERS
+    plug_cat = torch.cat([l[3] for l in lins]).cpu()
+    xs = {K: torch.randn((1, K), generator=g, device="cuda").to(torch.bfloat16) for K in (4096, 14336)}
+    ys = [torch.empty((1, N), dtype=torch.float32, device="cuda") for N, *_ in lins]
+    copy_s, comp_s = torch.cuda.Stream(), torch.cuda.Stream()
+    copy_s.wait_stream(torch.cuda.current_stream())
+    comp_s.wait_stream(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+
+    def layer_calls(plug_of):
+        for i, (N, K, h, p, a, o) in enumerate(lins):
+            D.htile(xs[K], h, plug_of(i), a, N, BS, mode="fast", out=ys[i], stream=comp_s)
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    # plugs resident: the same 224 decode calls
+    for _ in range(2):
+        for _l in range(n_layers):
+            layer_calls(lambda i: lins[i][3])
+    ev[0].record(comp_s)
+    for _l in range(n_layers):
+        layer_calls(lambda i: lins[i][3])
+    ev[1].record(comp_s)
+    torch.cuda.synchronize()
+    resident_ms = ev[0].elapsed_time(ev[1])
+    with PlugStreamer([layer_plug] * n_layers, copy_s.cuda_stream, comp_s.cuda_stream) as st:
+        for l in range(n_layers):
+            st.set_host_data(l, plug_cat.numpy())
+
+        def timed_pass(compute: bool) -> float:
+            st.reset_stats()
+            ev[0].record(comp_s)
+            if st.start() != 0:
+                raise RuntimeError("plug streamer start failed")
+            for l in range(n_layers):
+                rc, ptr = st.acquire(l)
+                if rc != 0:
+                    raise RuntimeError(f"plug streamer acquire rc={rc}")
+                if compute:
+                    layer_calls(lambda i: device_bytes(ptr + lins[i][5], lins[i][3].numel()))
+                if st.release(l) != 0:
+                    raise RuntimeError("plug streamer release failed")
+            ev[1].record(comp_s)
+            torch.cuda.synchronize()
+            return ev[0].elapsed_time(ev[1])
+
+        # the ring's copy rate alone (no reads between acquire and release): the PCIe ceiling
+        copy_ms = statistics.median([timed_pass(False) for _ in range(passes + 1)][1:])
+        pass_ms = statistics.median([timed_pass(True) for _ in range(passes + 1)][1:])
+        stats = st.stats()
+    streamed = n_layers * layer_plug
+    return {"model": "Llama-3-8B decode pass, M=1, 32 layers x 7 linears, fast mode",
+            "plug_bytes_per_layer": layer_plug, "layers": n_layers,
+            "pass_ms": round(pass_ms, 3), "h2d_gbs": round(streamed / (pass_ms * 1e-3) / 1e9, 2),
+            "copy_only_pass_ms": round(copy_ms, 3), "copy_only_h2d_gbs": round(streamed / (copy_ms * 1e-3) / 1e9, 2),
+            "frac_of_copy_only": round(copy_ms / pass_ms, 4),
+            "resident_pass_ms": round(resident_ms, 3), "stall_ms_last_pass": round(stats["total_stall_ms"], 3),
+            "timing": "CUDA events on the compute stream around start() .. last release, median of 3 passes"}
 
 
 # ------------------------------------------------------------------ CPU baselines

@@ -65,7 +65,32 @@ def _bind(lib):
     lib.glint_htile_stream.restype = i32
     lib.p7_abi_version.restype = ctypes.c_char_p
     lib.glint_b200_version.restype = ctypes.c_char_p
+    # plug streamer (include/glint_plug_streamer.h)
+    lib.glint_plug_streamer_create.argtypes = [ctypes.POINTER(vp), i32, ctypes.POINTER(ctypes.c_uint64), vp, vp]
+    lib.glint_plug_streamer_create.restype = i32
+    lib.glint_plug_streamer_destroy.argtypes = [vp]
+    lib.glint_plug_streamer_destroy.restype = None
+    lib.glint_plug_streamer_set_host_data.argtypes = [vp, i32, vp, ctypes.c_uint64]
+    lib.glint_plug_streamer_set_host_data.restype = i32
+    lib.glint_plug_streamer_start.argtypes = [vp]
+    lib.glint_plug_streamer_start.restype = i32
+    lib.glint_plug_streamer_acquire.argtypes = [vp, i32, ctypes.POINTER(vp)]
+    lib.glint_plug_streamer_acquire.restype = i32
+    lib.glint_plug_streamer_release.argtypes = [vp, i32]
+    lib.glint_plug_streamer_release.restype = i32
+    lib.glint_plug_streamer_get_stats.argtypes = [vp, ctypes.POINTER(StreamerStats)]
+    lib.glint_plug_streamer_get_stats.restype = i32
+    lib.glint_plug_streamer_reset_stats.argtypes = [vp]
+    lib.glint_plug_streamer_reset_stats.restype = None
+    lib.glint_plug_streamer_host_buffer.argtypes = [vp, i32]
+    lib.glint_plug_streamer_host_buffer.restype = vp
     return lib
+
+
+class StreamerStats(ctypes.Structure):
+    """GlintStreamerStats (include/glint_plug_streamer.h)."""
+    _fields_ = [("total_h2d_bytes", ctypes.c_uint64), ("total_stall_ms", ctypes.c_double),
+                ("per_layer_stall_ms", ctypes.c_double * 64), ("n_layers", ctypes.c_int)]
 
 
 def load():
