@@ -6,12 +6,14 @@
  * 64-weight block, then scans 2 x 16 table entries per weight.  Here one pass
  * reads the input once:
  *
- *   - one persistent CTA per SM: 24 consumer warps and a producer warp that
- *     streams 24 KB units (12288 BF16 weights) into a 6-slot shared-memory ring
- *     with cp.async.bulk, so up to 144 KB per SM are in flight whatever the
+ *   - one persistent CTA per SM: 24 consumer warps (12 for f32 input) and a
+ *     producer warp that streams 48 KB units (24576 BF16 weights) into a 3-slot
+ *     shared-memory ring, BF16 through 2-D TMA with the 64-byte swizzle (rows of
+ *     32 weights; a quarter-warp's 16-byte reads of eight rows cover the 32
+ *     banks), f32 with cp.async.bulk, so 144 KB per SM are in flight whatever the
  *     register pressure; full/empty mbarriers hand the slots over;
- *   - a consumer lane owns 16 consecutive weights (two 16-byte shared loads), so
- *     a block of bs weights is bs/16 adjacent lanes and its absmax a shuffle-max
+ *   - a consumer lane owns 32 consecutive weights (four 16-byte shared loads), so
+ *     a block of bs weights is bs/32 adjacent lanes and its absmax a shuffle-max
  *     over them.  The maximum is taken with the packed BF16 max of absolute
  *     values that propagates NaN (for f32 input: integer max of |w|'s bits, where
  *     NaN sorts above inf), so the same pass tells whether the block holds a NaN;
@@ -23,6 +25,8 @@
  *     with s outside the theorem's range use the IEEE divide (and 0 when s == 0);
  *   - code = base + (v >= thr) from a 513-cell table in shared memory, 16
  *     replicas so the 8-byte lookups of a half-warp hit 16 distinct bank pairs;
+ *     the replicas hold thr lowered by one ulp, so the test is v > thr', on the
+ *     fast path the sign bit of one subtraction;
  *     on NaN-free blocks v lies in [-1, 1], so the cell is one fma and its
  *     address one multiply-add (the other blocks clamp first);
  *   - codes are byte-permuted into 8 bytes of hole and 8 bytes of plug per lane
@@ -208,8 +212,19 @@ __device__ __forceinline__ void pack8(const uint32_t *c, uint32_t &hw, uint32_t 
     pw = (A & 0x0F0F0F0Fu) | ((B << 4) & 0xF0F0F0F0u);
 }
 
+/* Bits of the largest float below the float with bits `b` (b neither +-0 nor
+ * NaN: the table's thresholds are nonzero, +inf where a cell has none).  For
+ * every non-NaN v, v >= thr exactly when v > prev_below(thr): no float lies
+ * between the two. */
+__device__ __forceinline__ uint32_t prev_below(uint32_t b) { return (b >> 31) ? b + 1u : b - 1u; }
+
 /* Codes of 16 weights of one block of absmax s; y = RN(1/s) when `fast` (the block
- * is NaN-free and s lies in the Markstein range). */
+ * is NaN-free and s lies in the Markstein range).  The shared table holds
+ * (thr' = prev_below(thr), base) per cell, and code = base + (v > thr').  On the
+ * fast path v is finite, so v > thr' is the sign bit of RN(thr' - v): the
+ * difference is negative exactly when v > thr', and an exact zero comes out +0
+ * (it could be -0 only for thr' = -0, which prev_below never yields), so one
+ * subtraction and one shift-add replace the compare and select. */
 __device__ __forceinline__ void codes16(const float *w, float s, float y, bool fast, uint32_t lut_c, uint32_t (&c)[16])
 {
     if (fast) {
@@ -227,15 +242,15 @@ __device__ __forceinline__ void codes16(const float *w, float s, float y, bool f
             unpack2(t2, t0, t1);
             const uint2 e0 = lds64(__float_as_uint(t0) * (uint32_t)(kEncReplicas * 8) + lut_c);
             const uint2 e1 = lds64(__float_as_uint(t1) * (uint32_t)(kEncReplicas * 8) + lut_c);
-            c[j] = e0.y + (v0 >= __uint_as_float(e0.x) ? 1u : 0u);
-            c[j + 1] = e1.y + (v1 >= __uint_as_float(e1.x) ? 1u : 0u);
+            c[j] = e0.y + (__float_as_uint(__fsub_rn(__uint_as_float(e0.x), v0)) >> 31);
+            c[j + 1] = e1.y + (__float_as_uint(__fsub_rn(__uint_as_float(e1.x), v1)) >> 31);
         }
     } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             const float v = (s == 0.f) ? 0.f : __fdiv_rn(w[j], s);
             const uint2 e = lds64((cell_of(v) + kMagicBits) * (uint32_t)(kEncReplicas * 8) + lut_c);
-            c[j] = e.y + (v >= __uint_as_float(e.x) ? 1u : 0u);
+            c[j] = e.y + (v > __uint_as_float(e.x) ? 1u : 0u); /* NaN v: base, as v >= thr */
         }
     }
 }
@@ -285,8 +300,12 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
     uint64_t *full = reinterpret_cast<uint64_t *>(meta + kSlots);
     uint64_t *empty = full + kSlots;
 
-    for (int i = threadIdx.x; i < kNumCells * kEncReplicas; i += enc_threads<In>())
-        lut[i] = g_encode_lut[i / kEncReplicas];
+    /* the replicas hold each cell's threshold lowered by one ulp (prev_below), so
+     * v >= thr becomes v > thr' (see codes16) */
+    for (int i = threadIdx.x; i < kNumCells * kEncReplicas; i += enc_threads<In>()) {
+        const uint2 e = g_encode_lut[i / kEncReplicas];
+        lut[i] = make_uint2(prev_below(e.x), e.y);
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&full[s], 1);
