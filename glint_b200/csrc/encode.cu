@@ -108,6 +108,15 @@ struct UnitMeta {
 };
 static_assert(sizeof(UnitMeta) == kMetaBytes, "slot descriptor layout");
 
+/* ring position of the next unit: slot s, and the phase parity of its barriers */
+__device__ __forceinline__ void next_slot(int &s, uint32_t &ph)
+{
+    if (++s == kSlots) {
+        s = 0;
+        ph ^= 1u;
+    }
+}
+
 /* generic-path lookup (non-replicated table) */
 __device__ __forceinline__ uint32_t lut_code(const uint2 *lut, int stride, float v)
 {
@@ -212,6 +221,17 @@ __device__ __forceinline__ void pack8(const uint32_t *c, uint32_t &hw, uint32_t 
     pw = (A & 0x0F0F0F0Fu) | ((B << 4) & 0xF0F0F0F0u);
 }
 
+/* y = RN(1/s) for a block scale s in the Markstein range.  BF16 input: s is a
+ * BF16 value (the |w| maximum of BF16 weights), so y is the table entry of its
+ * 7-bit fraction with the exponent moved; f32 input: the correctly rounded
+ * reciprocal. */
+__device__ __forceinline__ float block_rcp(const uint16_t *, float s, const uint32_t *rcp_tab)
+{
+    const uint32_t b = __float_as_uint(s);
+    return __uint_as_float(rcp_tab[(b >> 16) & 0x7Fu] + (127u << 23) - (b & 0x7F800000u));
+}
+__device__ __forceinline__ float block_rcp(const float *, float s, const uint32_t *) { return __frcp_rn(s); }
+
 /* Bits of the largest float below the float with bits `b` (b neither +-0 nor
  * NaN: the table's thresholds are nonzero, +inf where a cell has none).  For
  * every non-NaN v, v >= thr exactly when v > prev_below(thr): no float lies
@@ -306,6 +326,12 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
         const uint2 e = g_encode_lut[i / kEncReplicas];
         lut[i] = make_uint2(prev_below(e.x), e.y);
     }
+    /* RN(1 / (1 + k/128)), k = 0..127: with BF16 input a block's absmax is itself a
+     * BF16 value, 1.k x 2^E with a 7-bit fraction k, and RN(1/s) = RN(1/1.k) x 2^-E
+     * exactly (scaling by a power of two rounds nothing) */
+    __shared__ uint32_t rcp_tab[128];
+    if (threadIdx.x < 128)
+        rcp_tab[threadIdx.x] = __float_as_uint(__frcp_rn(1.0f + (float)threadIdx.x * (1.0f / 128.0f)));
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&full[s], 1);
@@ -322,12 +348,11 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
     if (warp == CW) {
         /* producer: publish each unit's descriptor, then one bulk copy per full, aligned unit */
         if (lane == 0) {
-            int it = 0;
+            int it = 0, s = 0;
             int64_t i = 0;
+            uint32_t ph = 0;
             bool ok = true;
-            for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
-                const int s = (int)(i % kSlots);
-                const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
+            for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i, next_slot(s, ph)) {
                 if (i >= kSlots && !(ok = mbar_wait_bounded(&empty[s], ph ^ 1u, &g_encode_error)))
                     break;
                 while (b.unit_end[it] <= u)
@@ -374,10 +399,9 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
     /* consumers: a lane owns 32 consecutive weights of a unit */
     const uint32_t lut_c = saddr(lut) + (lane & (kEncReplicas - 1)) * 8u - kMagicBits * (uint32_t)(kEncReplicas * 8);
     const int rel = (warp * 32 + (int)lane) * kWpl; /* element offset inside a unit */
-    int64_t i = 0;
-    for (int64_t u = blockIdx.x; u < total; u += gridDim.x, ++i) {
-        const int s = (int)(i % kSlots);
-        const uint32_t ph = (uint32_t)(i / kSlots) & 1u;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int64_t u = blockIdx.x; u < total; u += gridDim.x, next_slot(s, ph)) {
         const bool ok = lane == 0 ? mbar_wait_bounded(&full[s], ph, &g_encode_error) : true;
         if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
             break;
@@ -427,7 +451,7 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
                 sc = nan_skipping_max<G>(both, 32); /* absmax skips NaN, as the reference's (a > m) does */
             }
             const bool fast = nan_free && sc >= kMarksteinLo && sc <= kMarksteinHi;
-            const float y = fast ? __frcp_rn(sc) : 0.f;
+            const float y = fast ? block_rcp(src, sc, rcp_tab) : 0.f;
             codes16(A.w, sc, y, fast, lut_c, ca);
             codes16(B.w, sc, y, fast, lut_c, cb);
             sa = sb = sc;
@@ -438,8 +462,8 @@ __global__ void __launch_bounds__(enc_threads<In>(), 1) encode_stream_kernel(con
             sb = nfb ? __uint_as_float(B.mag) : nan_skipping_max<1>(B.w, 16);
             const bool fa = nfa && sa >= kMarksteinLo && sa <= kMarksteinHi;
             const bool fb = nfb && sb >= kMarksteinLo && sb <= kMarksteinHi;
-            codes16(A.w, sa, fa ? __frcp_rn(sa) : 0.f, fa, lut_c, ca);
-            codes16(B.w, sb, fb ? __frcp_rn(sb) : 0.f, fb, lut_c, cb);
+            codes16(A.w, sa, fa ? block_rcp(src, sa, rcp_tab) : 0.f, fa, lut_c, ca);
+            codes16(B.w, sb, fb ? block_rcp(src, sb, rcp_tab) : 0.f, fb, lut_c, cb);
         }
         uint32_t h[4], p[4];
         pack16(ca, h[0], h[1], p[0], p[1]);
