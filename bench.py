@@ -380,12 +380,16 @@ def bench_htile(args, pk):
 def bench_tp_decode(args, world, rank, pk, M: int = 1):
     """configs[4]-style decode step of one Llama-3-70B layer, column-parallel over
     the ranks (glint_b200/tp.py): every rank holds 1/world of each linear's packed
-    rows and runs the decode kernel on them; all-gathers (NCCL) reassemble the
-    o_proj and down_proj inputs and outputs, the only places a consumer needs whole
-    rows (q/k/v and gate/up consumers work on their column shards).  The layer is
+    rows and runs the decode kernel on them.  Where a consumer needs whole rows the
+    output is gathered: with `fused`, inside the decode kernel (tp.PeerGather: each
+    rank stores its rows into every rank's buffer over NVLink) for o_proj, gate/up
+    (so every rank forms the whole down_proj input) and down_proj, with one NCCL
+    all-gather left for the attention output that feeds o_proj; without it, NCCL
+    all-gathers of the o_proj and down_proj inputs and outputs.  The layer is
     captured once in a CUDA graph (kernels and collectives), replayed, timed with
     CUDA events, max over ranks; tokens/s assumes the 80 identical layers."""
     import torch
+    import torch.nn.functional as F
     from glint_b200 import device as D
     from glint_b200 import shard as SH
     from glint_b200 import tp
@@ -401,11 +405,17 @@ def bench_tp_decode(args, world, rank, pk, M: int = 1):
         del w
         shards[nm] = tp.ColumnShard(n0, n1, N, K, BS, h, p, a)
         local_bytes += (n1 - n0) * K * (1 + 4 / 64)
-    x = torch.randn((M, 8192), generator=g, device="cuda").to(torch.bfloat16)
-    attn = torch.randn((M, 8192), generator=g, device="cuda").to(torch.bfloat16)
-    act_full = torch.randn((M, 28672), generator=g, device="cuda").to(torch.bfloat16)
+    gx = torch.Generator(device="cuda")
+    gx.manual_seed(7)  # activations replicated: the same on every rank
+    x = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
+    attn = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
+    act_full = torch.randn((M, 28672), generator=gx, device="cuda").to(torch.bfloat16)
+    pg = None
+    if world > 1:
+        pg = tp.PeerGather({"o": (M, 8192, torch.float32), "gate": (M, 28672, torch.float32),
+                            "up": (M, 28672, torch.float32), "down": (M, 8192, torch.float32)}, world, rank)
 
-    def layer():
+    def layer_nccl():
         outs = []
         for nm in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj"):
             outs.append(tp.column_parallel(x, shards[nm], world, rank, gather=False))
@@ -418,41 +428,62 @@ def bench_tp_decode(args, world, rank, pk, M: int = 1):
         d = tp.column_parallel(d_in.to(torch.bfloat16), shards["down_proj"], world, rank)
         return outs, o, d
 
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
+    def layer_fused():
+        outs = [tp.column_parallel(x, shards[nm], world, rank, gather=False) for nm in ("q_proj", "k_proj", "v_proj")]
+        o_in = tp.gather_columns(attn[:, shards["o_proj"].n0:shards["o_proj"].n1].float(), 8192, world, rank)
+        o = pg.linear(o_in.to(torch.bfloat16), shards["o_proj"], "o")
+        gate = pg.linear(x, shards["gate_proj"], "gate")
+        up = pg.linear(x, shards["up_proj"], "up")
+        act = (F.silu(gate) * up).to(torch.bfloat16)
+        d = pg.linear(act, shards["down_proj"], "down")
+        return outs, o, d
+
+    def timed(layer):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                layer()
+        torch.cuda.synchronize()
+        barrier(world)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gr, stream=s):
+                layer()
+        torch.cuda.synchronize()
+        barrier(world)
+        reps = 50
         for _ in range(3):
-            layer()
-    torch.cuda.synchronize()
-    barrier(world)
-    gr = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(gr, stream=s):
-            layer()
-    torch.cuda.synchronize()
-    barrier(world)
-    reps = 50
-    for _ in range(3):
-        gr.replay()
-    torch.cuda.synchronize()
-    barrier(world)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(reps):
-        gr.replay()
-    b.record()
-    torch.cuda.synchronize()
-    us = max_over_ranks(world, a.elapsed_time(b) * 1e3 / reps)
-    barrier(world)
-    del gr  # graphs holding NCCL calls go before the process group does
-    torch.cuda.synchronize()
-    gathers = 4 if world > 1 else 0
-    return {"model": "Llama-3-70B layer (configs[4] shapes)", "tp": world, "batch": M,
-            "us_per_layer": round(us, 2), "tokens_per_s_80_layers": round(M / (80 * us * 1e-6), 1),
-            "weight_bytes_per_gpu_per_layer": int(local_bytes),
-            "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
-            "all_gathers_per_layer": gathers, "kernels_per_layer": 7,
-            "timing": "one layer in a CUDA graph (decode kernels + NCCL all-gathers), replayed; max over ranks"}
+            gr.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            gr.replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = max_over_ranks(world, a.elapsed_time(b) * 1e3 / reps)
+        barrier(world)
+        del gr  # graphs holding NCCL calls go before the process group does
+        torch.cuda.synchronize()
+        return us
+
+    us_nccl = timed(layer_nccl)
+    res = {"model": "Llama-3-70B layer (configs[4] shapes)", "tp": world, "batch": M,
+           "weight_bytes_per_gpu_per_layer": int(local_bytes), "kernels_per_layer": 7,
+           "timing": "one layer in a CUDA graph (decode kernels + gathers), replayed; max over ranks"}
+    if pg is not None:
+        us = timed(layer_fused)
+        pg.close()
+        res.update({"us_per_layer": round(us, 2), "gathers": "fused into o/gate/up/down decode (peer stores) + 1 NCCL",
+                    "us_per_layer_nccl_gathers": round(us_nccl, 2)})
+    else:
+        us = us_nccl
+        res.update({"us_per_layer": round(us, 2), "gathers": "none (one GPU)"})
+    res.update({"tokens_per_s_80_layers": round(M / (80 * us * 1e-6), 1),
+                "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4)})
+    return res
 
 
 def bench_plug_stream(pk, passes: int = 3):

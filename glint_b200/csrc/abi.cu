@@ -510,6 +510,82 @@ int glint_htile_stream(const uint8_t *d_hole, const uint8_t *d_plug, const float
                         blocksize, mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
 }
 
+int glint_htile_gather_stream(const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
+                              const __nv_bfloat16 *d_x, void *const *d_y_ranks, unsigned int *const *d_flag_ranks,
+                              int world, int rank, int y_dtype, int M, int N, int K, int ld_y, int n0,
+                              int blocksize, int mode, cudaStream_t stream)
+{
+    if (!d_hole || !d_plug || !d_absmax || !d_x || !d_y_ranks || !d_flag_ranks || world < 1 || rank < 0 ||
+        rank >= world)
+        return kBadArg;
+    for (int r = 0; r < world; ++r)
+        if (!d_y_ranks[r] || !d_flag_ranks[r])
+            return kBadArg;
+    if ((y_dtype != GLINT_Y_F32 && y_dtype != GLINT_Y_BF16) || (mode != GLINT_HTILE_PRECISE && mode != GLINT_HTILE_FAST))
+        return kBadArg;
+    if (blocksize <= 0)
+        return kBadBlocksize;
+    if (M <= 0 || N <= 0 || K <= 0 || n0 < 0 || ld_y < n0 + N)
+        return kBadArg;
+    if (!htile_decode_supported(d_hole, d_plug, d_absmax, d_x, M, N, K, blocksize) || !htile_gather_supported(M, N))
+        return kUnsupported;
+    return htile_decode_gather_launch(d_hole, d_plug, d_absmax, d_x, d_y_ranks, d_flag_ranks, world, rank,
+                                      y_dtype == GLINT_Y_BF16 ? kOutBF16 : kOutF32, M, N, K, ld_y, n0,
+                                      mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
+}
+
+int glint_device_alloc(size_t bytes, void **d_ptr)
+{
+    if (!d_ptr || bytes == 0)
+        return kBadArg;
+    *d_ptr = nullptr;
+    if (cudaMalloc(d_ptr, bytes) != cudaSuccess || cudaMemset(*d_ptr, 0, bytes) != cudaSuccess) {
+        if (*d_ptr)
+            cudaFree(*d_ptr);
+        *d_ptr = nullptr;
+        cudaGetLastError();
+        return kLaunch;
+    }
+    return kOk;
+}
+int glint_device_free(void *d_ptr) { return d_ptr && cudaFree(d_ptr) != cudaSuccess ? kLaunch : kOk; }
+int glint_ipc_handle(const void *d_ptr, void *handle_out)
+{
+    if (!d_ptr || !handle_out)
+        return kBadArg;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, const_cast<void *>(d_ptr)) != cudaSuccess) {
+        cudaGetLastError();
+        return kLaunch;
+    }
+    std::memcpy(handle_out, &h, sizeof(h));
+    return kOk;
+}
+int glint_ipc_open(const void *handle, void **d_ptr)
+{
+    if (!handle || !d_ptr)
+        return kBadArg;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    *d_ptr = nullptr;
+    if (cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        *d_ptr = nullptr;
+        return kLaunch;
+    }
+    return kOk;
+}
+int glint_ipc_close(void *d_ptr)
+{
+    if (!d_ptr)
+        return kBadArg;
+    if (cudaIpcCloseMemHandle(d_ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return kLaunch;
+    }
+    return kOk;
+}
+
 int glint_htile_stream_noalloc(const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
                                const __nv_bfloat16 *d_x, void *d_y, int y_dtype, int M, int N, int K,
                                int blocksize, int mode, cudaStream_t stream)

@@ -25,6 +25,7 @@ enum Status : int {
     kLaunch = -3,
     kCodebook = -4,
     kScratch = -5, /* the fixed scratch area is too small for this call */
+    kUnsupported = -6, /* a shape or rank layout the gathered call does not cover */
 };
 
 /* Encode lookup table: {threshold bits, base code} per grid cell, generated at

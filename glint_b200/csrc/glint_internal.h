@@ -70,6 +70,14 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
                                 const __nv_bfloat16 *x, void *y, OutKind y_kind, int M, int N, int K,
                                 HtileMode mode, cudaStream_t stream);
 
+/* Decode with the output gathered into every rank's y over peer memory
+ * (1 <= M <= 16; kUnsupported otherwise). */
+bool htile_gather_supported(int M, int N);
+int htile_decode_gather_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax,
+                               const __nv_bfloat16 *x, void *const *y_ranks, uint32_t *const *flag_ranks,
+                               int world, int rank, OutKind y_kind, int M, int N, int K, int ldy, int n0,
+                               HtileMode mode, cudaStream_t stream);
+
 /* SM count of the current device (cached per device). */
 int sm_count();
 /* Raise a kernel's dynamic shared memory limit once per device. */

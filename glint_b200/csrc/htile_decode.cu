@@ -91,6 +91,77 @@ __device__ __forceinline__ uint32_t split_pair(float c)
     return hi | (f32_to_bf16_bits(rest) << 16);
 }
 
+/* Gathered output (world > 0): this call's rows [n0, n0 + N) of y[M, ldy] are
+ * stored into every rank's y (yr[r], this rank's own included), then counted in
+ * (gather_complete).  world == 0: plain y. */
+constexpr int kMaxGather = 8;
+struct GatherArgs {
+    int world, rank, ldy, n0;
+    uint32_t *flag; /* this rank's counters: [r] calls whose rows rank r has delivered here, [kMaxGather] warps done */
+    void *yr[kMaxGather];
+    uint32_t *fr[kMaxGather]; /* every rank's counters */
+};
+template <bool BF16OUT>
+__device__ __forceinline__ void gather_store(const GatherArgs &g, int col, int n, float v)
+{
+    /* every rank's y: NVLink stores to the peers, a local store for this rank */
+    const int64_t o = (int64_t)col * g.ldy + g.n0 + n;
+    for (int r = 0; r < g.world; ++r) {
+        if (BF16OUT)
+            static_cast<__nv_bfloat16 *>(g.yr[r])[o] = __float2bfloat16_rn(v);
+        else
+            static_cast<float *>(g.yr[r])[o] = v;
+    }
+}
+/* End of a gathered call, run by every active consumer warp after its last y
+ * stores.  The warp counts itself in, first in its CTA (shared memory), the CTA's
+ * last warp then in the rank (one global atomic per CTA); the rank's last warp
+ * resets the count and, after a system-scope fence, adds one to its own slot in
+ * every rank's counters, then waits (acquire, system scope), bounded,
+ * for one arrival from every rank and takes it (subtracts one).  Each rank's
+ * arrivals come in call order and a rank can be at most one call ahead (its next
+ * call cannot finish before this rank's arrival), so taking one per rank per call
+ * never confuses calls; nothing here depends on a call number, so the same launch
+ * can be replayed (CUDA graphs).  The kernel completes only when this rank's y
+ * holds every rank's rows.  Ranks run on different GPUs; inside a rank only this
+ * one warp waits. */
+__device__ __forceinline__ void gather_complete(const GatherArgs &a, int active, uint32_t lane, uint32_t *cta_done)
+{
+    /* the counting chain orders every warp's stores before the rank's last warp
+     * with device-scope acquire-release fences (fence, count; observe the count,
+     * fence); that warp's one system-scope acquire-release fence followed by the
+     * signals forms a release pattern that covers them all (an sc fence, or a
+     * release on every signal, cost ~5 us more per call for the same ordering) */
+    __syncwarp();
+    if (lane != 0)
+        return;
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    if (atomicAdd(cta_done, 1u) + 1u != (uint32_t)active)
+        return;
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    if (atomicAdd(a.flag + kMaxGather, 1u) + 1u != gridDim.x)
+        return;
+    atomicExch(a.flag + kMaxGather, 0u);
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < a.world; ++r)
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(a.fr[r] + a.rank) : "memory");
+    const long long t0 = clock64();
+    for (int r = 0; r < a.world; ++r) {
+        while (true) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.flag + r) : "memory");
+            if (v != 0u) {
+                atomicSub(a.flag + r, 1u);
+                break;
+            }
+            if (clock64() - t0 > kWaitCycles) {
+                atomicOr(&g_decode_error, kErrTimeout);
+                return;
+            }
+            __nanosleep(128);
+        }
+    }
+}
 struct DecodeArgs {
     const __nv_bfloat16 *x;
     void *y;
@@ -100,6 +171,7 @@ struct DecodeArgs {
     int KU;             /* units per row block (K / 256) */
     int64_t units;      /* row blocks * KU */
     int max_parts;
+    GatherArgs ga;
 };
 
 /* first unit of CTA c under the even split of `units` over `ctas` */
@@ -231,6 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         (reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + kSlots * kSlotBytes);
     uint64_t *empty = full + kSlots;
+    uint32_t *cta_done = reinterpret_cast<uint32_t *>(empty + kSlots); /* gathered calls: warps done */
 
     /* barriers first, so the producer can start streaming while the consumers
      * build the codebook */
@@ -239,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumers);
         }
+        *cta_done = 0u;
         mbar_init_fence();
     }
     if (threadIdx.x == kConsumers * 32) {
@@ -342,7 +416,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int MP = 8 * MT;
         auto put_y = [&](int n, int col, float v) {
             if (n < a.N && col < a.M) {
-                if (BF16OUT)
+                if (a.ga.world > 0)
+                    gather_store<BF16OUT>(a.ga, col, n, v);
+                else if (BF16OUT)
                     static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(v);
                 else
                     static_cast<float *>(a.y)[(int64_t)col * a.N + n] = v;
@@ -374,37 +450,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                 asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(flg + part * kConsumers) : "memory");
             return;
         }
+        /* lane l waits for the flag of part l (and l + 32, ...): the waits overlap */
         bool ok = true;
-        if (lane == 0) {
-            for (int pp = 1; pp < parts && ok; ++pp) {
-                int *f = flg + pp * kConsumers;
-                const long long t0 = clock64();
-                uint32_t v = 0;
-                while (true) {
-                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-                    if (v)
-                        break;
-                    if (clock64() - t0 > kWaitCycles) {
-                        atomicOr(&g_decode_error, kErrTimeout);
-                        ok = false;
-                        break;
-                    }
-                    __nanosleep(64);
+        for (int pp = (int)lane; pp < parts && ok; pp += 32) {
+            if (pp == 0)
+                continue;
+            int *f = flg + pp * kConsumers;
+            const long long t0 = clock64();
+            uint32_t v = 0;
+            while (true) {
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                if (v)
+                    break;
+                if (clock64() - t0 > kWaitCycles) {
+                    atomicOr(&g_decode_error, kErrTimeout);
+                    ok = false;
+                    break;
                 }
-                *f = 0; /* consumed: zero for the next call */
+                __nanosleep(64);
             }
+            *f = 0; /* consumed: zero for the next call */
         }
-        __syncwarp();
-        if (!__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
+        if (!__all_sync(0xFFFFFFFFu, ok))
             return;
+        /* the parts' sums in part (k) order; loads issued eight at a time so their
+         * L2 latencies overlap */
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int row = r0 + pg + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
+                const float *src = wsp + (int64_t)row * MP + col;
+                const int64_t step = (int64_t)kRows * MP;
                 float v = acc[mt][q];
-                for (int pp = 1; pp < parts; ++pp)
-                    v += __ldcg(wsp + ((int64_t)pp * kRows + row) * MP + col);
+                int pp = 1;
+                for (; pp + 8 <= parts; pp += 8) {
+                    float w8[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        w8[j] = __ldcg(src + (pp + j) * step);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        v += w8[j];
+                }
+                for (; pp < parts; ++pp)
+                    v += __ldcg(src + pp * step);
                 put_y(rb * kRows + row, col, v);
             }
         }
@@ -442,6 +532,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (cur_rb >= 0)
         flush(cur_rb, seg_k0, (int)(u1 - 1 - (int64_t)cur_rb * a.KU) + 1);
+    if (a.ga.world > 0)
+        gather_complete(a.ga, kConsumers, lane, cta_done);
 }
 
 /* ---- row-owned decode for wide layers ------------------------------------------
@@ -490,6 +582,7 @@ struct RowArgs {
     int sub;   /* bytes of a 256-k slice: 2 pt + at + activation boxes */
     int xrows; /* activation rows per box: min(M, 8 MT) */
     uint32_t tx; /* TMA bytes per stage */
+    GatherArgs ga;
 };
 
 template <int MT, bool SPLIT, bool BF16OUT, int NB>
@@ -507,6 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *empty = full + kRMaxStages;
     uint64_t *cmb_full = empty + kRMaxStages; /* a row block's KH-1 partials per tile are in scratch */
     uint64_t *cmb_empty = cmb_full + 1;       /* the tile owners have read them */
+    uint32_t *cta_done = reinterpret_cast<uint32_t *>(cmb_empty + 1); /* gathered calls: warps done */
     const int S = a.S, KH = a.KH;
     const int stage_bytes = a.UB * a.sub;
 
@@ -518,6 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(cmb_full, KH > 1 ? a.T * (KH - 1) : 1);
         mbar_init(cmb_empty, a.T);
+        *cta_done = 0u;
         mbar_init_fence();
     }
     if (threadIdx.x == kConsumers * 32) {
@@ -672,14 +767,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int row = r0 + pg + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
                 const int n = nb0 + row;
                 if (row < a.RB && n < n_end && col < a.M) {
-                    if (BF16OUT)
+                    if (a.ga.world > 0) {
+                        gather_store<BF16OUT>(a.ga, col, n, acc[mt][q]);
+                    } else if (BF16OUT) {
                         static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(acc[mt][q]);
-                    else
+                    } else {
                         static_cast<float *>(a.y)[(int64_t)col * a.N + n] = acc[mt][q];
+                    }
                 }
             }
         }
     }
+    if (a.ga.world > 0)
+        gather_complete(a.ga, active, lane, cta_done);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder()
@@ -836,13 +936,16 @@ constexpr int align1k(int v) { return (v + 1023) & ~1023; }
 
 /* the row-owned kernel for N >= 16 x SMs: no workspace, no split rows */
 int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
-                OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st, bool pdl)
+                OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st, bool pdl,
+                const GatherArgs *gt = nullptr)
 {
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
     const int sms = sm_count();
     const int g0 = std::max(1, std::min(sms, (N + 15) / 16));
     RowArgs a{};
     a.y = y, a.M = M, a.N = N, a.K = K;
+    if (gt)
+        a.ga = *gt;
     a.R = (N + g0 - 1) / g0;
     const int grid = (N + a.R - 1) / a.R;
     a.nb = (a.R + kRowBlockMax - 1) / kRowBlockMax;
@@ -900,9 +1003,16 @@ int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const
     return kLaunch;
 }
 
-/* wide enough for every SM to own >= 16 rows, and narrow enough for <= 2 row
- * blocks per CTA (beyond that stream-K keeps more warps busy) */
-bool rows_supported(int N) { return N >= 16 * sm_count() && N <= 2 * kRowBlockMax * sm_count(); }
+/* Row-owned decode when every SM can own >= 16 rows and no CTA has more than 2
+ * row blocks (beyond that stream-K keeps more warps busy), and for narrower layers
+ * (16-row CTAs on fewer SMs) while a CTA's slice stays <= 16 x 8192 weights: up
+ * to there it beats stream-K, whose split-K partial sums cost more than the SMs
+ * left idle (N = 1024, K = 4096: 8.0 against 11.7 us); for longer K, stream-K. */
+bool rows_supported(int N, int K)
+{
+    const int sms = sm_count();
+    return N >= 16 && N <= 2 * kRowBlockMax * sms && (N >= 16 * sms || K <= 8192);
+}
 
 } // namespace
 
@@ -930,11 +1040,11 @@ bool decode_maps(Maps &maps, const uint8_t *hole, const uint8_t *plug, const flo
                     (uint32_t)(8 * MT), CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
-                        OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
+int decode_launch_impl(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                       OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st, const GatherArgs *gt)
 {
-    if (rows_supported(N))
-        return launch_rows(hole, plug, am, x, y, yk, M, N, K, mode, st, true);
+    if (rows_supported(N, K))
+        return launch_rows(hole, plug, am, x, y, yk, M, N, K, mode, st, true, gt);
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
     Maps maps;
     if (!decode_maps(maps, hole, plug, am, x, M, N, K, MT))
@@ -957,6 +1067,8 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
         return kLaunch;
     a.ws = S.ws;
     a.flags = S.counters;
+    if (gt)
+        a.ga = *gt;
     const bool bf = yk == kOutBF16;
     if (mode == kPrecise)
         return bf ? launch_mt<true, true>(MT, maps, a, grid, st, true) : launch_mt<true, false>(MT, maps, a, grid, st, true);
@@ -983,13 +1095,34 @@ std::mutex g_noalloc_mu;
 void *g_noalloc_addr[64] = {};
 }
 
+int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                        OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
+{
+    return decode_launch_impl(hole, plug, am, x, y, yk, M, N, K, mode, st, nullptr);
+}
+
+bool htile_gather_supported(int M, int N) { return M >= 1 && M <= 16 && N >= 1; }
+
+int htile_decode_gather_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
+                               void *const *y_ranks, uint32_t *const *flag_ranks, int world, int rank,
+                               OutKind yk, int M, int N, int K, int ldy, int n0, HtileMode mode, cudaStream_t st)
+{
+    if (world < 1 || world > kMaxGather || rank < 0 || rank >= world || !htile_gather_supported(M, N))
+        return kUnsupported;
+    GatherArgs g{};
+    g.world = world, g.rank = rank, g.ldy = ldy, g.n0 = n0, g.flag = flag_ranks[rank];
+    for (int r = 0; r < world; ++r)
+        g.yr[r] = y_ranks[r], g.fr[r] = flag_ranks[r];
+    return decode_launch_impl(hole, plug, am, x, y_ranks[rank], yk, M, N, K, mode, st, &g);
+}
+
 int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
                                 void *y, OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
 {
     /* the documented limit of this entry point, whichever kernel runs */
     if (N > kNoAllocMaxN)
         return kScratch;
-    if (rows_supported(N)) /* needs no scratch at all */
+    if (rows_supported(N, K)) /* needs no scratch at all */
         return launch_rows(hole, plug, am, x, y, yk, M, N, K, mode, st, false);
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)

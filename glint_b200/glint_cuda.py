@@ -65,6 +65,20 @@ def _bind(lib):
     lib.glint_htile_stream.restype = i32
     lib.p7_abi_version.restype = ctypes.c_char_p
     lib.glint_b200_version.restype = ctypes.c_char_p
+    # gathered decode and CUDA IPC (include/glint_htile.h, additive)
+    lib.glint_htile_gather_stream.argtypes = [vp, vp, vp, vp, ctypes.POINTER(vp), ctypes.POINTER(vp), i32, i32, i32,
+                                              i32, i32, i32, i32, i32, i32, i32, vp]
+    lib.glint_htile_gather_stream.restype = i32
+    lib.glint_device_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+    lib.glint_device_alloc.restype = i32
+    lib.glint_device_free.argtypes = [vp]
+    lib.glint_device_free.restype = i32
+    lib.glint_ipc_handle.argtypes = [vp, vp]
+    lib.glint_ipc_handle.restype = i32
+    lib.glint_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
+    lib.glint_ipc_open.restype = i32
+    lib.glint_ipc_close.argtypes = [vp]
+    lib.glint_ipc_close.restype = i32
     # plug streamer (include/glint_plug_streamer.h)
     lib.glint_plug_streamer_create.argtypes = [ctypes.POINTER(vp), i32, ctypes.POINTER(ctypes.c_uint64), vp, vp]
     lib.glint_plug_streamer_create.restype = i32

@@ -6,14 +6,17 @@ ranks the weight shards column-parallel: rank r holds packed rows [n0, n1) of W
 (`shard.column_shard`, boundaries on 16-row multiples), which for K % blocksize == 0
 is one contiguous byte range of hole and plug and one float range of absmax
 (`shard.shard_planes`).  Each rank runs its local H-TILE kernel on its rows and a
-single all-gather (NCCL over NVLink/NVSwitch on a B200 node) reassembles y where the
-consumer needs whole rows.  Activations are replicated, so there is no other
-exchange; nothing reads another GPU's memory directly.
+single all-gather reassembles y where the consumer needs whole rows: either NCCL
+(`gather_columns`) or, for decode shapes, fused into the kernel (`PeerGather`: each
+rank's kernel stores its rows into every rank's output over NVLink and counts itself
+in).  Activations are replicated, so there is no other exchange; no kernel reads
+another GPU's memory.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
-from typing import Callable, Optional
+from typing import Callable, Dict, Optional, Tuple
 
 import torch
 
@@ -74,6 +77,123 @@ def gather_columns(y_local: torch.Tensor, N: int, world: int, rank: int, align: 
     dist.all_gather_into_tensor(recv, send.contiguous(), group=group)
     parts = recv.view(world, M, width)
     return torch.cat([parts[r, :, : n1 - n0] for r, (n0, n1) in enumerate(ranges)], dim=1)
+
+
+class PeerGather:
+    """Output buffers shared by the ranks of a group, for column-parallel linears
+    whose all-gather is fused into the decode kernel (glint_htile_gather_stream).
+
+    Every rank allocates each named output y[M, N] (and a pair of arrival
+    counters) with glint_device_alloc, the CUDA IPC handles are exchanged once over
+    the process group, and every rank maps every other rank's buffers.  A gathered
+    call computes this rank's rows and stores them into all ranks' y over NVLink;
+    when it completes on the stream, the local y holds every rank's rows, with no
+    NCCL call and no copy.  All ranks must make the same gathered calls in the
+    same order; a rank that skips one makes the others give up after about a
+    second with glint_kernel_error() set.  A gathered call may be captured in a
+    CUDA graph and replayed (the completion count needs no call number).  Each output has two buffers used in turn, so a
+    result stays valid until the second-next call with that name: a rank can only
+    start that call once every rank has started the next one, which each rank
+    enqueues after its reads of this result.  No multicast objects are created."""
+
+    def __init__(self, outputs: Dict[str, Tuple[int, int, torch.dtype]], world: int, rank: int, group=None):
+        import torch.distributed as dist
+        from . import glint_cuda
+        from .streamer import device_bytes
+        self._lib = lib = glint_cuda._require()
+        self.world, self.rank = world, rank
+        self._local, self._opened = [], []
+        self.y: Dict[str, list] = {}
+        self._yptrs: Dict[str, list] = {}
+        self._calls: Dict[str, int] = {}
+        self.shapes = dict(outputs)
+
+        def alloc(nbytes):
+            p = ctypes.c_void_p()
+            rc = lib.glint_device_alloc(nbytes, ctypes.byref(p))
+            if rc != 0:
+                raise RuntimeError(f"glint_device_alloc rc={rc}")
+            self._local.append(p.value)
+            h = ctypes.create_string_buffer(64)
+            rc = lib.glint_ipc_handle(p, h)
+            if rc != 0:
+                raise RuntimeError(f"glint_ipc_handle rc={rc}")
+            return p.value, h.raw
+
+        keys = [(nm, b) for nm in sorted(outputs) for b in (0, 1)]
+        mine = {}
+        for nm, b in keys:
+            M, N, dt = outputs[nm]
+            esz = torch.empty((), dtype=dt).element_size()
+            ptr, h = alloc(M * N * esz)
+            mine[f"{nm}/{b}"] = (ptr, h)
+            self.y.setdefault(nm, []).append(device_bytes(ptr, M * N * esz).view(dt).view(M, N))
+        fptr, fh = alloc(256)
+        mine["__flags__"] = (fptr, fh)
+        every = [None] * world
+        dist.all_gather_object(every, {k: v[1] for k, v in mine.items()}, group=group)
+
+        def mapped(key):
+            arr = (ctypes.c_void_p * world)()
+            for r in range(world):
+                if r == rank:
+                    arr[r] = mine[key][0]
+                    continue
+                p = ctypes.c_void_p()
+                rc = lib.glint_ipc_open(every[r][key], ctypes.byref(p))
+                if rc != 0:
+                    raise RuntimeError(f"glint_ipc_open rc={rc} (rank {r}, {key})")
+                self._opened.append(p.value)
+                arr[r] = p.value
+            return arr
+
+        for nm, b in keys:
+            self._yptrs.setdefault(nm, []).append(mapped(f"{nm}/{b}"))
+            self._calls[nm] = 0
+        self._flags = mapped("__flags__")
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+
+    @staticmethod
+    def supported(M: int, rows: int) -> bool:
+        """Shapes the gathered kernel covers (the decode kernels, M <= 16; also
+        bs == 64 and K % 256 == 0, as for the decode path)."""
+        return 1 <= M <= 16 and rows >= 1
+
+    def linear(self, x: torch.Tensor, sh: ColumnShard, name: str, mode: str = "fast", stream=None) -> torch.Tensor:
+        """y[M, N] = x . W^T on every rank: this rank's rows [n0, n1) computed here,
+        the others' written by their ranks.  Returns one of the name's two shared
+        local buffers (valid once the call completes on the stream, until the
+        second-next call with the same name)."""
+        M, N, dt = self.shapes[name]
+        if x.shape[0] != M or sh.N != N:
+            raise ValueError("output shape differs from the buffer's")
+        buf = self._calls[name] & 1
+        ydt = 1 if dt == torch.bfloat16 else 0
+        s = stream if stream is not None else torch.cuda.current_stream()
+        rc = self._lib.glint_htile_gather_stream(
+            sh.hole.data_ptr(), sh.plug.data_ptr(), sh.absmax.data_ptr(), x.data_ptr(), self._yptrs[name][buf],
+            self._flags, self.world, self.rank, ydt, M, sh.rows, sh.K, N, sh.n0, sh.blocksize,
+            1 if mode == "fast" else 0, ctypes.c_void_p(s.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(f"glint_htile_gather_stream rc={rc}")
+        self._calls[name] += 1
+        return self.y[name][buf]
+
+    def close(self, group=None) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank is done with them)."""
+        import torch.distributed as dist
+        if not self._local:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        for p in self._opened:
+            self._lib.glint_ipc_close(ctypes.c_void_p(p))
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        for p in self._local:
+            self._lib.glint_device_free(ctypes.c_void_p(p))
+        self._local, self._opened, self.y = [], [], {}
 
 
 def column_parallel(x: torch.Tensor, sh: ColumnShard, world: int, rank: int, mode: str = "fast",

@@ -61,6 +61,38 @@ int glint_htile_stream_noalloc(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
     const __nv_bfloat16 *d_x, void *d_y, int y_dtype,
     int M, int N, int K, int blocksize, int mode, cudaStream_t stream);
+
+/* Column-parallel decode with the all-gather fused in (one process per GPU; no
+ * counterpart in the reference, which runs on one device).  This rank holds rows
+ * [n0, n0 + N) of a weight with ld_y rows in all; the call computes them and
+ * stores them straight into every rank's y[M, ld_y] (d_y_ranks[r]: rank r's
+ * buffer as mapped in this process, this rank's own at d_y_ranks[rank]) over
+ * NVLink, then signals every rank (d_flag_ranks[r]: rank r's counters, 9
+ * zero-initialised uint32 per rank) and waits for one signal from every rank.
+ * When the call completes on `stream`, this rank's y holds every rank's rows.
+ * Every rank must make every gathered call of the group, in the same order (a
+ * missing rank makes the others give up after about a second with
+ * glint_kernel_error() = 1); the same launch may be replayed in a CUDA graph.
+ * Peer buffers come from glint_device_alloc and are shared with
+ * glint_ipc_handle / glint_ipc_open.
+ * Covers 1 <= M <= 16, bs == 64, K % 256 == 0, 16-byte aligned operands,
+ * world <= 8; else GLINT_ERR_UNSUPPORTED.  The calls of a group go on one stream
+ * per rank. */
+#define GLINT_ERR_UNSUPPORTED (-6)
+int glint_htile_gather_stream(
+    const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
+    const __nv_bfloat16 *d_x, void *const *d_y_ranks, unsigned int *const *d_flag_ranks,
+    int world, int rank, int y_dtype, int M, int N, int K, int ld_y, int n0,
+    int blocksize, int mode, cudaStream_t stream);
+/* Zero-initialised device memory that can be shared with other processes
+ * (cudaMalloc'd, so glint_ipc_handle covers exactly this range). */
+int glint_device_alloc(size_t bytes, void **d_ptr);
+int glint_device_free(void *d_ptr);
+/* CUDA IPC: a 64-byte handle for a glint_device_alloc pointer, and its mapping in
+ * another process on the same node (peer access enabled on open). */
+int glint_ipc_handle(const void *d_ptr, void *handle_out);
+int glint_ipc_open(const void *handle, void **d_ptr);
+int glint_ipc_close(void *d_ptr);
 #ifdef __cplusplus
 }
 #endif

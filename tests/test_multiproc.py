@@ -132,3 +132,55 @@ def test_column_parallel_nccl_two_gpus():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.spawn(_nccl_worker, args=(2, _free_port(), 4096, 4096, 4), nprocs=2, join=True)
+
+
+def _gather_worker(rank, world, port):
+    import os
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist = _init(rank, world, port, backend="nccl")
+    from glint_b200 import device as D
+    from glint_b200 import glint_cuda
+    from glint_b200 import tp
+    L = glint_cuda.load()
+    L.glint_kernel_error(1)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(31)  # the same weights and activations on every rank
+    # 4096 rows per rank run the row-owned decode, 1024 the stream-K decode
+    for N, K in [(8192, 4096), (2048, 4096)]:
+        w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        hole, plug, am = D.encode(w, 64)
+        sh = tp.ColumnShard.from_full(hole, plug, am, N, K, 64, rank, world)
+        for M, dt, mode, tol in [(1, torch.float32, "precise", 1e-5), (4, torch.bfloat16, "fast", 1e-2),
+                                 (16, torch.float32, "fast", 1e-2)]:
+            pg = tp.PeerGather({"y": (M, N, dt)}, world, rank)
+            for _ in range(3):  # consecutive calls alternate the buffers and reuse the counters
+                x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+                y = pg.linear(x, sh, "y", mode=mode)
+                ref = D.htile(x, hole, plug, am, N, 64, mode=mode, out_dtype=dt)
+                torch.cuda.synchronize()
+                err = float((y.float() - ref.float()).abs().max() / max(1.0, float(ref.float().abs().max())))
+                assert err <= tol, (N, M, mode, err)
+            pg.close()
+    assert L.glint_kernel_error(1) == 0
+    N, K = sh.N, sh.K
+    # a rank that skips a gathered call: the other's kernel gives up after about a
+    # second with the error word set, instead of hanging
+    pg = tp.PeerGather({"y": (1, N, torch.float32)}, world, rank)
+    if rank == 0:
+        x = torch.randn((1, K), generator=g, device="cuda").to(torch.bfloat16)
+        pg.linear(x, sh, "y")
+        torch.cuda.synchronize()
+        assert L.glint_kernel_error(1) == 1
+    pg.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_gathered_decode_two_gpus():
+    """Column-parallel decode with the all-gather fused into the kernel (peer
+    stores over NVLink, CUDA IPC buffers): every rank ends with the whole y, equal
+    to the one-GPU decode within the precise / fast bounds, over repeated calls."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_gather_worker, args=(2, _free_port()), nprocs=2, join=True)
