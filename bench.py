@@ -469,17 +469,17 @@ def bench_tp_decode(args, world, rank, pk, M: int = 1):
         torch.cuda.synchronize()
         return us
 
-    us_nccl = timed(layer_nccl)
     res = {"model": "Llama-3-70B layer (configs[4] shapes)", "tp": world, "batch": M,
            "weight_bytes_per_gpu_per_layer": int(local_bytes), "kernels_per_layer": 7,
            "timing": "one layer in a CUDA graph (decode kernels + gathers), replayed; max over ranks"}
     if pg is not None:
-        us = timed(layer_fused)
+        us = timed(layer_fused)  # first: the fused layer is not measured behind the all-NCCL graph
         pg.close()
+        us_nccl = timed(layer_nccl)
         res.update({"us_per_layer": round(us, 2), "gathers": "fused into o/gate/up/down decode (peer stores) + 1 NCCL",
                     "us_per_layer_nccl_gathers": round(us_nccl, 2)})
     else:
-        us = us_nccl
+        us = timed(layer_nccl)
         res.update({"us_per_layer": round(us, 2), "gathers": "none (one GPU)"})
     res.update({"tokens_per_s_80_layers": round(M / (80 * us * 1e-6), 1),
                 "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4)})
