@@ -76,6 +76,29 @@ def test_bad_arguments_rejected_without_gpu(lib):
     assert lib.glint_htile_stream(p, p, p, p, p, 0, 1, 1, 1, 64, 9, None) == -1   # bad mode
 
 
+def test_gathered_decode_and_ipc_reject_bad_arguments_without_gpu(lib):
+    """glint_htile_gather_stream and the IPC helpers check their arguments before
+    touching a device (include/glint_htile.h; -1 bad argument, -2 blocksize)."""
+    buf = (ctypes.c_uint8 * 64)()
+    p = ctypes.addressof(buf)
+    ptrs = (ctypes.c_void_p * 2)(p, p)
+    nul = (ctypes.c_void_p * 2)(p, None)
+    g = lib.glint_htile_gather_stream
+    assert g(None, p, p, p, ptrs, ptrs, 2, 0, 0, 1, 64, 256, 128, 0, 64, 1, None) == -1   # null plane
+    assert g(p, p, p, p, nul, ptrs, 2, 0, 0, 1, 64, 256, 128, 0, 64, 1, None) == -1       # null peer y
+    assert g(p, p, p, p, ptrs, nul, 2, 0, 0, 1, 64, 256, 128, 0, 64, 1, None) == -1       # null peer counters
+    assert g(p, p, p, p, ptrs, ptrs, 2, 2, 0, 1, 64, 256, 128, 0, 64, 1, None) == -1      # rank >= world
+    assert g(p, p, p, p, ptrs, ptrs, 2, 0, 5, 1, 64, 256, 128, 0, 64, 1, None) == -1      # bad y dtype
+    assert g(p, p, p, p, ptrs, ptrs, 2, 0, 0, 1, 64, 256, 128, 0, 64, 7, None) == -1      # bad mode
+    assert g(p, p, p, p, ptrs, ptrs, 2, 0, 0, 1, 64, 256, 128, 0, 0, 1, None) == -2       # blocksize
+    assert g(p, p, p, p, ptrs, ptrs, 2, 0, 0, 1, 64, 256, 100, 64, 64, 1, None) == -1     # rows past ld_y
+    q = ctypes.c_void_p()
+    assert lib.glint_device_alloc(0, ctypes.byref(q)) == -1
+    assert lib.glint_ipc_handle(None, p) == -1
+    assert lib.glint_ipc_open(None, ctypes.byref(q)) == -1
+    assert lib.glint_ipc_close(None) == -1
+
+
 def test_glint_cuda_mirror_interface():
     """Same public names and signatures as the reference's glint_cuda.py:1-85."""
     import inspect
