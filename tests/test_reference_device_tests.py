@@ -1,0 +1,28 @@
+"""The reference's own H-TILE device tests, run against this library.
+
+oracle/Makefile compiles tests/test_glint_htile.cu and
+tests/test_htile_k_bounds_device.cu of the reference (Jadon-Fox/glint) where they
+lie and links them against glint_b200/libglint_encode.so (runpath), so
+launch_glint_htile_s3_f32 there is this repository's.  They check y against their
+own host double-precision products within 1e-5 (1 + |y|) and 1e-3, with unaligned
+pointers, odd K, blocksizes that straddle rows, M and N below a tile, and guard
+canaries around y (test_htile_k_bounds_device.cu:40-118).  The binaries are built
+where the reference checkout exists and travel prebuilt."""
+import subprocess
+from pathlib import Path
+
+import pytest
+
+REF = Path(__file__).resolve().parents[1] / "oracle" / "_ref"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,marker", [("test_glint_htile", "ALL 10 TESTS PASSED GREEN."),
+                                         ("test_htile_k_bounds_device", "independent_matmul=PASS")])
+def test_reference_device_test_passes_on_this_library(name, marker):
+    exe = REF / name
+    if not exe.is_file():
+        pytest.skip(f"{exe} not built (needs the reference checkout at build time)")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert marker in r.stdout, r.stdout[-2000:]
