@@ -1,9 +1,12 @@
-"""The reference's own H-TILE device tests, run against this library.
+"""The reference's own device tests, run against this library.
 
-oracle/Makefile compiles tests/test_glint_htile.cu and
-tests/test_htile_k_bounds_device.cu of the reference (Jadon-Fox/glint) where they
-lie and links them against glint_b200/libglint_encode.so (runpath), so
-launch_glint_htile_s3_f32 there is this repository's.  They check y against their
+oracle/Makefile compiles tests/test_glint_htile.cu,
+tests/test_htile_k_bounds_device.cu and tests/test_glint_plug_streamer.cu of the
+reference (Jadon-Fox/glint) where they lie, against the reference's headers, and
+links them to glint_b200/libglint_encode.so (runpath), so the H-TILE and streamer
+entry points they call are this repository's.  The streamer test reads only its
+own layer's bytes over delayed passes and checks the call-order codes
+(test_glint_plug_streamer.cu:1-125); the H-TILE tests check y against their
 own host double-precision products within 1e-5 (1 + |y|) and 1e-3, with unaligned
 pointers, odd K, blocksizes that straddle rows, M and N below a tile, and guard
 canaries around y (test_htile_k_bounds_device.cu:40-118).  The binaries are built
@@ -18,7 +21,8 @@ REF = Path(__file__).resolve().parents[1] / "oracle" / "_ref"
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,marker", [("test_glint_htile", "ALL 10 TESTS PASSED GREEN."),
-                                         ("test_htile_k_bounds_device", "independent_matmul=PASS")])
+                                         ("test_htile_k_bounds_device", "independent_matmul=PASS"),
+                                         ("test_glint_plug_streamer", "PASS: 0 failed checks")])
 def test_reference_device_test_passes_on_this_library(name, marker):
     exe = REF / name
     if not exe.is_file():
