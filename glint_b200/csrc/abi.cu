@@ -33,7 +33,8 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr int kSlots = 3;
-constexpr int64_t kChunkWeights = int64_t(1) << 24; /* 16 Mi weights per pipeline chunk */
+constexpr int64_t kChunkWeights = int64_t(1) << 24;    /* at most 16 Mi weights per pipeline chunk */
+constexpr int64_t kMinChunkWeights = int64_t(1) << 21; /* at least 2 Mi (unless the tensor is smaller) */
 
 struct Buffer {
     void *p = nullptr;
@@ -135,7 +136,12 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 int64_t chunk_len(int64_t n, int bs)
 {
     const int64_t unit = (int64_t)bs / gcd64(bs, 512) * 512;
-    int64_t c = std::max(unit, kChunkWeights / unit * unit);
+    /* about eight chunks per tensor, 2-16 Mi weights each: the copy-in, kernel and
+     * copy-out of neighbouring chunks overlap, so only ~1/8 of a mid-size tensor's
+     * transfer is left unoverlapped at its start and end (one 33 MB chunk left all
+     * of it); below 2 Mi weights the per-chunk call overhead would dominate */
+    const int64_t target = std::min(kChunkWeights, std::max(kMinChunkWeights, (n + 7) / 8));
+    const int64_t c = std::max(unit, (target + unit - 1) / unit * unit);
     const int64_t need = (n + unit - 1) / unit * unit;
     return std::min(c, need);
 }
