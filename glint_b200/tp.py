@@ -97,16 +97,24 @@ class PeerGather:
     enqueues after its reads of this result.  No multicast objects are created."""
 
     def __init__(self, outputs: Dict[str, Tuple[int, int, torch.dtype]], world: int, rank: int, group=None):
-        import torch.distributed as dist
         from . import glint_cuda
         from .streamer import device_bytes
-        self._lib = lib = glint_cuda._require()
+        self._lib = glint_cuda._require()
         self.world, self.rank = world, rank
         self._local, self._opened = [], []
         self.y: Dict[str, list] = {}
         self._yptrs: Dict[str, list] = {}
         self._calls: Dict[str, int] = {}
         self.shapes = dict(outputs)
+        try:
+            self._setup(outputs, group, device_bytes)
+        except Exception:
+            self._release()
+            raise
+
+    def _setup(self, outputs, group, device_bytes) -> None:
+        import torch.distributed as dist
+        lib, world, rank = self._lib, self.world, self.rank
 
         def alloc(nbytes):
             p = ctypes.c_void_p()
@@ -168,6 +176,8 @@ class PeerGather:
         M, N, dt = self.shapes[name]
         if x.shape[0] != M or sh.N != N:
             raise ValueError("output shape differs from the buffer's")
+        if not x.is_cuda or x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != sh.K or not x.is_contiguous():
+            raise ValueError("x must be a contiguous bfloat16 CUDA tensor [M, K]")
         buf = self._calls[name] & 1
         ydt = 1 if dt == torch.bfloat16 else 0
         s = stream if stream is not None else torch.cuda.current_stream()
@@ -189,8 +199,15 @@ class PeerGather:
         dist.barrier(group=group)
         for p in self._opened:
             self._lib.glint_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
         torch.cuda.synchronize()
         dist.barrier(group=group)
+        self._release()
+
+    def _release(self) -> None:
+        """Unmap and free without synchronising with the other ranks (set-up failure)."""
+        for p in self._opened:
+            self._lib.glint_ipc_close(ctypes.c_void_p(p))
         for p in self._local:
             self._lib.glint_device_free(ctypes.c_void_p(p))
         self._local, self._opened, self.y = [], [], {}
