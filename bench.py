@@ -481,8 +481,11 @@ def bench_tp_decode(args, world, rank, pk, M: int = 1):
     else:
         us = timed(layer_nccl)
         res.update({"us_per_layer": round(us, 2), "gathers": "none (one GPU)"})
+    from glint_b200 import glint_cuda
     res.update({"tokens_per_s_80_layers": round(M / (80 * us * 1e-6), 1),
-                "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4)})
+                "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
+                # nonzero if any bounded wait (pipeline barrier or gather arrival) ran out
+                "kernel_error": int(max_over_ranks(world, float(glint_cuda.load().glint_kernel_error(1))))})
     return res
 
 
