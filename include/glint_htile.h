@@ -17,17 +17,25 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+/* BF16 activations are passed by pointer.  C++ (CUDA) callers see exactly the
+ * reference's __nv_bfloat16; cuda_bf16.h declares that type for C++ only, so C
+ * translation units get its 16-bit storage struct, which has the same layout. */
+#ifdef __cplusplus
+typedef __nv_bfloat16 glint_bf16_t;
+#else
+typedef __nv_bfloat16_raw glint_bf16_t;
+#endif
 #ifdef __cplusplus
 extern "C" {
 #endif
 int launch_glint_htile_s3_f32_stream(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
-    const __nv_bfloat16 *d_x, float *d_y,
+    const glint_bf16_t *d_x, float *d_y,
     int M, int N, int K, int blocksize, cudaStream_t stream);
 /* Same on the legacy default stream. */
 int launch_glint_htile_s3_f32(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
-    const __nv_bfloat16 *d_x, float *d_y,
+    const glint_bf16_t *d_x, float *d_y,
     int M, int N, int K, int blocksize);
 
 /* ---- additive (no counterpart in the reference ABI) ----------------------- */
@@ -41,7 +49,7 @@ int launch_glint_htile_s3_f32(
 #define GLINT_HTILE_FAST 1
 int glint_htile_stream(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
-    const __nv_bfloat16 *d_x, void *d_y, int y_dtype,
+    const glint_bf16_t *d_x, void *d_y, int y_dtype,
     int M, int N, int K, int blocksize, int mode, cudaStream_t stream);
 
 /* Same contract as glint_htile_stream for decode shapes, for callers that cannot
@@ -59,7 +67,7 @@ int glint_htile_stream(
 #define GLINT_ERR_SCRATCH (-5)
 int glint_htile_stream_noalloc(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
-    const __nv_bfloat16 *d_x, void *d_y, int y_dtype,
+    const glint_bf16_t *d_x, void *d_y, int y_dtype,
     int M, int N, int K, int blocksize, int mode, cudaStream_t stream);
 
 /* Column-parallel decode with the all-gather fused in (one process per GPU; no
@@ -81,7 +89,7 @@ int glint_htile_stream_noalloc(
 #define GLINT_ERR_UNSUPPORTED (-6)
 int glint_htile_gather_stream(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,
-    const __nv_bfloat16 *d_x, void *const *d_y_ranks, unsigned int *const *d_flag_ranks,
+    const glint_bf16_t *d_x, void *const *d_y_ranks, unsigned int *const *d_flag_ranks,
     int world, int rank, int y_dtype, int M, int N, int K, int ld_y, int n0,
     int blocksize, int mode, cudaStream_t stream);
 /* Zero-initialised device memory that can be shared with other processes

@@ -99,6 +99,21 @@ def test_gathered_decode_and_ipc_reject_bad_arguments_without_gpu(lib):
     assert lib.glint_ipc_close(None) == -1
 
 
+def test_headers_compile_and_link_from_plain_c(lib, tmp_path):
+    """Every public header compiles in a C11 translation unit and the library links
+    from C (tests/native/abi_from_c.c); the device-free helpers answer."""
+    import shutil
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc absent")
+    exe = tmp_path / "abi_from_c"
+    cuda_inc = "/usr/local/cuda/include"
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", f"-I{cuda_inc}", "-o", str(exe),
+                    str(ROOT / "tests" / "native" / "abi_from_c.c"), f"-L{ROOT / 'glint_b200'}", "-lglint_encode",
+                    f"-Wl,-rpath,{ROOT / 'glint_b200'}"], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and r.stdout.strip() == "OK", r.stdout + r.stderr
+
+
 def test_glint_cuda_mirror_interface():
     """Same public names and signatures as the reference's glint_cuda.py:1-85."""
     import inspect
