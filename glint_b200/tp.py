@@ -178,6 +178,10 @@ class PeerGather:
             raise ValueError("output shape differs from the buffer's")
         if not x.is_cuda or x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != sh.K or not x.is_contiguous():
             raise ValueError("x must be a contiguous bfloat16 CUDA tensor [M, K]")
+        if sh.rows < 1:
+            # every rank signals every gathered call; a rank without rows cannot, and its
+            # peers would give up after about a second
+            raise ValueError("a gathered call needs at least one row on every rank (N >= 16 x world)")
         buf = self._calls[name] & 1
         ydt = 1 if dt == torch.bfloat16 else 0
         s = stream if stream is not None else torch.cuda.current_stream()
