@@ -560,10 +560,18 @@ constexpr int r_ring() { return (MT == 1 ? 4 : 3) * (2 * kRowBlockMax * 128 + 20
 /* partial sums exchanged at a row block's end: T * (KH - 1) <= 14 warps x 32 lanes */
 template <int MT>
 constexpr int r_scratch_floats() { return (MT <= 2 ? 14 : 7) * 32 * 4 * MT; }
+/* one unit of a shared tail tile (MT <= 2): hole and plug 16 x 128 B, absmax
+ * 16 x 16 B in 1 KB, four activation boxes, and the partial sums of 3 of the 4
+ * warps that share it (32 lanes x 4 MT floats each) */
+constexpr int kTailWarps = 4;
+constexpr int kTailX = 5 * 1024; /* offset of the activation boxes */
+template <int MT>
+constexpr int r_tail_bytes() { return MT <= 2 ? kTailX + r_xsub<MT>() + 3 * 32 * 4 * MT * 4 : 0; }
 template <int MT>
 constexpr int r_smem_bytes()
 {
-    return kLutBytes + 1024 + r_ring<MT>() + r_scratch_floats<MT>() * 4 + 8 * (2 * kRMaxStages + 2) + 64;
+    return kLutBytes + 1024 + r_ring<MT>() + r_tail_bytes<MT>() + r_scratch_floats<MT>() * 4 +
+           8 * (2 * kRMaxStages + 3) + 64;
 }
 
 struct RowArgs {
@@ -583,28 +591,45 @@ struct RowArgs {
     int xrows; /* activation rows per box: min(M, 8 MT) */
     uint32_t tx; /* TMA bytes per stage */
     GatherArgs ga;
+    /* Shared tail: when the 16-row tiles do not divide evenly over the SMs, every
+     * CTA owns R = 16 * floor(tiles / SMs) rows and the leftover tiles, from row
+     * tail_row0, are cut into 16-row x 256-k units: CTA c < tail_units takes unit
+     * c % KU of tile c / KU on kTailWarps otherwise idle warps, stores its partial
+     * sum in tail_ws[c], and the last of a tile's KU CTAs (tail_cnt) adds the KU
+     * partials in unit order and writes y.  0 tail units: off. */
+    int tail_units;
+    int tail_row0;
+    uint32_t tail_tx;
+    float *tail_ws;
+    int *tail_cnt;
 };
 
 template <int MT, bool SPLIT, bool BF16OUT, int NB>
 __global__ void __launch_bounds__(kThreads, 1)
     htile_rows_kernel(const __grid_constant__ CUtensorMap hmap, const __grid_constant__ CUtensorMap pmap,
-                      const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap xmap, const RowArgs a)
+                      const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap xmap,
+                      const __grid_constant__ CUtensorMap hmap16, const __grid_constant__ CUtensorMap pmap16,
+                      const __grid_constant__ CUtensorMap amap16, const RowArgs a)
 {
     static_assert(r_smem_bytes<MT>() <= 232448, "shared memory");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem_raw);
     uint8_t *ring = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) & ~uintptr_t(1023));
-    float *scratch = reinterpret_cast<float *>(ring + r_ring<MT>());
+    uint8_t *tail = ring + r_ring<MT>(); /* 1 KB aligned: the ring is a multiple of 1 KB */
+    float *scratch = reinterpret_cast<float *>(tail + r_tail_bytes<MT>());
     uint64_t *full = reinterpret_cast<uint64_t *>(scratch + r_scratch_floats<MT>());
     uint64_t *empty = full + kRMaxStages;
     uint64_t *cmb_full = empty + kRMaxStages; /* a row block's KH-1 partials per tile are in scratch */
     uint64_t *cmb_empty = cmb_full + 1;       /* the tile owners have read them */
-    uint32_t *cta_done = reinterpret_cast<uint32_t *>(cmb_empty + 1); /* gathered calls: warps done */
+    uint64_t *tail_full = cmb_empty + 1;      /* the tail unit's planes, absmax and activations landed */
+    uint32_t *cta_done = reinterpret_cast<uint32_t *>(tail_full + 1); /* gathered calls: warps done */
     const int S = a.S, KH = a.KH;
     const int stage_bytes = a.UB * a.sub;
 
     const int active = a.T * KH;
+    const bool has_tail = MT <= 2 && (int)blockIdx.x < a.tail_units;
+    const int tail_tile = (int)blockIdx.x / a.KU, tail_ku = (int)blockIdx.x % a.KU;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -612,6 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(cmb_full, KH > 1 ? a.T * (KH - 1) : 1);
         mbar_init(cmb_empty, a.T);
+        mbar_init(tail_full, 1);
         *cta_done = 0u;
         mbar_init_fence();
     }
@@ -638,6 +664,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_2d(xs + c * (8 * MT * 128), &xmap, &full[s], (ku * a.UB + sb) * 256 + c * 64, 0);
                 }
             };
+            /* the tail unit first, so its warps work beside the row blocks (one
+             * 256-k slice: the ring's units have UB == 1 whenever a tail is set) */
+            if (has_tail) {
+                const int n16 = a.tail_row0 + tail_tile * 16;
+                mbar_expect_tx(tail_full, a.tail_tx);
+                tma_load_2d(tail, &hmap16, tail_full, tail_ku * 128, n16);
+                tma_load_2d(tail + 2048, &pmap16, tail_full, tail_ku * 128, n16);
+                tma_load_2d(tail + 4096, &amap16, tail_full, tail_ku * 4, n16);
+            }
             bool ok = true;
             int i = 0, s = 0, blk = 0, ku = 0;
             uint32_t ph = 0;
@@ -660,6 +695,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     /* weights stream before the previous kernel is done, activations after
                      * (programmatic dependent launch; a no-op otherwise) */
                     asm volatile("griddepcontrol.wait;" ::: "memory");
+                    if (has_tail) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            tma_load_2d(tail + kTailX + c * (8 * MT * 128), &xmap, tail_full, tail_ku * 256 + c * 64, 0);
+                    }
                     for (int j = 0; j <= i; ++j)
                         load_x(j % a.KU, j);
                 }
@@ -673,6 +713,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = i > S ? i - S : 0; j < i; ++j)
                     if (!mbar_wait_bounded(&full[j % S], (uint32_t)(j / S) & 1u, &g_decode_error))
                         break;
+                if (has_tail)
+                    mbar_wait_bounded(tail_full, 0u, &g_decode_error);
             }
         }
         return;
@@ -687,13 +729,99 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (warp >= active)
+    const int g = (int)(lane >> 2), t = (int)(lane & 3), pg = frag_row<128>(g);
+    const uint32_t lut_base = saddr(lut), lane4 = lane * 4u;
+    if (warp >= active) {
+        /* tail warp j: 64-k block j of the tail unit; warp 0 of them adds the four
+         * in block order, publishes the unit's partial and, as the tile's last
+         * unit, adds the tile's KU partials in unit order.  No waits on other CTAs:
+         * a failed TMA wait still publishes (zeros), so the count stays whole. */
+        const int j = warp - active;
+        if (!has_tail || j >= kTailWarps)
+            return;
+        float acc[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+            acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+        const bool ok = lane == 0 ? mbar_wait_suspend_bounded(tail_full, 0u, &g_decode_error) : true;
+        const uint32_t ts = saddr(tail);
+        if (__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
+            tile_block<MT, SPLIT, 128>(ts, ts + 2048, ts + 4096, (uint32_t)j,
+                                       ts + (uint32_t)(kTailX + j * (8 * MT * 128)), j, 0, g, t, lut_base, lane4,
+                                       a.M, acc);
+        float4 *part = reinterpret_cast<float4 *>(tail + kTailX + r_xsub<MT>());
+        if (j > 0) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+                part[((j - 1) * 32 + (int)lane) * MT + mt] = make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
+        }
+        asm volatile("bar.sync 2, %0;" ::"n"(kTailWarps * 32) : "memory");
+        if (j > 0)
+            return;
+#pragma unroll
+        for (int jj = 1; jj < kTailWarps; ++jj)
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const float4 v = part[((jj - 1) * 32 + (int)lane) * MT + mt];
+                acc[mt][0] += v.x, acc[mt][1] += v.y, acc[mt][2] += v.z, acc[mt][3] += v.w;
+            }
+        float4 *ws = reinterpret_cast<float4 *>(a.tail_ws);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+            __stcg(ws + ((int64_t)blockIdx.x * 32 + lane) * MT + mt,
+                   make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]));
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0)
+            last = atomicAdd(a.tail_cnt + tail_tile, 1) == a.KU - 1;
+        if (!__shfl_sync(0xFFFFFFFFu, last, 0))
+            return;
+        __threadfence();
+        float sum[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+            sum[mt][0] = sum[mt][1] = sum[mt][2] = sum[mt][3] = 0.f;
+        const int64_t u0 = (int64_t)tail_tile * a.KU;
+        for (int u = 0; u < a.KU; u += 8) {
+            /* eight units' loads in flight at once, added in unit order */
+            float4 v[8][MT];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                    v[q][mt] = u + q < a.KU ? __ldcg(ws + ((u0 + u + q) * 32 + lane) * MT + mt)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (u + q < a.KU) {
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                        sum[mt][0] += v[q][mt].x, sum[mt][1] += v[q][mt].y;
+                        sum[mt][2] += v[q][mt].z, sum[mt][3] += v[q][mt].w;
+                    }
+                }
+        }
+        if (lane == 0)
+            a.tail_cnt[tail_tile] = 0; /* every unit has arrived: zero for the next call */
+        const int n16 = a.tail_row0 + tail_tile * 16;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int n = n16 + pg + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
+                if (n < a.N && col < a.M) {
+                    if (BF16OUT)
+                        static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(sum[mt][q]);
+                    else
+                        static_cast<float *>(a.y)[(int64_t)col * a.N + n] = sum[mt][q];
+                }
+            }
         return;
+    }
 
     /* warp kh takes the unit's 64-k blocks [kh*NB, (kh+1)*NB) (block b: slice b/4, block b%4) */
-    const int tile = warp / KH, kh = warp % KH, b0 = kh * NB;
-    const int g = (int)(lane >> 2), t = (int)(lane & 3), r0 = tile * 16, pg = frag_row<128>(g);
-    const uint32_t lut_base = saddr(lut), lane4 = lane * 4u;
+    const int tile = warp / KH, kh = warp % KH, b0 = kh * NB, r0 = tile * 16;
     float acc[MT][4];
     bool alive = true;
     int s = 0;
@@ -859,6 +987,7 @@ bool get_scratch(cudaStream_t st, size_t ws_floats, size_t n_counters, Scratch &
 
 struct Maps {
     CUtensorMap h, p, am, x;
+    CUtensorMap h16, p16, am16; /* 16-row boxes: the row-owned kernel's shared tail */
 };
 
 /* Launched with programmatic stream serialisation (PDL): the kernel may start
@@ -915,7 +1044,7 @@ int launch_rows_nb(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, b
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (cudaLaunchKernelEx(&cfg, kern, m.h, m.p, m.am, m.x, a) != cudaSuccess) {
+    if (cudaLaunchKernelEx(&cfg, kern, m.h, m.p, m.am, m.x, m.h16, m.p16, m.am16, a) != cudaSuccess) {
         cudaGetLastError();
         return kLaunch;
     }
@@ -934,20 +1063,11 @@ int launch_rows_t(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bo
 
 constexpr int align1k(int v) { return (v + 1023) & ~1023; }
 
-/* the row-owned kernel for N >= 16 x SMs: no workspace, no split rows */
-int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
-                OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st, bool pdl,
-                const GatherArgs *gt = nullptr)
+/* Row block, warp and ring layout of the row-owned kernel for R rows per CTA. */
+bool plan_rows(RowArgs &a, int R, int MT)
 {
-    const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
-    const int sms = sm_count();
-    const int g0 = std::max(1, std::min(sms, (N + 15) / 16));
-    RowArgs a{};
-    a.y = y, a.M = M, a.N = N, a.K = K;
-    if (gt)
-        a.ga = *gt;
-    a.R = (N + g0 - 1) / g0;
-    const int grid = (N + a.R - 1) / a.R;
+    const int M = a.M, K = a.K;
+    a.R = R;
     a.nb = (a.R + kRowBlockMax - 1) / kRowBlockMax;
     a.RB = (a.R + a.nb - 1) / a.nb;
     a.T = (a.RB + 15) / 16;
@@ -968,7 +1088,7 @@ int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const
         a.KH = blocks / nbk;
     }
     if (a.T * a.KH > kConsumers || a.T * (a.KH - 1) > scratch_warps || nbk > 2)
-        return kLaunch;
+        return false;
     a.KU = K / (256 * a.UB);
     a.xrows = std::min(M, 8 * MT);
     a.pt = align1k(a.RB * 128);
@@ -977,8 +1097,50 @@ int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const
     const int ring = MT == 1 ? r_ring<1>() : MT == 2 ? r_ring<2>() : r_ring<4>();
     a.S = std::min(kRMaxStages, ring / (a.UB * a.sub));
     if (a.S < 2)
-        return kLaunch;
+        return false;
     a.tx = (uint32_t)(a.UB * (2 * a.RB * 128 + a.RB * 16 + 4 * a.xrows * 128));
+    return true;
+}
+
+/* The row-owned kernel for N >= 16 x SMs.  Where the 16-row tiles leave a
+ * remainder over the SMs (N = 14336: 896 tiles, 6.05 per SM) and it is small
+ * enough for one 256-k unit per CTA, the CTAs own 16 x floor(tiles / SMs) rows
+ * and share the leftover tiles unit by unit on idle warps (`tail`: not for
+ * gathered calls or the fixed-scratch entry), instead of 16 x ceil rows, which
+ * leave most SMs a mostly empty last tile. */
+int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st, bool pdl,
+                const GatherArgs *gt = nullptr, bool tail = false)
+{
+    const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
+    const int sms = sm_count();
+    RowArgs a{};
+    a.y = y, a.M = M, a.N = N, a.K = K;
+    if (gt)
+        a.ga = *gt;
+    int grid = 0;
+    const int tiles = (N + 15) / 16, base = tiles / sms, extra = tiles - base * sms;
+    if (tail && !gt && MT <= 2 && base >= 1 && extra > 0 && (int64_t)extra * (K / 256) <= sms) {
+        RowArgs t = a;
+        if (plan_rows(t, base * 16, MT) && t.UB == 1 && t.T * t.KH + kTailWarps <= kConsumers) {
+            Scratch S;
+            t.tail_units = extra * t.KU;
+            if (get_scratch(st, (size_t)t.tail_units * 32 * 4 * MT, (size_t)extra, S)) {
+                t.tail_row0 = sms * base * 16;
+                t.tail_tx = (uint32_t)(2 * 16 * 128 + 16 * 16 + 4 * t.xrows * 128);
+                t.tail_ws = S.ws;
+                t.tail_cnt = S.counters;
+                a = t;
+                grid = sms;
+            }
+        }
+    }
+    if (!grid) {
+        const int g0 = std::max(1, std::min(sms, tiles));
+        if (!plan_rows(a, (N + g0 - 1) / g0, MT))
+            return kLaunch;
+        grid = (N + a.R - 1) / a.R;
+    }
     Maps maps;
     if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
                   (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -989,6 +1151,17 @@ int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const
         !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
                   (uint32_t)a.xrows, CU_TENSOR_MAP_SWIZZLE_128B))
         return kLaunch;
+    if (a.tail_units) {
+        if (!make_map(&maps.h16, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                      128, 16, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_map(&maps.p16, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                      128, 16, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !make_map(&maps.am16, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N,
+                      (uint64_t)K / 64 * 4, 4, 16, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return kLaunch;
+    } else {
+        maps.h16 = maps.h, maps.p16 = maps.p, maps.am16 = maps.am; /* not read */
+    }
     const bool bf = yk == kOutBF16, pr = mode == kPrecise;
 #define GLINT_ROWS_CASE(mt)                                                                                            \
     if (MT == mt)                                                                                                      \
@@ -1044,7 +1217,7 @@ int decode_launch_impl(const uint8_t *hole, const uint8_t *plug, const float *am
                        OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st, const GatherArgs *gt)
 {
     if (rows_supported(N, K))
-        return launch_rows(hole, plug, am, x, y, yk, M, N, K, mode, st, true, gt);
+        return launch_rows(hole, plug, am, x, y, yk, M, N, K, mode, st, true, gt, gt == nullptr);
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
     Maps maps;
     if (!decode_maps(maps, hole, plug, am, x, M, N, K, MT))

@@ -482,3 +482,38 @@ def test_htile_decode_stream_k_vs_oracle(M, N, K):
     assert rel_err(yp.cpu().numpy(), ref) <= PRECISE_TOL
     assert rel_err(yf.cpu().numpy(), ref) <= FAST_TOL
     assert rel_err(yb.float().cpu().numpy(), ref) <= FAST_TOL
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 14336, 4096), (12, 14336, 4096), (1, 14331, 4096), (16, 14352, 4096),
+                                   (7, 14496, 2048)])
+def test_htile_decode_shared_tail_vs_oracle(M, N, K):
+    """Row-owned decode whose 16-row tiles leave a remainder over the SMs (on 148
+    SMs: 8 or 9 leftover tiles of 256-k units shared by up to 144 CTAs, a ragged
+    last tile at N = 14331): the leftover rows within 1e-5 (precise) and 1e-2 (fast)
+    of the oracle on their own, the whole y too, BF16 y, and bit-identical repeated
+    calls (the shared units are added in unit order, whatever CTA finishes last)."""
+    from glint_b200 import glint_cuda
+    L = glint_cuda.load()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    tiles = (N + 15) // 16
+    row0 = 16 * (tiles // sms) * sms  # first shared row when the tail split applies
+    bits = synth_bf16(N * K, seed=N * 3 + M)
+    ho, po, ao = O.encode_bf16(bits, 64)
+    x = O.f32_to_bf16(np.random.default_rng(M * K + 1).normal(0, 1, M * K).astype(np.float32))
+    ref = O.htile(ho, po, ao, x, M, N, K, 64).astype(np.float64)
+    dev = [torch.from_numpy(a).cuda() for a in (ho, po, ao)]
+    dx = to_dev_bf16(x).view(M, K)
+    for _ in range(2):  # the unit counters are zero again after each call
+        yp = D().htile(dx, *dev, N, 64, mode="precise")
+        yp2 = D().htile(dx, *dev, N, 64, mode="precise")
+        yf = D().htile(dx, *dev, N, 64, mode="fast")
+        yb = D().htile(dx, *dev, N, 64, mode="fast", out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        assert L.glint_kernel_error(1) == 0
+        assert torch.equal(yp, yp2)
+        p, f, b = yp.cpu().numpy(), yf.cpu().numpy(), yb.float().cpu().numpy()
+        assert rel_err(p[:, row0:], ref[:, row0:]) <= PRECISE_TOL, rel_err(p[:, row0:], ref[:, row0:])
+        assert rel_err(f[:, row0:], ref[:, row0:]) <= FAST_TOL
+        assert rel_err(p, ref) <= PRECISE_TOL
+        assert rel_err(f, ref) <= FAST_TOL
+        assert rel_err(b, ref) <= FAST_TOL
