@@ -252,6 +252,10 @@ def bench_glint(args):
 
     # ---- e2e through the reference-facing host ABI (pinned host buffers, PCIe inside the timing)
     result["e2e"] = e2e_encode(ws, args, world)
+    # host copies for the pin-pipeline sub-result: the 8 linears after the embedding (one
+    # layer's 7 and the next q_proj, 235 M weights, 0.47 GB BF16)
+    ws_pin = [(mine[i].name, mine[i].rows, mine[i].cols, ws[i].view(torch.int16).cpu().numpy())
+              for i in range(1, min(len(ws), 9))] if world == 1 else []
     del ws, planes
     torch.cuda.empty_cache()
 
@@ -262,6 +266,12 @@ def bench_glint(args):
     # ---- plugs in host memory, streamed through the two-slot ring (one GPU's PCIe link)
     if world == 1:
         result["plug_stream"] = bench_plug_stream(pk)
+        # ---- the pin pipeline: safetensors on disk -> GLINT pin files (file IO, PCIe, encode, rmse)
+        try:
+            result["pin_pipeline"] = bench_pin(ws_pin)
+        except Exception as e:  # a sub-result; the headline stands without it
+            result["pin_pipeline"] = {"error": f"{type(e).__name__}: {e}"}
+        del ws_pin
     # gpu_launches counts the headline's timed region (encode); the sub-results carry their own counts
     result["expand"]["launches"] = args.steps * len(groups)
     barrier(world)
@@ -269,6 +279,42 @@ def bench_glint(args):
         import torch.distributed as dist
         dist.destroy_process_group()
     return rank, result
+
+
+def bench_pin(tensors):
+    """glint_b200.pin.convert of a two-shard BF16 model written to a temporary
+    directory: wall clock of the second of two conversions (so the source is in the
+    page cache and the pipeline's staging exists), which covers reading the shards,
+    host->device and device->host copies, the GPU encode and rmse, and writing the pin."""
+    import shutil
+    import tempfile
+    from glint_b200 import pin, st_io
+    root = Path(tempfile.mkdtemp(prefix="glint_pin_bench_"))
+    try:
+        src = root / "src"
+        src.mkdir()
+        half = (len(tensors) + 1) // 2
+        names = ["model-00001-of-00002.safetensors", "model-00002-of-00002.safetensors"]
+        weight_map = {}
+        for name, part in zip(names, (tensors[:half], tensors[half:])):
+            st_io.write_file(str(src / name), [(n, "BF16", (r, c), a) for n, r, c, a in part], {"format": "pt"})
+            weight_map.update({n: name for n, _r, _c, _a in part})
+        (src / pin.INDEX_NAME).write_text(json.dumps({"metadata": {}, "weight_map": weight_map}))
+        n_in = sum(a.nbytes for _n, _r, _c, a in tensors)
+        times = []
+        for k in range(2):
+            out = root / f"pin{k}"
+            t = time.perf_counter()
+            got = pin.convert(src, out, BS)
+            times.append(time.perf_counter() - t)
+        out_bytes = sum(p.stat().st_size for p in (root / "pin1").iterdir())
+        return {"gbs_bf16_in": round(n_in / times[-1] / 1e9, 2), "seconds": round(times[-1], 3),
+                "first_run_seconds": round(times[0], 3), "bf16_in_bytes": n_in, "pin_bytes": out_bytes,
+                "linears": got["pin"]["n_converted"], "rmse_max": got["pin"]["rmse_max"],
+                "sample": f"{len(tensors)} BF16 linears in 2 shards on local disk",
+                "timing": "wall clock of convert(), second of two runs (source in the page cache)"}
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
 
 
 def e2e_encode(ws, args, world):

@@ -10,6 +10,7 @@ include/glint_htile.h, cuda/p7_abi.c).  Python front ends:
                          stream ordered), used by the tests and bench.py
   glint_b200.shard       multi-GPU placement: per-tensor LPT and column-parallel
                          linears
+  glint_b200.pin         the pin tool (glint_pin.py's interface) as a GPU pipeline
 """
 from .build import library_path  # noqa: F401
 

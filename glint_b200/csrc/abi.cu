@@ -14,9 +14,13 @@
  * compiled into the kernels, so every device sees it.
  */
 #include <algorithm>
+#include <condition_variable>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <vector>
+
+#include <unistd.h>
 
 #include "../../include/glint_b200.h"
 #include "../../include/glint_encode.h"
@@ -109,6 +113,88 @@ bool ensure_streams(DevState &S)
     return true;
 }
 
+/* Host memcpy split with a few persistent threads (at most 8 with the caller), for
+ * the pipeline's copies between pageable caller memory and pinned staging: one
+ * thread moves ~5-10 GB/s, and first-touch page faults of a memory-mapped input
+ * are taken in parallel too.  Workers take fixed parts of one copy at a time
+ * (copies are serialised), so every worker sees every copy exactly once.  The pool
+ * is never destroyed: idle workers block on a condition variable until exit. */
+class CopyPool {
+  public:
+    static CopyPool &get()
+    {
+        static CopyPool *pool = new CopyPool();
+        return *pool;
+    }
+    void copy(void *dst, const void *src, size_t bytes)
+    {
+        /* a forked child has the pool's state but not its threads */
+        if (bytes < kMinSplit || workers_ == 0 || getpid() != pid_) {
+            std::memcpy(dst, src, bytes);
+            return;
+        }
+        std::lock_guard<std::mutex> one(call_mu_);
+        const size_t parts = (size_t)workers_ + 1;
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            dst_ = static_cast<char *>(dst);
+            src_ = static_cast<const char *>(src);
+            bytes_ = bytes;
+            part_ = ((bytes + parts - 1) / parts + 4095) & ~size_t(4095);
+            done_ = 0;
+            ++gen_;
+        }
+        cv_.notify_all();
+        run_part(0);
+        std::unique_lock<std::mutex> lk(mu_);
+        done_cv_.wait(lk, [&] { return done_ == workers_; });
+    }
+
+  private:
+    static constexpr size_t kMinSplit = size_t(4) << 20;
+    CopyPool() : pid_(getpid())
+    {
+        const unsigned hw = std::thread::hardware_concurrency();
+        workers_ = (int)std::min(7u, hw > 1 ? hw - 1 : 0u);
+        for (int i = 0; i < workers_; ++i)
+            std::thread([this, i] { loop(i + 1); }).detach();
+    }
+    void run_part(int k)
+    {
+        const size_t off = (size_t)k * part_;
+        if (off < bytes_)
+            std::memcpy(dst_ + off, src_ + off, std::min(part_, bytes_ - off));
+    }
+    void loop(int k)
+    {
+        uint64_t seen = 0;
+        for (;;) {
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return gen_ != seen; });
+                seen = gen_;
+            }
+            run_part(k);
+            {
+                std::lock_guard<std::mutex> lk(mu_);
+                ++done_;
+            }
+            done_cv_.notify_one();
+        }
+    }
+    pid_t pid_;
+    int workers_ = 0;
+    std::mutex call_mu_, mu_;
+    std::condition_variable cv_, done_cv_;
+    char *dst_ = nullptr;
+    const char *src_ = nullptr;
+    size_t bytes_ = 0, part_ = 0;
+    int done_ = 0;
+    uint64_t gen_ = 0;
+};
+
+void host_copy(void *dst, const void *src, size_t bytes) { CopyPool::get().copy(dst, src, bytes); }
+
 bool is_pinned(const void *p)
 {
     cudaPointerAttributes a;
@@ -147,22 +233,26 @@ int64_t chunk_len(int64_t n, int bs)
 }
 
 struct Layout {
-    size_t dense, planes, am, total;
+    size_t dense, planes, am, err, total; /* bytes of each part of a slot, in this order */
 };
-Layout slot_layout(int64_t chunk, int bs, size_t dense_elem)
+Layout slot_layout(int64_t chunk, int bs, size_t dense_elem, bool with_err)
 {
     Layout L;
     L.dense = align256((size_t)chunk * dense_elem);
     L.planes = align256((size_t)(chunk / 2));
     L.am = align256((size_t)(chunk / bs) * sizeof(float));
-    L.total = L.dense + 2 * L.planes + L.am;
+    L.err = with_err ? align256((size_t)kMaxSqErrPartials * sizeof(double)) : 0;
+    L.total = L.dense + 2 * L.planes + L.am + L.err;
     return L;
 }
 
 /* Encode (to_planes) or expand (!to_planes) a host tensor through the slots.
- * dense: host input (encode) or output (expand) of n elements of dense_elem bytes. */
+ * dense: host input (encode) or output (expand) of n elements of dense_elem bytes.
+ * sq_err (encode only, may be null): the f64 squared dequantisation error of the
+ * whole tensor, each chunk's partials added in order on the host, then the chunks
+ * in order. */
 int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs, uint8_t *hole, uint8_t *plug,
-                  float *am)
+                  float *am, double *sq_err = nullptr)
 {
     const int dev = current_device();
     if (dev < 0)
@@ -173,18 +263,21 @@ int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs
         return kLaunch;
     const size_t de = f32_dense ? 4 : 2;
     const int64_t chunk = chunk_len(n, bs);
-    const Layout L = slot_layout(chunk, bs, de);
+    const bool want_err = to_planes && sq_err;
+    const Layout L = slot_layout(chunk, bs, de, want_err);
+    const size_t err_off = L.dense + 2 * L.planes + L.am;
     const int64_t nb_total = (n + bs - 1) / bs;
     const bool pin_dense = is_pinned(dense);
     const bool pin_planes = is_pinned(hole) && is_pinned(plug) && is_pinned(am);
     for (int s = 0; s < kSlots; ++s) {
         if (!grow_device(S.dbuf[s], L.total))
             return to_planes ? kBadArg : kLaunch;
-        if ((!pin_dense || !pin_planes) && !grow_pinned(S.hbuf[s], L.total))
+        if ((!pin_dense || !pin_planes || want_err) && !grow_pinned(S.hbuf[s], L.total))
             return kLaunch;
     }
     const int64_t nchunks = (n + chunk - 1) / chunk;
     std::vector<int64_t> pending(kSlots, -1); /* chunk whose results still sit in a staging slot */
+    std::vector<double> chunk_err(want_err ? nchunks : 0, 0.0);
     int rc = kOk;
 
     auto span = [&](int64_t ci, int64_t &off, int64_t &cn, int64_t &bytes_pk, int64_t &nam) {
@@ -203,12 +296,19 @@ int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs
         span(pending[s], off, cn, bpk, nam);
         char *h = static_cast<char *>(S.hbuf[s].p);
         if (to_planes && !pin_planes) {
-            memcpy(hole + off / 2, h + L.dense, bpk);
-            memcpy(plug + off / 2, h + L.dense + L.planes, bpk);
-            memcpy(am + off / bs, h + L.dense + 2 * L.planes, nam * sizeof(float));
+            host_copy(hole + off / 2, h + L.dense, bpk);
+            host_copy(plug + off / 2, h + L.dense + L.planes, bpk);
+            host_copy(am + off / bs, h + L.dense + 2 * L.planes, nam * sizeof(float));
         }
         if (!to_planes && !pin_dense)
-            memcpy(static_cast<char *>(dense) + off * de, h, cn * de);
+            host_copy(static_cast<char *>(dense) + off * de, h, cn * de);
+        if (want_err) {
+            const double *part = reinterpret_cast<const double *>(h + err_off);
+            double e = 0.0;
+            for (int g = 0, G = sq_error_grid(cn); g < G; ++g)
+                e += part[g];
+            chunk_err[pending[s]] = e;
+        }
         pending[s] = -1;
         return kOk;
     };
@@ -234,7 +334,7 @@ int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs
         if (to_planes) {
             const char *src = static_cast<const char *>(dense) + off * de;
             if (!pin_dense) {
-                memcpy(h, src, cn * de);
+                host_copy(h, src, cn * de);
                 src = h;
             }
             if (cudaMemcpyAsync(d, src, cn * de, cudaMemcpyHostToDevice, st) != cudaSuccess) {
@@ -244,6 +344,16 @@ int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs
             EncodeJob j{d, cn, d_hole, d_plug, d_am};
             if ((rc = encode_launch(&j, 1, bs, f32_dense, st)) != kOk)
                 break;
+            if (want_err) {
+                double *d_err = reinterpret_cast<double *>(d + err_off);
+                if ((rc = sq_error_launch(d, f32_dense, d_hole, d_plug, d_am, cn, bs, d_err, st)) != kOk)
+                    break;
+                if (cudaMemcpyAsync(h + err_off, d_err, (size_t)sq_error_grid(cn) * sizeof(double),
+                                    cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+                    rc = kLaunch;
+                    break;
+                }
+            }
             uint8_t *oh = pin_planes ? hole + off / 2 : reinterpret_cast<uint8_t *>(h + L.dense);
             uint8_t *op = pin_planes ? plug + off / 2 : reinterpret_cast<uint8_t *>(h + L.dense + L.planes);
             float *oa = pin_planes ? am + off / bs : reinterpret_cast<float *>(h + L.dense + 2 * L.planes);
@@ -257,9 +367,9 @@ int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs
             const uint8_t *sh = hole + off / 2, *sp = plug + off / 2;
             const float *sa = am + off / bs;
             if (!pin_planes) {
-                memcpy(h + L.dense, sh, bpk);
-                memcpy(h + L.dense + L.planes, sp, bpk);
-                memcpy(h + L.dense + 2 * L.planes, sa, nam * sizeof(float));
+                host_copy(h + L.dense, sh, bpk);
+                host_copy(h + L.dense + L.planes, sp, bpk);
+                host_copy(h + L.dense + 2 * L.planes, sa, nam * sizeof(float));
                 sh = reinterpret_cast<uint8_t *>(h + L.dense);
                 sp = reinterpret_cast<uint8_t *>(h + L.dense + L.planes);
                 sa = reinterpret_cast<float *>(h + L.dense + 2 * L.planes);
@@ -283,7 +393,7 @@ int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs
             rc = kLaunch;
             break;
         }
-        pending[s] = ((to_planes && !pin_planes) || (!to_planes && !pin_dense)) ? ci : -1;
+        pending[s] = ((to_planes && !pin_planes) || (!to_planes && !pin_dense) || want_err) ? ci : -1;
     }
     /* finish every slot, also after an error, so no copy into caller memory outlives the call */
     for (int s = 0; s < kSlots; ++s) {
@@ -297,18 +407,28 @@ int host_pipeline(bool to_planes, bool f32_dense, void *dense, int64_t n, int bs
     }
     if (cudaGetLastError() != cudaSuccess && rc == kOk)
         rc = kLaunch;
+    if (want_err && rc == kOk) {
+        double e = 0.0;
+        for (double c : chunk_err)
+            e += c;
+        *sq_err = e;
+    }
     return rc;
 }
 
-int encode_host(const void *w, int64_t n, int bs, uint8_t *hole, uint8_t *plug, float *am, bool f32)
+int encode_host(const void *w, int64_t n, int bs, uint8_t *hole, uint8_t *plug, float *am, bool f32,
+                double *sq_err = nullptr)
 {
     if (n < 0 || bs <= 0)
         return kBadArg;
-    if (n == 0)
+    if (n == 0) {
+        if (sq_err)
+            *sq_err = 0.0;
         return kOk;
+    }
     if (!w || !hole || !plug || !am)
         return kBadArg;
-    return host_pipeline(true, f32, const_cast<void *>(w), n, bs, hole, plug, am);
+    return host_pipeline(true, f32, const_cast<void *>(w), n, bs, hole, plug, am, sq_err);
 }
 
 int expand_host(const uint8_t *hole, const uint8_t *plug, const float *am, int64_t n, int bs, void *out, bool f32)
@@ -411,6 +531,28 @@ int glint_encode_f32_host(const float *w, int64_t n, int blocksize, uint8_t *hol
                           float *absmax)
 {
     return encode_host(w, n, blocksize, hole_packed, plug_packed, absmax, true);
+}
+int glint_encode_bf16_host_sqerr(const uint16_t *w_bf16, int64_t n, int blocksize, uint8_t *hole_packed,
+                                 uint8_t *plug_packed, float *absmax, double *sum_sq_err)
+{
+    if (!sum_sq_err)
+        return kBadArg;
+    return encode_host(w_bf16, n, blocksize, hole_packed, plug_packed, absmax, false, sum_sq_err);
+}
+int glint_encode_f32_host_sqerr(const float *w, int64_t n, int blocksize, uint8_t *hole_packed, uint8_t *plug_packed,
+                                float *absmax, double *sum_sq_err)
+{
+    if (!sum_sq_err)
+        return kBadArg;
+    return encode_host(w, n, blocksize, hole_packed, plug_packed, absmax, true, sum_sq_err);
+}
+int glint_cells_f32(float *out)
+{
+    static const float kCells[16][16] = GLINT_CELLS_INIT;
+    if (!out)
+        return kBadArg;
+    memcpy(out, kCells, sizeof(kCells));
+    return 256;
 }
 int glint_expand_packed_to_f32_host(const uint8_t *hole_packed, const uint8_t *plug_packed, const float *absmax,
                                     int64_t n, int blocksize, float *out_f32)

@@ -359,6 +359,79 @@ int expand_launch(const ExpandJob *jobs, int count, int bs, OutKind out, cudaStr
     return rc;
 }
 
+namespace {
+
+/* Squared dequantisation error of an encoded range, per CTA: the f64 sum over the
+ * CTA's elements of ((double)w_i - (double)(CELLS[h_i][p_i] * absmax[i / bs]))^2,
+ * the dequantised value being the expand kernels' f32 product.  Element pairs (one
+ * plane byte) are dealt out grid-stride, then lanes and warps are added in index
+ * order, so a given grid gives the same bits on every call.  The pin tool's rmse
+ * (glint_pin.py:66-72 of the reference: glint_np.rmse on glint_np.expand,
+ * glint_np.py:93-95) is sqrt(total / n). */
+template <bool F32IN>
+__global__ void __launch_bounds__(kSqErrThreads) sq_error_kernel(const void *w, const uint8_t *hole,
+                                                                 const uint8_t *plug, const float *absmax,
+                                                                 int64_t n, int bs, double *partial)
+{
+    __shared__ float cells[256];
+    __shared__ double warp_sum[kSqErrThreads / 32];
+    for (int i = threadIdx.x; i < 256; i += kSqErrThreads)
+        cells[i] = (&g_cells[0][0])[i];
+    __syncthreads();
+    double acc = 0.0;
+    const int64_t pairs = (n + 1) / 2;
+    for (int64_t b = (int64_t)blockIdx.x * kSqErrThreads + threadIdx.x; b < pairs;
+         b += (int64_t)gridDim.x * kSqErrThreads) {
+        const uint32_t hb = hole[b], pb = plug[b];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int64_t i = 2 * b + e;
+            if (i >= n)
+                break;
+            const uint32_t h = (hb >> (4 * e)) & 15u, p = (pb >> (4 * e)) & 15u;
+            const float wf = F32IN ? static_cast<const float *>(w)[i]
+                                   : __uint_as_float((uint32_t)static_cast<const uint16_t *>(w)[i] << 16);
+            const float q = __fmul_rn(cells[h * 16 + p], absmax[i / bs]);
+            const double d = __dsub_rn((double)wf, (double)q);
+            acc = __dadd_rn(acc, __dmul_rn(d, d));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        acc = __dadd_rn(acc, __shfl_down_sync(0xFFFFFFFFu, acc, o));
+    if ((threadIdx.x & 31) == 0)
+        warp_sum[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int k = 0; k < kSqErrThreads / 32; ++k)
+            s = __dadd_rn(s, warp_sum[k]);
+        partial[blockIdx.x] = s;
+    }
+}
+
+} // namespace
+
+int sq_error_grid(int64_t n)
+{
+    const int64_t pairs = (n + 1) / 2;
+    return (int)std::max<int64_t>(1, std::min<int64_t>((pairs + kSqErrThreads - 1) / kSqErrThreads,
+                                                       std::min<int64_t>(kMaxSqErrPartials, 2 * sm_count())));
+}
+
+int sq_error_launch(const void *w, bool f32_in, const uint8_t *hole, const uint8_t *plug, const float *absmax,
+                    int64_t n, int bs, double *partial, cudaStream_t st)
+{
+    if (n <= 0 || bs <= 0 || !w || !hole || !plug || !absmax || !partial)
+        return kBadArg;
+    const int grid = sq_error_grid(n);
+    if (f32_in)
+        sq_error_kernel<true><<<grid, kSqErrThreads, 0, st>>>(w, hole, plug, absmax, n, bs, partial);
+    else
+        sq_error_kernel<false><<<grid, kSqErrThreads, 0, st>>>(w, hole, plug, absmax, n, bs, partial);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+}
+
 /* This file's kernel error word (bounded waits that ran out); clear resets it. */
 int expand_error_word(bool clear)
 {

@@ -40,6 +40,15 @@ int encode_launch(const EncodeJob *jobs, int count, int blocksize, bool f32_in, 
 /* Launch the expand of `count` tensors. */
 int expand_launch(const ExpandJob *jobs, int count, int blocksize, OutKind out, cudaStream_t stream);
 
+/* Squared dequantisation error of one encoded tensor (or chunk): sq_error_grid(n)
+ * f64 partial sums into `partial`, whose in-order total is
+ * sum_i ((double)w_i - (double)(CELLS[h_i][p_i] * absmax[i / bs]))^2. */
+constexpr int kSqErrThreads = 256;
+constexpr int kMaxSqErrPartials = 1024;
+int sq_error_grid(int64_t n);
+int sq_error_launch(const void *w, bool f32_in, const uint8_t *hole, const uint8_t *plug, const float *absmax,
+                    int64_t n, int blocksize, double *partial, cudaStream_t stream);
+
 /* y[M,N] = x[M,K] . W^T with W dequantised from hole/plug/absmax. */
 int htile_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
                  void *y, OutKind y_kind, int M, int N, int K, int blocksize, HtileMode mode, cudaStream_t stream);

@@ -736,87 +736,90 @@ __global__ void __launch_bounds__(kThreads, 1)
          * in block order, publishes the unit's partial and, as the tile's last
          * unit, adds the tile's KU partials in unit order.  No waits on other CTAs:
          * a failed TMA wait still publishes (zeros), so the count stays whole. */
-        const int j = warp - active;
-        if (!has_tail || j >= kTailWarps)
-            return;
-        float acc[MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-            acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
-        const bool ok = lane == 0 ? mbar_wait_suspend_bounded(tail_full, 0u, &g_decode_error) : true;
-        const uint32_t ts = saddr(tail);
-        if (__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
-            tile_block<MT, SPLIT, 128>(ts, ts + 2048, ts + 4096, (uint32_t)j,
-                                       ts + (uint32_t)(kTailX + j * (8 * MT * 128)), j, 0, g, t, lut_base, lane4,
-                                       a.M, acc);
-        float4 *part = reinterpret_cast<float4 *>(tail + kTailX + r_xsub<MT>());
-        if (j > 0) {
+        if constexpr (MT <= 2) { /* the tail's shared buffer exists for MT <= 2 only */
+            const int j = warp - active;
+            if (!has_tail || j >= kTailWarps)
+                return;
+            float acc[MT][4];
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
-                part[((j - 1) * 32 + (int)lane) * MT + mt] = make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
-        }
-        asm volatile("bar.sync 2, %0;" ::"n"(kTailWarps * 32) : "memory");
-        if (j > 0)
-            return;
-#pragma unroll
-        for (int jj = 1; jj < kTailWarps; ++jj)
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                const float4 v = part[((jj - 1) * 32 + (int)lane) * MT + mt];
-                acc[mt][0] += v.x, acc[mt][1] += v.y, acc[mt][2] += v.z, acc[mt][3] += v.w;
-            }
-        float4 *ws = reinterpret_cast<float4 *>(a.tail_ws);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-            __stcg(ws + ((int64_t)blockIdx.x * 32 + lane) * MT + mt,
-                   make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]));
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0)
-            last = atomicAdd(a.tail_cnt + tail_tile, 1) == a.KU - 1;
-        if (!__shfl_sync(0xFFFFFFFFu, last, 0))
-            return;
-        __threadfence();
-        float sum[MT][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-            sum[mt][0] = sum[mt][1] = sum[mt][2] = sum[mt][3] = 0.f;
-        const int64_t u0 = (int64_t)tail_tile * a.KU;
-        for (int u = 0; u < a.KU; u += 8) {
-            /* eight units' loads in flight at once, added in unit order */
-            float4 v[8][MT];
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
+                acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+            const bool ok = lane == 0 ? mbar_wait_suspend_bounded(tail_full, 0u, &g_decode_error) : true;
+            const uint32_t ts = saddr(tail);
+            if (__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
+                tile_block<MT, SPLIT, 128>(ts, ts + 2048, ts + 4096, (uint32_t)j,
+                                           ts + (uint32_t)(kTailX + j * (8 * MT * 128)), j, 0, g, t, lut_base, lane4,
+                                           a.M, acc);
+            float4 *part = reinterpret_cast<float4 *>(tail + kTailX + r_xsub<MT>());
+            if (j > 0) {
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
-                    v[q][mt] = u + q < a.KU ? __ldcg(ws + ((u0 + u + q) * 32 + lane) * MT + mt)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                    part[((j - 1) * 32 + (int)lane) * MT + mt] = make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
+            }
+            asm volatile("bar.sync 2, %0;" ::"n"(kTailWarps * 32) : "memory");
+            if (j > 0)
+                return;
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                if (u + q < a.KU) {
+            for (int jj = 1; jj < kTailWarps; ++jj)
 #pragma unroll
-                    for (int mt = 0; mt < MT; ++mt) {
-                        sum[mt][0] += v[q][mt].x, sum[mt][1] += v[q][mt].y;
-                        sum[mt][2] += v[q][mt].z, sum[mt][3] += v[q][mt].w;
+                for (int mt = 0; mt < MT; ++mt) {
+                    const float4 v = part[((jj - 1) * 32 + (int)lane) * MT + mt];
+                    acc[mt][0] += v.x, acc[mt][1] += v.y, acc[mt][2] += v.z, acc[mt][3] += v.w;
+                }
+            float4 *ws = reinterpret_cast<float4 *>(a.tail_ws);
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+                __stcg(ws + ((int64_t)blockIdx.x * 32 + lane) * MT + mt,
+                       make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]));
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0)
+                last = atomicAdd(a.tail_cnt + tail_tile, 1) == a.KU - 1;
+            if (!__shfl_sync(0xFFFFFFFFu, last, 0))
+                return;
+            __threadfence();
+            float sum[MT][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+                sum[mt][0] = sum[mt][1] = sum[mt][2] = sum[mt][3] = 0.f;
+            const int64_t u0 = (int64_t)tail_tile * a.KU;
+            for (int u = 0; u < a.KU; u += 8) {
+                /* eight units' loads in flight at once, added in unit order */
+                float4 v[8][MT];
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+                        v[q][mt] = u + q < a.KU ? __ldcg(ws + ((u0 + u + q) * 32 + lane) * MT + mt)
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (u + q < a.KU) {
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            sum[mt][0] += v[q][mt].x, sum[mt][1] += v[q][mt].y;
+                            sum[mt][2] += v[q][mt].z, sum[mt][3] += v[q][mt].w;
+                        }
+                    }
+            }
+            if (lane == 0)
+                a.tail_cnt[tail_tile] = 0; /* every unit has arrived: zero for the next call */
+            const int n16 = a.tail_row0 + tail_tile * 16;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int n = n16 + pg + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
+                    if (n < a.N && col < a.M) {
+                        if (BF16OUT)
+                            static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(sum[mt][q]);
+                        else
+                            static_cast<float *>(a.y)[(int64_t)col * a.N + n] = sum[mt][q];
                     }
                 }
+            return;
         }
-        if (lane == 0)
-            a.tail_cnt[tail_tile] = 0; /* every unit has arrived: zero for the next call */
-        const int n16 = a.tail_row0 + tail_tile * 16;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int n = n16 + pg + (q >> 1) * 8, col = mt * 8 + 2 * t + (q & 1);
-                if (n < a.N && col < a.M) {
-                    if (BF16OUT)
-                        static_cast<__nv_bfloat16 *>(a.y)[(int64_t)col * a.N + n] = __float2bfloat16_rn(sum[mt][q]);
-                    else
-                        static_cast<float *>(a.y)[(int64_t)col * a.N + n] = sum[mt][q];
-                }
-            }
         return;
     }
 

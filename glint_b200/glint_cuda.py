@@ -47,6 +47,11 @@ def _bind(lib):
     for f in (lib.glint_expand_packed_to_f32_host, lib.glint_expand_packed_to_bf16_host):
         f.argtypes = [vp, vp, vp, i64, i32, vp]
         f.restype = i32
+    for f in (lib.glint_encode_bf16_host_sqerr, lib.glint_encode_f32_host_sqerr):
+        f.argtypes = [vp, i64, i32, vp, vp, vp, ctypes.POINTER(ctypes.c_double)]
+        f.restype = i32
+    lib.glint_cells_f32.argtypes = [vp]
+    lib.glint_cells_f32.restype = i32
     for f in (lib.glint_encode_bf16_device, lib.glint_encode_f32_device):
         f.argtypes = [vp, i64, i32, vp, vp, vp, vp]
         f.restype = i32

@@ -84,6 +84,25 @@ int glint_encode_bf16_device_batch(
 int glint_expand_packed_to_bf16_device_batch(
     const GlintTensorDesc *tensors, int count, int blocksize, struct CUstream_st *stream);
 
+/* glint_encode_bf16_host / glint_encode_f32_host that also return, in *sum_sq_err,
+ * the f64 sum over the n weights of (w - dequant(w))^2, dequant(w) being the f32
+ * product GLINT_CELLS[h][p] * absmax that expand writes.  sqrt(*sum_sq_err / n)
+ * is the rmse the reference pin tool reports per linear (glint_pin.py:66-72, from
+ * glint_np.rmse of glint_np.expand, glint_np.py:93-95), here computed on the GPU
+ * while the tensor streams through; the sum's order is fixed, so repeated calls
+ * on one GPU give the same bits.  A null sum_sq_err returns -1. */
+int glint_encode_bf16_host_sqerr(
+    const uint16_t *w_bf16, int64_t n, int blocksize,
+    uint8_t *hole_packed, uint8_t *plug_packed, float *absmax, double *sum_sq_err);
+int glint_encode_f32_host_sqerr(
+    const float *w, int64_t n, int blocksize,
+    uint8_t *hole_packed, uint8_t *plug_packed, float *absmax, double *sum_sq_err);
+
+/* Copies the compiled codebook GLINT_CELLS (16 x 16 f32, row-major: the pin's
+ * `_glint_cells` tensor, glint_pin.py:158-159) into out[256]; returns 256, or -1
+ * for a null out.  Needs no GPU. */
+int glint_cells_f32(float *out);
+
 #ifdef __cplusplus
 }
 #endif
