@@ -86,7 +86,10 @@ class Reader:
 
     def close(self) -> None:
         if getattr(self, "_mm", None) is not None:
-            self._mm.close()
+            try:
+                self._mm.close()
+            except BufferError:
+                pass  # a view is still alive (e.g. in a traceback): the mapping goes with it
             self._mm = None
         self._f.close()
 
