@@ -285,10 +285,11 @@ def bench_pin(tensors):
     """glint_b200.pin.convert of a two-shard BF16 model written to a temporary
     directory: wall clock of the second of two conversions (so the source is in the
     page cache and the pipeline's staging exists), which covers reading the shards,
-    host->device and device->host copies, the GPU encode and rmse, and writing the pin."""
+    host->device and device->host copies, the GPU encode and rmse, and writing the pin;
+    then glint_b200.unpin.unpin of that pin back to BF16, timed the same way."""
     import shutil
     import tempfile
-    from glint_b200 import pin, st_io
+    from glint_b200 import pin, st_io, unpin
     root = Path(tempfile.mkdtemp(prefix="glint_pin_bench_"))
     try:
         src = root / "src"
@@ -308,11 +309,18 @@ def bench_pin(tensors):
             got = pin.convert(src, out, BS)
             times.append(time.perf_counter() - t)
         out_bytes = sum(p.stat().st_size for p in (root / "pin1").iterdir())
+        utimes = []
+        for k in range(2):
+            t = time.perf_counter()
+            unpin.unpin(root / "pin1", root / f"dense{k}", "BF16")
+            utimes.append(time.perf_counter() - t)
         return {"gbs_bf16_in": round(n_in / times[-1] / 1e9, 2), "seconds": round(times[-1], 3),
+                "unpin_gbs_bf16_out": round(n_in / utimes[-1] / 1e9, 2), "unpin_seconds": round(utimes[-1], 3),
                 "first_run_seconds": round(times[0], 3), "bf16_in_bytes": n_in, "pin_bytes": out_bytes,
                 "linears": got["pin"]["n_converted"], "rmse_max": got["pin"]["rmse_max"],
                 "sample": f"{len(tensors)} BF16 linears in 2 shards on local disk",
-                "timing": "wall clock of convert(), second of two runs (source in the page cache)"}
+                "timing": "wall clock of convert() (and of unpin() of its pin), second of two runs each "
+                          "(inputs in the page cache)"}
     finally:
         shutil.rmtree(root, ignore_errors=True)
 

@@ -11,6 +11,7 @@ include/glint_htile.h, cuda/p7_abi.c).  Python front ends:
   glint_b200.shard       multi-GPU placement: per-tensor LPT and column-parallel
                          linears
   glint_b200.pin         the pin tool (glint_pin.py's interface) as a GPU pipeline
+  glint_b200.unpin       the unpin tool (glint_unpin.py's interface) on the GPU
 """
 from .build import library_path  # noqa: F401
 

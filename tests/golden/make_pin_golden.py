@@ -11,6 +11,9 @@ pin the reference's own tool makes of it.
 - pin/ref/, pin/ref_single/: glint_pin.convert(src, out, 64, allow_cpu=True) of the
   reference (Jadon-Fox/glint, imported from its checkout; its host numpy encoder, which
   its tests hold byte-equal to its CUDA encoder), plus dry_run.json, its dry-run plan.
+- pin/unpin_bf16/, pin/unpin_single_{bf16,f16,f32}/: the reference's
+  glint_unpin.unpin of those pins (dense model back, with the pin's own codebook), and
+  unpin.json, its return value.
 
 Run from the repository root in a checkout where the reference's Python is importable:
     python tests/golden/make_pin_golden.py /path/to/reference
@@ -109,10 +112,24 @@ def run_reference(ref: Path, root: Path) -> None:
             (out / name).write_text(json.dumps(doc, indent=2) + "\n")
 
 
+def run_reference_unpin(root: Path) -> None:
+    import glint_unpin  # noqa: E402  (the reference's tool; its path was added above)
+    for pin_dir, out, dtype in ((root / "ref", root / "unpin_bf16", "BF16"),
+                                (root / "ref_single", root / "unpin_single_bf16", "BF16"),
+                                (root / "ref_single", root / "unpin_single_f16", "F16"),
+                                (root / "ref_single", root / "unpin_single_f32", "F32")):
+        if out.exists():
+            shutil.rmtree(out)
+        got = glint_unpin.unpin(pin_dir, out, dtype)
+        got["out"] = "<out>"  # the generating machine's path
+        (out / "unpin.json").write_text(json.dumps(got, indent=2) + "\n")
+
+
 if __name__ == "__main__":
     if len(sys.argv) != 2:
         raise SystemExit(__doc__)
     root = HERE / "pin"
     make_sources(root)
     run_reference(Path(sys.argv[1]), root)
+    run_reference_unpin(root)
     print("wrote", root)

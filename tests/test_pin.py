@@ -1,6 +1,7 @@
-"""Pin pipeline (glint_b200/pin.py, glint_b200/st_io.py) against the pin the reference's
-own tool wrote (tests/golden/pin/, made by tests/golden/make_pin_golden.py with
-glint_pin.convert of Jadon-Fox/glint).
+"""Pin and unpin pipelines (glint_b200/pin.py, glint_b200/unpin.py, glint_b200/st_io.py)
+against the files the reference's own tools wrote (tests/golden/pin/, made by
+tests/golden/make_pin_golden.py with glint_pin.convert and glint_unpin.unpin of
+Jadon-Fox/glint).
 
 CPU: the safetensors writer reproduces every reference-written file byte for byte
 from its tensors; the plan (which tensors are linears) equals the reference's dry
@@ -9,7 +10,8 @@ GPU: the whole conversion of the two-shard model and of the one-file model gives
 reference's shard files, index and sidecars byte for byte, pin.json and
 CONVERT_REPORT.json with the same fields, and per-linear rmse within 1e-9 relative
 (both sum squares in f64, in different orders); a multi-chunk tensor's planes equal
-the oracle's encode.
+the oracle's encode; unpin of the reference's pins to BF16, F16 and F32 gives the
+reference unpin's files byte for byte and its return value.
 """
 import filecmp
 import json
@@ -21,7 +23,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from glint_b200 import glint_cuda, pin
+from glint_b200 import glint_cuda, pin, unpin
 from glint_b200.st_io import Reader, Writer, header_bytes, write_file
 
 GOLD = Path(__file__).resolve().parent / "golden" / "pin"
@@ -171,3 +173,58 @@ def test_convert_multi_chunk_tensor_vs_oracle(tmp_path):
         want = float(np.sqrt(np.mean(d * d)))
         mod = next(m for m in got["modules"] if m["src"] == name)
         assert math.isclose(mod["rmse"], want, rel_tol=1e-9), (mod["rmse"], want)
+
+
+UNPIN_CASES = [(GOLD / "ref", GOLD / "unpin_bf16", "BF16"), (GOLD / "ref_single", GOLD / "unpin_single_bf16", "BF16"),
+               (GOLD / "ref_single", GOLD / "unpin_single_f16", "F16"),
+               (GOLD / "ref_single", GOLD / "unpin_single_f32", "F32")]
+
+
+def test_unpin_argument_errors(tmp_path):
+    with pytest.raises(ValueError):
+        unpin.unpin(GOLD / "ref", tmp_path / "o", "F64")
+    with pytest.raises(FileNotFoundError):
+        unpin.unpin(tmp_path, tmp_path / "o")
+    bad = tmp_path / "bad"
+    shutil.copytree(GOLD / "ref_single", bad)
+    doc = json.loads((bad / "pin.json").read_text())
+    doc["schema"] = "something_else"
+    (bad / "pin.json").write_text(json.dumps(doc))
+    with pytest.raises(ValueError, match="glint_pin_v1"):
+        unpin.unpin(bad, tmp_path / "o")
+
+
+def test_unpin_no_host_path_without_gpu(tmp_path):
+    if glint_cuda.gpu_ok():
+        pytest.skip("a GPU is present")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        unpin.unpin(GOLD / "ref", tmp_path / "o")
+    assert not (tmp_path / "o").exists()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pin_dir,ref,dtype", UNPIN_CASES)
+def test_unpin_matches_reference(pin_dir, ref, dtype, tmp_path):
+    out = tmp_path / "dense"
+    got = unpin.unpin(pin_dir, out, dtype)
+    want = json.loads((ref / "unpin.json").read_text())
+    assert got["out"] == str(out.resolve())
+    got["out"] = want["out"]
+    assert got == want
+    names = sorted(p.name for p in ref.iterdir() if p.name != "unpin.json")
+    assert sorted(p.name for p in out.iterdir()) == names
+    for name in names:
+        assert filecmp.cmp(out / name, ref / name, shallow=False), name
+
+
+@pytest.mark.gpu
+def test_unpin_refuses_a_foreign_codebook(tmp_path):
+    """A pin whose _glint_cells is not the compiled table: refused, not expanded wrongly."""
+    foreign = tmp_path / "pin"
+    shutil.copytree(GOLD / "ref_single", foreign)
+    meta, tensors = _tensors(foreign / "model.safetensors")
+    tensors = [(n, d, s, (np.frombuffer(b, "<f4") * np.float32(2)).tobytes() if n == "_glint_cells" else b)
+               for n, d, s, b in tensors]
+    write_file(str(foreign / "model.safetensors"), tensors, meta)
+    with pytest.raises(RuntimeError, match="_glint_cells"):
+        unpin.unpin(foreign, tmp_path / "o")
