@@ -22,6 +22,8 @@ from pathlib import Path
 
 import numpy as np
 import pytest
+from hypothesis import given, settings
+from hypothesis import strategies as st
 
 from glint_b200 import glint_cuda, pin, unpin
 from glint_b200.st_io import Reader, Writer, header_bytes, write_file
@@ -42,6 +44,33 @@ def test_writer_reproduces_reference_files(rel, tmp_path):
     meta, tensors = _tensors(GOLD / rel)
     write_file(str(tmp_path / "x.safetensors"), tensors, meta)
     assert (tmp_path / "x.safetensors").read_bytes() == (GOLD / rel).read_bytes()
+
+
+_DT = ["BOOL", "U8", "I8", "I16", "U16", "F16", "BF16", "I32", "U32", "F32", "F64", "I64", "U64"]
+
+
+@settings(max_examples=60, deadline=None)
+@given(spec=st.lists(st.tuples(st.sampled_from(_DT), st.lists(st.integers(0, 5), min_size=0, max_size=3)),
+                     min_size=0, max_size=6),
+       meta=st.dictionaries(st.text("abcxyz", min_size=1, max_size=4), st.text(max_size=6), max_size=2),
+       seed=st.integers(0, 2 ** 16))
+def test_write_read_round_trip(spec, meta, seed, tmp_path_factory):
+    """Any dtypes, shapes (empty ones too) and metadata: the reader gets back the
+    names, dtypes, shapes, metadata and bytes the writer was given, with the data
+    starting on an 8-byte boundary."""
+    from glint_b200.st_io import DTYPE_WIDTH
+    rng = np.random.default_rng(seed)
+    tensors = []
+    for i, (dt, shape) in enumerate(spec):
+        nbytes = int(np.prod(shape, dtype=np.int64)) * DTYPE_WIDTH[dt]
+        tensors.append((f"t{i}.{dt.lower()}", dt, tuple(shape), rng.integers(0, 256, nbytes, dtype=np.uint8).tobytes()))
+    path = tmp_path_factory.mktemp("rt") / "x.safetensors"
+    write_file(str(path), tensors, meta)
+    got_meta, got = _tensors(path)
+    assert got_meta == meta
+    assert [(n, d, tuple(sh), b) for n, d, sh, b in got] == tensors
+    with Reader(str(path)) as r:
+        assert r.data_start % 8 == 0
 
 
 def test_header_padding_and_order():
