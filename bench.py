@@ -473,6 +473,9 @@ def bench_tp_decode(args, world, rank, pk, M: int = 1):
         outs = []
         for nm in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj"):
             outs.append(tp.column_parallel(x, shards[nm], world, rank, gather=False))
+        if world == 1:  # nothing to gather: the seven decode calls back to back
+            return outs, tp.column_parallel(attn, shards["o_proj"], 1, 0), \
+                tp.column_parallel(act_full, shards["down_proj"], 1, 0)
         # o_proj: gather its input shard (the attention output), then its output
         o_in = tp.gather_columns(attn[:, shards["o_proj"].n0:shards["o_proj"].n1].float(), 8192, world, rank)
         o = tp.column_parallel(o_in.to(torch.bfloat16), shards["o_proj"], world, rank)
