@@ -196,3 +196,15 @@ def gpu_ok() -> bool:
         return True
     except (RuntimeError, OSError):
         return False
+
+
+def require_gpu(work: str = "GLINT encode", host_path: str = "the reference's glint_pin.py --allow-cpu"):
+    """The loaded library when a GPU can run it; RuntimeError otherwise, naming `work`
+    and the reference tool that is the host path (the front ends here have none)."""
+    lib = load()
+    if lib is None:
+        raise RuntimeError(f"{work} is CUDA (libglint_encode.so): {_ERR}")
+    if not gpu_ok():
+        raise RuntimeError(f"{work} is CUDA: libglint_encode.so loaded but no usable GPU; there is no host "
+                           f"path here ({host_path} is one)")
+    return lib

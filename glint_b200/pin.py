@@ -34,17 +34,15 @@ import argparse
 import ctypes
 import json
 import math
-import queue
 import shutil
 import sys
-import threading
 from pathlib import Path
 from typing import Dict, List, Optional, Tuple
 
 import numpy as np
 
 from . import glint_cuda
-from .st_io import Reader, Writer
+from .st_io import Reader, ThreadedWriter, Writer
 
 # Which tensors stay dense and which files travel with the pin: the reference's
 # rules (glint_pin.py:23-44), since they decide the pin's contents.
@@ -120,54 +118,6 @@ def _encode(lib, dtype: str, raw: np.ndarray, n: int, bs: int):
     return hole, plug, am, (math.sqrt(sq.value / n) if n else 0.0)
 
 
-class _ShardWriter:
-    """A few threads that write queued tensors to their places in the shard file
-    (positional writes), so file writes overlap each other and the next encode."""
-
-    def __init__(self, writer: Writer, threads: int = 4):
-        self.w, self.q, self.err = writer, queue.Queue(maxsize=2 * threads), None
-        self.th = [threading.Thread(target=self._run, daemon=True) for _ in range(threads)]
-        for t in self.th:
-            t.start()
-
-    def _run(self):
-        while True:
-            item = self.q.get()
-            if item is None:
-                return
-            if self.err is None:
-                try:
-                    self.w.put_at(*item)
-                except BaseException as e:  # reported by put() / finish()
-                    self.err = e
-
-    def put(self, i: int, name: str, *parts):
-        if self.err is not None:
-            raise self.err
-        self.q.put((i, name) + parts)
-
-    def finish(self, abort: bool = False):
-        """Write what is queued and close the file; re-raise a writer's error.  With
-        `abort` (the caller failed) close without checking that every tensor came."""
-        for _ in self.th:
-            self.q.put(None)
-        for t in self.th:
-            t.join()
-        self.w.close(check=not abort and self.err is None)
-        if self.err is not None and not abort:
-            raise self.err
-
-
-def _require_gpu():
-    lib = glint_cuda.load()
-    if lib is None:
-        raise RuntimeError(f"GLINT encode is CUDA (libglint_encode.so): {glint_cuda._ERR}")
-    if not glint_cuda.gpu_ok():
-        raise RuntimeError("GLINT encode is CUDA: libglint_encode.so loaded but no usable GPU; this pipeline has "
-                           "no host encoder (the reference's glint_pin.py --allow-cpu is the host path)")
-    return lib
-
-
 def convert(src: Path, out: Path, blocksize: int = 64, dry_run: bool = False, allow_cpu: bool = False,
             force_python: bool = False) -> dict:
     """As glint_pin.convert (glint_pin.py:78-190); allow_cpu / force_python are accepted
@@ -187,7 +137,7 @@ def convert(src: Path, out: Path, blocksize: int = 64, dry_run: bool = False, al
         return {"schema": "glint_pin_v1", "n_linears": len(plan_linears), "n_keep": len(plan_keep),
                 "blocksize": blocksize, "shards": [s.name for s in shards], "linears": plan_linears,
                 "cuda": glint_cuda.load() is not None, "numpy": True}
-    lib = _require_gpu()
+    lib = glint_cuda.require_gpu("GLINT encode", "the reference's glint_pin.py --allow-cpu")
     out.mkdir(parents=True, exist_ok=True)
     reports = []
     weight_map: Dict[str, str] = {}
@@ -214,7 +164,7 @@ def convert(src: Path, out: Path, blocksize: int = 64, dry_run: bool = False, al
             for name, _dt, _sh, nbytes in layout:
                 weight_map[name] = out_name
                 total_size += nbytes
-            wt = _ShardWriter(Writer(str(out / out_name), layout, {"format": "pt", "quantization": "glint"}))
+            wt = ThreadedWriter(Writer(str(out / out_name), layout, {"format": "pt", "quantization": "glint"}))
             ok = False
             try:
                 entries = r.entries

@@ -15,6 +15,7 @@ from __future__ import annotations
 import json
 import mmap
 import os
+import queue
 import struct
 import threading
 from dataclasses import dataclass
@@ -174,6 +175,45 @@ class Writer:
                 raise ValueError(f"{missing} declared tensors were not written")
         finally:
             self._f.close()
+
+
+class ThreadedWriter:
+    """A few threads that take queued tensors and put each at its place in a Writer's
+    file (positional writes), so file writes overlap each other and the caller's next
+    piece of work.  `put(i, name, *parts)` queues tensor i; `finish()` writes what is
+    queued, closes the file and re-raises a writer thread's error."""
+
+    def __init__(self, writer: Writer, threads: int = 4):
+        self.w, self.q, self.err = writer, queue.Queue(maxsize=2 * threads), None
+        self.th = [threading.Thread(target=self._run, daemon=True) for _ in range(threads)]
+        for t in self.th:
+            t.start()
+
+    def _run(self):
+        while True:
+            item = self.q.get()
+            if item is None:
+                return
+            if self.err is None:
+                try:
+                    self.w.put_at(*item)
+                except BaseException as e:  # reported by put() / finish()
+                    self.err = e
+
+    def put(self, i: int, name: str, *parts):
+        if self.err is not None:
+            raise self.err
+        self.q.put((i, name) + parts)
+
+    def finish(self, abort: bool = False):
+        """With `abort` (the caller failed) close without checking that every tensor came."""
+        for _ in self.th:
+            self.q.put(None)
+        for t in self.th:
+            t.join()
+        self.w.close(check=not abort and self.err is None)
+        if self.err is not None and not abort:
+            raise self.err
 
 
 def write_file(path: str, tensors: Sequence[Tuple[str, str, Sequence[int], bytes]],

@@ -34,8 +34,9 @@ from typing import Dict, List, Optional, Tuple
 
 import numpy as np
 
-from .pin import INDEX_NAME, _require_gpu, _ShardWriter
-from .st_io import Entry, Reader, Writer
+from . import glint_cuda
+from .pin import INDEX_NAME
+from .st_io import Entry, Reader, ThreadedWriter, Writer
 
 DTYPES = ("BF16", "F16", "F32")
 STATE_SUFFIX = ".weight.glint_state"
@@ -92,7 +93,7 @@ def unpin(pin_dir: Path, out: Path, dtype: str = "BF16") -> dict:
         stems = [n[: -len(STATE_SUFFIX)] for n in where if n.endswith(STATE_SUFFIX)]
         stem_of = {stem + ".weight": stem for stem in stems}
         owned = {m for stem in stems for m in _module_names(stem)}
-        lib = _require_gpu()
+        lib = glint_cuda.require_gpu("GLINT expand", "the reference's glint_unpin.py")
         if "_glint_cells" in where:
             s, e = where["_glint_cells"]
             compiled = np.empty(256, dtype="<f4")
@@ -121,7 +122,7 @@ def unpin(pin_dir: Path, out: Path, dtype: str = "BF16") -> dict:
         n_expanded = 0
         for s in shard_names:
             entries = plan[s]
-            wt = _ShardWriter(Writer(str(out / s), [(n, d, sh, nb) for n, d, sh, nb, _ in entries],
+            wt = ThreadedWriter(Writer(str(out / s), [(n, d, sh, nb) for n, d, sh, nb, _ in entries],
                                      {"format": "pt", "unpinned_from": "glint"}))
             ok = False
             try:
