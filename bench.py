@@ -666,6 +666,39 @@ def cpu_encode_sample(seconds: float = 10.0):
             "sample": f"{done // n} x one 4096x4096 BF16 tensor of config 2 ({done / 1e6:.0f} M weights, {dt:.1f} s)"}
 
 
+def cpu_other_paths(seconds: float = 3.0):
+    """The reference's host paths for the other kernels, on the same sample tensor and
+    host cores: expand to BF16 (the oracle's C restatement of glint_np.expand +
+    f32_to_bf16_bytes, all cores) and the host GEMV, numpy x @ W.T on the expanded
+    f32 weights (numpy's BLAS threads), each repeated for about `seconds`."""
+    import numpy as np
+    O, bits, threads = _cpu_sample()
+    n = bits.size
+    ho, po, ao = O.encode_bf16(bits, BS)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        O.expand_bf16(ho, po, ao, n, BS)
+        done += n
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    W = O.expand_f32(ho, po, ao, n, BS).reshape(4096, 4096)
+    x = np.random.default_rng(1).normal(0, 1, (1, 4096)).astype(np.float32)
+    x @ W.T
+    calls, t1 = 0, time.perf_counter()
+    while True:
+        x @ W.T
+        calls += 1
+        if time.perf_counter() - t1 >= seconds:
+            break
+    dg = time.perf_counter() - t1
+    return {"expand_bf16": {"value": round(done * 2 / dt / 1e9, 4), "unit": "GB/s of BF16 output", "cores": threads,
+                            "kind": "port", "sample": f"{done // n} x the 4096x4096 sample ({dt:.1f} s)"},
+            "gemv_m1": {"us_per_call": round(dg / calls * 1e6, 1), "gweights_per_s": round(n * calls / dg / 1e9, 3),
+                        "kind": "numpy", "sample": f"{calls} x x[1,4096] @ W.T, W the expanded f32 4096x4096 "
+                                                   f"(64 MB), numpy's BLAS threads ({dg:.1f} s)"}}
+
+
 def bench_reference(args):
     """The reference arm: the CPU encode (oracle port on all host cores), W warm-up
     and K timed steps, each step a bounded sample of the workload; the whole run
@@ -768,6 +801,7 @@ def main():
     if not args.no_cpu_baseline and int(os.environ.get("RANK", "0")) == 0 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
         # the CPU baseline runs first, before this process creates a CUDA context
         cb = cpu_encode_sample()
+        cb["other_paths"] = cpu_other_paths()
     rank, result = bench_glint(args)
     if rank == 0:
         result["cpu_baseline"] = cb
