@@ -76,6 +76,30 @@ def test_bad_arguments_rejected_without_gpu(lib):
     assert lib.glint_htile_stream(p, p, p, p, p, 0, 1, 1, 1, 64, 9, None) == -1   # bad mode
 
 
+def test_codebook_export_and_sqerr_arguments_without_gpu(lib):
+    """glint_cells_f32 returns the pinned codebook (the bits the reference's
+    glint_codec.CELLS holds, tests/golden/tables.json) with no GPU; the
+    glint_encode_*_host_sqerr entries check their arguments before any device work
+    and give a zero sum for an empty tensor."""
+    import json
+    import numpy as np
+    cells = np.empty(256, dtype="<f4")
+    assert lib.glint_cells_f32(cells.ctypes.data) == 256
+    want = json.loads((ROOT / "tests" / "golden" / "tables.json").read_text())["cells_bits"]
+    assert cells.view("<u4").tolist() == want
+    assert lib.glint_cells_f32(None) == -1
+    buf = (ctypes.c_uint8 * 64)()
+    p = ctypes.addressof(buf)
+    sq = ctypes.c_double(-1.0)
+    for f in (lib.glint_encode_bf16_host_sqerr, lib.glint_encode_f32_host_sqerr):
+        assert f(p, 4, 64, p, p, p, None) == -1                       # no sum pointer
+        assert f(p, -1, 64, p, p, p, ctypes.byref(sq)) == -1          # n < 0
+        assert f(p, 4, 0, p, p, p, ctypes.byref(sq)) == -1            # blocksize <= 0
+        assert f(None, 4, 64, p, p, p, ctypes.byref(sq)) == -1        # null input
+        sq.value = -1.0
+        assert f(p, 0, 64, p, p, p, ctypes.byref(sq)) == 0 and sq.value == 0.0   # empty tensor
+
+
 def test_gathered_decode_and_ipc_reject_bad_arguments_without_gpu(lib):
     """glint_htile_gather_stream and the IPC helpers check their arguments before
     touching a device (include/glint_htile.h; -1 bad argument, -2 blocksize)."""
