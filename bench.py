@@ -760,6 +760,13 @@ def profile_case(case: str, iters: int = 5):
         y = torch.empty((M, 14336), dtype=torch.float32, device="cuda")
         n = 14336 * 4096
         fn = lambda: D.htile(x, *planes[0], 14336, BS, mode="fast", out=y)  # noqa: E731
+    elif case.startswith("gemvt"):
+        # the down_proj shape, K = 14336, N = 4096: the same planes read as [4096, 14336]
+        M = int(case[5:] or 1)
+        x = torch.randn((M, 14336), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, 4096), dtype=torch.float32, device="cuda")
+        n = 14336 * 4096
+        fn = lambda: D.htile(x, *planes[0], 4096, BS, mode="fast", out=y)  # noqa: E731
     elif case.startswith("gemv"):
         M = int(case[4:] or 1)
         x = torch.randn((M, 4096), generator=g, device="cuda").to(torch.bfloat16)

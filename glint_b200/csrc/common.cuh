@@ -64,6 +64,30 @@ __device__ __forceinline__ float warp_sum(float v)
 
 inline bool aligned_to(const void *p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
 
+/* Read-and-clear of a kernel error word as one device atomic, so a bit that a
+ * still-running kernel sets between a read and a reset cannot be lost. */
+static __global__ void take_word_kernel(int *word, int *out) { *out = atomicExch(word, 0); }
+
+/* Value of the __device__ int `word` of the calling translation unit; with `clear`,
+ * taken and zeroed atomically (through `taken`, another __device__ int of that
+ * unit).  Synchronous on the legacy default stream; -1 on a CUDA error. */
+template <class W>
+inline int read_error_word(W &word, W &taken, bool clear)
+{
+    int v = 0;
+    if (!clear)
+        return cudaMemcpyFromSymbol(&v, word, sizeof(int)) == cudaSuccess ? v : -1;
+    void *pw = nullptr, *pt = nullptr;
+    if (cudaGetSymbolAddress(&pw, word) != cudaSuccess || cudaGetSymbolAddress(&pt, taken) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    take_word_kernel<<<1, 1, 0, 0>>>(static_cast<int *>(pw), static_cast<int *>(pt));
+    if (cudaGetLastError() != cudaSuccess || cudaMemcpyFromSymbol(&v, taken, sizeof(int)) != cudaSuccess)
+        return -1;
+    return v;
+}
+
 } // namespace glint
 
 #endif

@@ -54,6 +54,7 @@
 namespace glint {
 
 __device__ int g_encode_error = 0;
+__device__ int g_encode_error_taken = 0; /* read_error_word's result slot */
 
 namespace {
 
@@ -672,16 +673,6 @@ int encode_launch(const EncodeJob *jobs, int count, int bs, bool f32_in, cudaStr
 }
 
 /* This file's kernel error word (bounded waits that ran out); clear resets it. */
-int encode_error_word(bool clear)
-{
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_encode_error, sizeof(int)) != cudaSuccess)
-        return -1;
-    if (clear && v) {
-        const int z = 0;
-        cudaMemcpyToSymbol(g_encode_error, &z, sizeof(int));
-    }
-    return v;
-}
+int encode_error_word(bool clear) { return read_error_word(g_encode_error, g_encode_error_taken, clear); }
 
 } // namespace glint

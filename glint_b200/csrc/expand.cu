@@ -32,6 +32,7 @@
 namespace glint {
 
 __device__ int g_expand_error = 0;
+__device__ int g_expand_error_taken = 0; /* read_error_word's result slot */
 
 namespace {
 
@@ -433,16 +434,6 @@ int sq_error_launch(const void *w, bool f32_in, const uint8_t *hole, const uint8
 }
 
 /* This file's kernel error word (bounded waits that ran out); clear resets it. */
-int expand_error_word(bool clear)
-{
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_expand_error, sizeof(int)) != cudaSuccess)
-        return -1;
-    if (clear && v) {
-        const int z = 0;
-        cudaMemcpyToSymbol(g_expand_error, &z, sizeof(int));
-    }
-    return v;
-}
+int expand_error_word(bool clear) { return read_error_word(g_expand_error, g_expand_error_taken, clear); }
 
 } // namespace glint

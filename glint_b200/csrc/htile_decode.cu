@@ -48,6 +48,7 @@
 namespace glint {
 
 __device__ int g_decode_error = 0;
+__device__ int g_decode_error_taken = 0; /* read_error_word's result slot */
 
 namespace {
 
@@ -1260,16 +1261,77 @@ int decode_launch_impl(const uint8_t *hole, const uint8_t *plug, const float *am
  * per-stream workspace above: kNoAllocBytes per device, allocated with the
  * library's device image when it is loaded on a device and held until the
  * process exits.  The first kNoAllocCounterBytes hold the per (row block, part,
- * warp) split-block flags, the rest the split-K partial sums. */
+ * warp) split-block flags, the rest the split-K partial sums: rb x parts x 256
+ * rows x 8 MT floats (rb row blocks, parts as max_parts below), so calls whose
+ * sums exceed 4 MiB - 64 KiB return kScratch.  Only the stream-K kernel uses it;
+ * row-owned shapes need no scratch. */
 constexpr size_t kNoAllocBytes = size_t(4) << 20;   /* 4 MiB per device */
 constexpr size_t kNoAllocCounterBytes = 64 << 10;   /* 16384 flags (row blocks x parts x warps) */
 constexpr int kNoAllocMaxN = 65536;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 namespace {
+/* The array's device address, looked up once per device and context: keyed on the
+ * context's process-unique id, so a context destroyed by cudaDeviceReset and
+ * created again gets a fresh lookup instead of a dangling address. */
+struct NoAllocAddr {
+    unsigned long long ctx_id = 0;
+    void *addr = nullptr;
+};
 std::mutex g_noalloc_mu;
-void *g_noalloc_addr[64] = {};
+NoAllocAddr g_noalloc_addr[64];
+
+using PFN_ctxGetCurrent = CUresult (*)(CUcontext *);
+using PFN_ctxGetId = CUresult (*)(CUcontext, unsigned long long *);
+
+/* id of the calling thread's current context (0 when none is current or the driver
+ * entry points are unavailable) */
+unsigned long long current_ctx_id()
+{
+    static PFN_ctxGetCurrent get_cur = nullptr;
+    static PFN_ctxGetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr, *q = nullptr;
+        cudaDriverEntryPointQueryResult r1, r2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r1) == cudaSuccess &&
+            r1 == cudaDriverEntryPointSuccess &&
+            cudaGetDriverEntryPoint("cuCtxGetId", &q, cudaEnableDefault, &r2) == cudaSuccess &&
+            r2 == cudaDriverEntryPointSuccess) {
+            get_cur = reinterpret_cast<PFN_ctxGetCurrent>(p);
+            get_id = reinterpret_cast<PFN_ctxGetId>(q);
+        } else {
+            cudaGetLastError();
+        }
+    });
+    CUcontext c = nullptr;
+    unsigned long long id = 0;
+    if (!get_cur || !get_id || get_cur(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
 }
+
+/* Device address of g_noalloc_scratch on the current device (nullptr on failure). */
+void *noalloc_base(int dev)
+{
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocAddr &e = g_noalloc_addr[dev];
+    const unsigned long long id = current_ctx_id();
+    if (e.addr && id != 0 && id == e.ctx_id)
+        return e.addr;
+    /* host code only sees a stand-in for the array: ask the runtime for its device
+     * address with this device current (this also creates the context if needed) */
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        e = NoAllocAddr{};
+        return nullptr;
+    }
+    e.addr = p;
+    e.ctx_id = current_ctx_id();
+    return p;
+}
+} // namespace
 
 int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
                         OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
@@ -1303,21 +1365,9 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return kLaunch;
-    void *base = nullptr;
-    {
-        std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        if (!g_noalloc_addr[dev]) {
-            /* host code only sees a stand-in for the array: ask the runtime for its
-             * device address, once per device, with that device current */
-            void *p = nullptr;
-            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
-                cudaGetLastError();
-                return kLaunch;
-            }
-            g_noalloc_addr[dev] = p;
-        }
-        base = g_noalloc_addr[dev];
-    }
+    void *base = noalloc_base(dev);
+    if (!base)
+        return kLaunch;
     const int MT = M <= 8 ? 1 : (M <= 16 ? 2 : 4);
     DecodeArgs a{};
     a.x = x;
@@ -1350,16 +1400,6 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
 }
 
 /* This file's kernel error word (bounded waits that ran out); clear resets it. */
-int decode_error_word(bool clear)
-{
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_decode_error, sizeof(int)) != cudaSuccess)
-        return -1;
-    if (clear && v) {
-        const int z = 0;
-        cudaMemcpyToSymbol(g_decode_error, &z, sizeof(int));
-    }
-    return v;
-}
+int decode_error_word(bool clear) { return read_error_word(g_decode_error, g_decode_error_taken, clear); }
 
 } // namespace glint

@@ -55,6 +55,7 @@
 namespace glint {
 
 __device__ int g_glint_kernel_error = 0;
+__device__ int g_glint_kernel_error_taken = 0; /* read_error_word's result slot */
 
 namespace {
 
@@ -778,13 +779,9 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
 
 int read_kernel_error(bool clear)
 {
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, g_glint_kernel_error, sizeof(int)) != cudaSuccess)
+    const int v = read_error_word(g_glint_kernel_error, g_glint_kernel_error_taken, clear);
+    if (v < 0)
         return -1;
-    if (clear && v) {
-        const int z = 0;
-        cudaMemcpyToSymbol(g_glint_kernel_error, &z, sizeof(int));
-    }
     const int e = encode_error_word(clear), x = expand_error_word(clear), d = decode_error_word(clear);
     if (e < 0 || x < 0 || d < 0)
         return -1;

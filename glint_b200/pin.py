@@ -64,26 +64,30 @@ def _is_linear(name: str, dtype: str, shape) -> bool:
 
 
 def resolve_shards(src: Path) -> List[Path]:
-    """Source -> ordered shard list, by the reference's rules (glint_pin.py:45-64): a file;
-    or a dir with model.safetensors, an index (its shards, sorted), or exactly one shard."""
-    src = Path(src).expanduser().resolve()
-    if not src.is_dir():
-        return [src]
-    single = src / "model.safetensors"
-    if single.is_file():
-        return [single]
-    index = src / INDEX_NAME
+    """The shard files a pin reads, in order.  The reference tool's rules
+    (glint_pin.py:45-64), in order of precedence:
+    - a path that is not a directory is the one shard;
+    - a directory's consolidated `model.safetensors`;
+    - else the shards its index's weight map names, each once, in name order (a
+      named shard that is absent is an error);
+    - else the directory's only `.safetensors` file (none or several is an error)."""
+    root = Path(src).expanduser().resolve()
+    if not root.is_dir():
+        return [root]
+    files = {p.name: p for p in root.glob("*.safetensors") if p.is_file()}
+    if "model.safetensors" in files:
+        return [files["model.safetensors"]]
+    index = root / INDEX_NAME
     if index.is_file():
         weight_map: Dict[str, str] = json.loads(index.read_text())["weight_map"]
-        names = sorted(set(weight_map.values()))
-        missing = [n for n in names if not (src / n).is_file()]
-        if missing:
-            raise FileNotFoundError(f"{INDEX_NAME} names missing shards: {missing}")
-        return [src / n for n in names]
-    shards = sorted(src.glob("*.safetensors"))
-    if len(shards) != 1:
-        raise FileNotFoundError(f"need model.safetensors, {INDEX_NAME}, or exactly one .safetensors in {src}")
-    return shards
+        chosen = [root / name for name in sorted(frozenset(weight_map.values()))]
+        absent = [p.name for p in chosen if not p.is_file()]
+        if absent:
+            raise FileNotFoundError(f"{INDEX_NAME} names missing shards: {absent}")
+        return chosen
+    if len(files) == 1:
+        return list(files.values())
+    raise FileNotFoundError(f"need model.safetensors, {INDEX_NAME}, or exactly one .safetensors in {root}")
 
 
 def _state(blocksize: int, shape, dtype: str) -> bytes:

@@ -58,12 +58,22 @@ int glint_htile_stream(
  * fixed before the first call).  No counterpart in the reference ABI.
  * It allocates nothing: the split-K partial sums and counters live in one 4 MiB
  * array compiled into the library, which every GPU that loads the library holds
- * until the process exits.  The first call on a device looks the array's device
- * address up; make that first call before any stream capture.  All calls share
- * the array, so calls that overlap on the GPU (other streams, other threads) race
- * and give wrong results; serialise them.  Limits: M <= 32, blocksize == 64,
- * K % 256 == 0, 16-byte aligned pointers (-1 otherwise), N <= 65536 and the
- * partial sums within the array (-5 GLINT_ERR_SCRATCH otherwise). */
+ * until the process exits.  The first call on a device (and the first after a
+ * device reset) looks the array's device address up; make that first call before
+ * any stream capture.  All calls share the array, so calls that overlap on the
+ * GPU (other streams, other threads) race and give wrong results; serialise them.
+ * Limits: M <= 32, blocksize == 64, K % 256 == 0, 16-byte aligned pointers (-1
+ * otherwise); N <= 65536, else -5 GLINT_ERR_SCRATCH.
+ * Only stream-K shapes use the array: N < 16, N > 224 x SMs (33152 on a B200's
+ * 148 SMs), or N < 16 x SMs with K > 8192; the others need no scratch.  Those
+ * return -5 unless their partial sums fit 4 MiB - 64 KiB:
+ *   rb x parts x 256 x 8 MT x 4 bytes <= 4128768, where
+ *   MT = 1 (M <= 8), 2 (M <= 16), 4 (M <= 32); ku = K / 256 (M <= 16) or K / 128;
+ *   rb = ceil(N / 256); units = rb x ku; ctas = min(units, SMs);
+ *   parts = min(ctas, ceil(ku / max(1, floor(units / ctas))) + 1).
+ * On 148 SMs, for example: M <= 8 covers N up to about 64000 at any K; M = 4,
+ * N = 1024, K = 14336 fits (1.9 MB); M = 16, N = 1024, K = 16384 (4.3 MB) and
+ * M = 1, N = 65536, K = 4096 (4.2 MB) return -5. */
 #define GLINT_ERR_SCRATCH (-5)
 int glint_htile_stream_noalloc(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,

@@ -21,9 +21,21 @@ HERE = Path(__file__).resolve().parent
 _LIB = None
 
 
+def reference_checkout() -> Path | None:
+    """The read-only reference checkout: GLINT_REFERENCE if set, else a checkout named
+    `reference` beside this repository; None when neither exists."""
+    env = os.environ.get("GLINT_REFERENCE")
+    cand = Path(env) if env else HERE.parent.parent / "reference"
+    return cand if (cand / "cuda" / "glint_encode.cu").is_file() else None
+
+
 def build() -> Path:
     """Compile the oracle (and oracle/_ref when the reference checkout is present)."""
-    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    env = dict(os.environ)
+    ref = reference_checkout()
+    if ref is not None:
+        env["GLINT_REFERENCE"] = str(ref)
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True, env=env)
     return HERE / "libglint_oracle.so"
 
 

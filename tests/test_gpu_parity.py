@@ -458,6 +458,60 @@ def test_htile_prefill_tcgen05_vs_oracle(M, N, K):
     assert rel_err(yr.cpu().numpy(), ref) <= PRECISE_TOL, rel_err(yr.cpu().numpy(), ref)
 
 
+_FULL_PLANES = {}
+
+
+def _full_size_planes(N, K):
+    """Planes of one [N, K] weight drawn as the prefill config draws them (N(0, 0.02),
+    exactly 0.1 % of entries x20 without replacement, BF16 RNE), encoded by the oracle;
+    cached per shape so the six shapes encode two weights."""
+    if (N, K) not in _FULL_PLANES:
+        _FULL_PLANES.clear()
+        bits = synth_bf16(N * K, seed=N + K)
+        ho, po, ao = O.encode_bf16(bits, 64)
+        _FULL_PLANES[(N, K)] = (ho, po, ao, [torch.from_numpy(a).cuda() for a in (ho, po, ao)])
+    return _FULL_PLANES[(N, K)]
+
+
+def _sample_rows(M, count=64):
+    """count rows of an M-row activation: both ends, the 128/256-row tile edges and
+    evenly spread rows between them (y row m depends on x row m only)."""
+    edges = {0, 1, 127, 128, 255, 256, M // 2, M - 2, M - 1}
+    spread = np.linspace(0, M - 1, count - len(edges)).astype(np.int64)
+    return np.array(sorted(edges.union(spread.tolist())), np.int64)[:count]
+
+
+@pytest.mark.parametrize("N", [4096, 14336])
+@pytest.mark.parametrize("M", [512, 2048, 8192])
+def test_htile_prefill_full_config_vs_oracle(M, N):
+    """The prefill config at its full sizes (M in {512, 2048, 8192}, K = 4096,
+    N in {4096, 14336}): the tcgen05 kernel's full-size schedules (data-parallel
+    rounds and the stream-K remainder over 56 to 448 tiles per CTA pair) in fast mode
+    within max|y - y_ref| <= 1e-2 * max(1, max|y_ref|) of the oracle on a 64-row
+    sample of y (the oracle computes the sampled rows only), BF16 y too, and two
+    calls bit-identical."""
+    from glint_b200 import glint_cuda
+    L = glint_cuda.load()
+    K = 4096
+    ho, po, ao, dev = _full_size_planes(N, K)
+    x = O.f32_to_bf16(np.random.default_rng(M + N).normal(0, 1, M * K).astype(np.float32)).reshape(M, K)
+    rows = _sample_rows(M)
+    ref = O.htile(ho, po, ao, np.ascontiguousarray(x[rows]), len(rows), N, K, 64).astype(np.float64)
+    dx = to_dev_bf16(x.reshape(-1)).view(M, K)
+    yf = D().htile(dx, *dev, N, 64, mode="fast")
+    yf2 = D().htile(dx, *dev, N, 64, mode="fast")
+    yb = D().htile(dx, *dev, N, 64, mode="fast", out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert L.glint_kernel_error(1) == 0
+    assert torch.equal(yf, yf2)
+    idx = torch.from_numpy(rows).cuda()
+    got = yf.index_select(0, idx).cpu().numpy()
+    gotb = yb.index_select(0, idx).float().cpu().numpy()
+    assert np.all(np.isfinite(got))
+    assert rel_err(got, ref) <= FAST_TOL, rel_err(got, ref)
+    assert rel_err(gotb, ref) <= FAST_TOL, rel_err(gotb, ref)
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 100, 256), (3, 1000, 512), (16, 4096, 14336), (17, 384, 2048), (32, 200, 4096),
                                    (5, 14336, 4096), (2, 130, 768)])
 def test_htile_decode_stream_k_vs_oracle(M, N, K):
