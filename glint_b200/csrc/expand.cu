@@ -117,12 +117,12 @@ __global__ void __launch_bounds__(kExpThreads, 1) expand_stream_kernel(const __g
     uint64_t *full = reinterpret_cast<uint64_t *>(meta + kSlots);
     uint64_t *empty = full + kSlots;
 
-    if (threadIdx.x < 256) {
-        const float c = (&g_cells[0][0])[threadIdx.x];
-        float4 *dst = reinterpret_cast<float4 *>(lut + threadIdx.x * 64);
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-            dst[r] = make_float4(c, c, c, c);
+    /* 32 replicas per entry in the first 128 B of its 256-B row; a 16-byte store
+     * covers a quarter row, so each warp store fills four whole rows (no bank
+     * conflicts) */
+    for (int i = (int)threadIdx.x; i < 256 * 8; i += kExpThreads) {
+        const float c = (&g_cells[0][0])[i >> 3];
+        reinterpret_cast<float4 *>(lut + (i >> 3) * 64)[i & 7] = make_float4(c, c, c, c);
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {

@@ -92,6 +92,19 @@ __device__ __forceinline__ uint32_t split_pair(float c)
     return hi | (f32_to_bf16_bits(rest) << 16);
 }
 
+/* The per-lane codebook replicas, written by the consumer threads: each 16-byte
+ * store covers a quarter of one entry's 128-byte row of 32 replicas, so a warp's
+ * store fills four whole rows (four wavefronts, no bank conflicts; one thread per
+ * entry writing its own row would put all 32 lanes on the same four banks). */
+__device__ __forceinline__ void build_pair_lut(uint32_t *lut)
+{
+    for (int i = (int)threadIdx.x; i < 256 * 8; i += kConsumers * 32) {
+        const int e = i >> 3;
+        const uint32_t v = split_pair(g_cells[e >> 4][e & 15]);
+        reinterpret_cast<uint4 *>(lut + e * 64)[i & 7] = make_uint4(v, v, v, v);
+    }
+}
+
 /* Gathered output (world > 0): this call's rows [n0, n0 + N) of y[M, ldy] are
  * stored into every rank's y (yr[r], this rank's own included), then counted in
  * (gather_complete).  world == 0: plain y. */
@@ -379,15 +392,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     /* codebook as BF16 hi/lo pairs, one replica per lane (first 128 B of each 256-B
-     * entry row): each thread converts one entry and writes its 32 replicas; the
-     * consumer warps then meet on named barrier 1 (the producer is not in it) */
-    if (threadIdx.x < 256) {
-        const uint32_t e = split_pair(g_cells[threadIdx.x >> 4][threadIdx.x & 15]);
-        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 64);
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-            dst[r] = make_uint4(e, e, e, e);
-    }
+     * entry row); the consumer warps then meet on named barrier 1 (the producer is
+     * not in it) */
+    build_pair_lut(lut);
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     /* y, the workspace and its flags are touched only after the previous kernel
      * in the stream is complete (no-op without programmatic dependent launch) */
@@ -721,13 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return;
     }
 
-    if (threadIdx.x < 256) {
-        const uint32_t e = split_pair(g_cells[threadIdx.x >> 4][threadIdx.x & 15]);
-        uint4 *dst = reinterpret_cast<uint4 *>(lut + threadIdx.x * 64);
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-            dst[r] = make_uint4(e, e, e, e);
-    }
+    build_pair_lut(lut);
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int g = (int)(lane >> 2), t = (int)(lane & 3), pg = frag_row<128>(g);
