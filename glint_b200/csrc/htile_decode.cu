@@ -217,9 +217,11 @@ __device__ __forceinline__ int frag_row(int g)
 /* One 64-k absmax block of a 16-row weight tile against the activations:
  * acc[mt] += absmax * (W[rows r0+g, r0+g+8][block] . x[mt*8+g'][block]).
  * `hole`/`plug`: plane tiles with ROWB-byte rows (128: 128B swizzle, 16-byte chunk j
- * of row r at j ^ (r & 7); 64: 64B swizzle, j ^ ((r >> 1) & 3)), the block at byte
- * 32*c of a row; `am`: absmax rows of 16 bytes, this block in column am_col; `xbox`:
- * the block's activation box, 8*MT rows x 128 B, 128B swizzle.  Swap-AB
+ * of row r at j ^ (r & 7); 64: 64B swizzle, j ^ ((r >> 1) & 3)), 1 KB aligned; the
+ * tile's rows start at row `ro` of them (the swizzle phase follows the row's place
+ * in the tile, ro + r); the block at byte 32*c of a row; `am`: absmax rows of 16
+ * bytes (row ro + r), this block in column am_col; `xbox`: the block's activation
+ * rows of 128 B (128B swizzle) whose first row has swizzle phase `xph`.  Swap-AB
  * mma.sync.m16n8k16: weights are the A operand (lane (g, t) holds rows
  * frag_row(g) and frag_row(g)+8),
  * activations the B operand read with the same k map, so the dot product is exact
@@ -228,14 +230,14 @@ __device__ __forceinline__ int frag_row(int g)
  * take zeros without reading shared memory. */
 template <int MT, bool SPLIT, int ROWB>
 __device__ __forceinline__ void tile_block(uint32_t hole, uint32_t plug, uint32_t am, uint32_t am_col, uint32_t xbox,
-                                           int c, int r0, int g, int t, uint32_t lut_base, uint32_t lane4, int M,
-                                           float (&acc)[MT][4])
+                                           uint32_t xph, int c, int r0, int ro, int g, int t, uint32_t lut_base,
+                                           uint32_t lane4, int M, float (&acc)[MT][4])
 {
     uint32_t E[2][2], O[2][2];
     float sc[2];
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-        const int row = r0 + frag_row<ROWB>(g) + 8 * r;
+        const int row = ro + r0 + frag_row<ROWB>(g) + 8 * r;
         const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(ROWB == 128 ? (row & 7) : ((row >> 1) & 3));
         const uint32_t off = (uint32_t)row * (uint32_t)ROWB + (chunk << 4) + (uint32_t)(t & 1) * 8u;
         const uint2 hw = lds64(hole + off), pw = lds64(plug + off);
@@ -247,15 +249,17 @@ __device__ __forceinline__ void tile_block(uint32_t hole, uint32_t plug, uint32_
         }
         sc[r] = __uint_as_float(lds32(am + (uint32_t)row * 16u + am_col * 4u));
     }
-    /* x fragments: row m = mt*8 + g of the box, 16 consecutive k at 32*t bytes
-     * (16-byte chunks 2t and 2t+1, 128B swizzle: chunk ^ (m & 7)) */
+    /* x fragments: row m = mt*8 + g of the block's rows, 16 consecutive k at 32*t
+     * bytes (16-byte chunks 2t and 2t+1, 128B swizzle: chunk ^ ((xph + m) & 7)) */
     uint4 xb[MT][2];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-        const uint32_t rowb = xbox + (uint32_t)(mt * 8 + g) * 128u;
-        const bool live = mt * 8 + g < M;
-        xb[mt][0] = lds128_if(rowb + ((uint32_t)((2 * t) ^ g) << 4), live);
-        xb[mt][1] = lds128_if(rowb + ((uint32_t)((2 * t + 1) ^ g) << 4), live);
+        const int m = mt * 8 + g;
+        const uint32_t rowb = xbox + (uint32_t)m * 128u;
+        const uint32_t ph = (xph + (uint32_t)m) & 7u;
+        const bool live = m < M;
+        xb[mt][0] = lds128_if(rowb + (((uint32_t)(2 * t) ^ ph) << 4), live);
+        xb[mt][1] = lds128_if(rowb + (((uint32_t)(2 * t + 1) ^ ph) << 4), live);
     }
     /* two accumulators (even and odd MMA steps) keep the chains independent */
     float part[2][MT][4];
@@ -533,7 +537,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < kKU / 64; ++c)
             tile_block<MT, SPLIT, kKU / 2>(slot, slot + kPlaneTile, slot + 2 * kPlaneTile, am_col + c,
-                                           xs + (uint32_t)c * (8 * MT * 128), c, r0, g, t, lut_base, lane4, a.M, acc);
+                                           xs + (uint32_t)c * (8 * MT * 128), 0u, c, r0, 0, g, t, lut_base, lane4, a.M,
+                                           acc);
         __syncwarp();
         if (lane == 0)
             mbar_arrive(&empty[s]);
@@ -549,11 +554,14 @@ __global__ void __launch_bounds__(kThreads, 1)
  * [c*R, (c+1)*R), R = ceil(N / ctas), over the whole K, so no row is split between
  * CTAs: no workspace, no cross-CTA sums, and the per-SM work differs by at most
  * one row.  Its rows go in row blocks of RB <= 112 (7 tiles of 16).  A unit is
- * (row block, UB x 256 k): per 256 k, hole and plug tiles [RB rows x 128 B] (128B
- * swizzle), an absmax box [RB rows x 4 blocks] and the activation slice (only the
- * M rows that exist), through a TMA ring whose stage size follows RB, so narrow
- * row blocks take two 256-k slices per stage and more stages: the bytes in flight
- * per SM stay near the same whatever RB is.  Consumer warp w works on tile w / KH
+ * (row block, UB x 256 k), loaded into one ring stage by four 3-D TMA requests:
+ * hole and plug [UB slices][RB rows][128 B] (128B swizzle), absmax
+ * [UB][RB][4 blocks] and the activations [4 UB blocks][M rows][64 k] (128B
+ * swizzle; only the M rows that exist).  Narrow row blocks take up to four 256-k
+ * slices per unit: a TMA request then carries ~14 KB instead of one slice's 3.5 KB
+ * (with 28-row blocks, one slice per request streamed 62 MB in ~20 us, four in
+ * ~11 us), and the bytes in flight per SM stay near the same whatever RB is.
+ * Consumer warp w works on tile w / KH
  * and NB = 4*UB/KH of every unit's 64-k blocks (unrolled, so the blocks' shared
  * loads and MMAs interleave); at the end of a row block the KH partial sums of a
  * tile are added in k order through shared memory (bounded mbarrier handshakes)
@@ -561,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kRowBlockMax = 112;
 constexpr int kRMaxStages = 8;
 template <int MT>
-constexpr int r_xsub() { return 4 * 8 * MT * 128; } /* activation boxes of 256 k, 1 KB apart per 8 rows */
+constexpr int r_xsub() { return 4 * 8 * MT * 128; } /* activation rows of 256 k: 4 blocks x up to 8 MT rows */
 /* ring capacity: 4 (MT 1) or 3 stages of the widest row block and one 256-k slice */
 template <int MT>
 constexpr int r_ring() { return (MT == 1 ? 4 : 3) * (2 * kRowBlockMax * 128 + 2048 + r_xsub<MT>()); }
@@ -569,8 +577,8 @@ constexpr int r_ring() { return (MT == 1 ? 4 : 3) * (2 * kRowBlockMax * 128 + 20
 template <int MT>
 constexpr int r_scratch_floats() { return (MT <= 2 ? 14 : 7) * 32 * 4 * MT; }
 /* one unit of a shared tail tile (MT <= 2): hole and plug 16 x 128 B, absmax
- * 16 x 16 B in 1 KB, four activation boxes, and the partial sums of 3 of the 4
- * warps that share it (32 lanes x 4 MT floats each) */
+ * 16 x 16 B in 1 KB, the unit's activations [4 blocks][M rows][64 k], and the
+ * partial sums of 3 of the 4 warps that share it (32 lanes x 4 MT floats each) */
 constexpr int kTailWarps = 4;
 constexpr int kTailX = 5 * 1024; /* offset of the activation boxes */
 template <int MT>
@@ -593,10 +601,11 @@ struct RowArgs {
     int T;  /* 16-row tiles per row block */
     int KH; /* consumer warps per tile */
     int S;  /* ring stages */
-    int pt; /* bytes of a plane tile (RB x 128, 1 KB aligned) */
-    int at; /* bytes of an absmax tile (RB x 16, 1 KB aligned) */
-    int sub;   /* bytes of a 256-k slice: 2 pt + at + activation boxes */
-    int xrows; /* activation rows per box: min(M, 8 MT) */
+    int pt; /* bytes of a unit's plane tile (UB x RB x 128, 1 KB aligned) */
+    int at; /* bytes of its absmax tile (UB x RB x 16, 1 KB aligned) */
+    int xt; /* bytes of its activation tile (4 UB x xrows x 128, 1 KB aligned) */
+    int stage; /* bytes of a ring stage: 2 pt + at + xt */
+    int xrows; /* activation rows loaded: min(M, 8 MT) */
     uint32_t tx; /* TMA bytes per stage */
     GatherArgs ga;
     /* Shared tail: when the 16-row tiles do not divide evenly over the SMs, every
@@ -633,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *tail_full = cmb_empty + 1;      /* the tail unit's planes, absmax and activations landed */
     uint32_t *cta_done = reinterpret_cast<uint32_t *>(tail_full + 1); /* gathered calls: warps done */
     const int S = a.S, KH = a.KH;
-    const int stage_bytes = a.UB * a.sub;
+    const int stage_bytes = a.stage;
 
     const int active = a.T * KH;
     const bool has_tail = MT <= 2 && (int)blockIdx.x < a.tail_units;
@@ -664,13 +673,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kConsumers) {
         if (lane == 0) {
+            /* the unit's activations: blocks [4 UB ku, 4 UB (ku + 1)) of every row */
             auto load_x = [&](int ku, int s) {
-                for (int sb = 0; sb < a.UB; ++sb) {
-                    uint8_t *xs = ring + s * stage_bytes + sb * a.sub + 2 * a.pt + a.at;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-                        tma_load_2d(xs + c * (8 * MT * 128), &xmap, &full[s], (ku * a.UB + sb) * 256 + c * 64, 0);
-                }
+                tma_load_3d(ring + s * stage_bytes + 2 * a.pt + a.at, &xmap, &full[s], 0, 0, ku * a.UB * 4);
             };
             /* the tail unit first, so its warps work beside the row blocks (one
              * 256-k slice: the ring's units have UB == 1 whenever a tail is set) */
@@ -690,24 +695,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int nb0 = n_begin + blk * a.RB;
                 uint8_t *st = ring + s * stage_bytes;
                 mbar_expect_tx(&full[s], a.tx);
-                for (int sb = 0; sb < a.UB; ++sb) {
-                    uint8_t *ss = st + sb * a.sub;
-                    const int k256 = ku * a.UB + sb;
-                    tma_load_2d(ss, &hmap, &full[s], k256 * 128, nb0);
-                    tma_load_2d(ss + a.pt, &pmap, &full[s], k256 * 128, nb0);
-                    tma_load_2d(ss + 2 * a.pt, &amap, &full[s], k256 * 4, nb0);
-                }
+                /* slices [UB ku, UB (ku + 1)) of rows [nb0, nb0 + RB): one request per tensor */
+                tma_load_3d(st, &hmap, &full[s], 0, nb0, ku * a.UB);
+                tma_load_3d(st + a.pt, &pmap, &full[s], 0, nb0, ku * a.UB);
+                tma_load_3d(st + 2 * a.pt, &amap, &full[s], 0, nb0, ku * a.UB);
                 if (i >= S) {
                     load_x(ku, s);
                 } else if (i == S - 1 || i == units - 1) {
                     /* weights stream before the previous kernel is done, activations after
                      * (programmatic dependent launch; a no-op otherwise) */
                     asm volatile("griddepcontrol.wait;" ::: "memory");
-                    if (has_tail) {
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            tma_load_2d(tail + kTailX + c * (8 * MT * 128), &xmap, tail_full, tail_ku * 256 + c * 64, 0);
-                    }
+                    if (has_tail) /* UB == 1 whenever a tail is set: the map's box is one 256-k slice */
+                        tma_load_3d(tail + kTailX, &xmap, tail_full, 0, 0, tail_ku * 4);
                     for (int j = 0; j <= i; ++j)
                         load_x(j % a.KU, j);
                 }
@@ -750,8 +749,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t ts = saddr(tail);
             if (__shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0))
                 tile_block<MT, SPLIT, 128>(ts, ts + 2048, ts + 4096, (uint32_t)j,
-                                           ts + (uint32_t)(kTailX + j * (8 * MT * 128)), j, 0, g, t, lut_base, lane4,
-                                           a.M, acc);
+                                           ts + (uint32_t)(kTailX + j * a.xrows * 128), (uint32_t)(j * a.xrows) & 7u, j,
+                                           0, 0, g, t, lut_base, lane4, a.M, acc);
             float4 *part = reinterpret_cast<float4 *>(tail + kTailX + r_xsub<MT>());
             if (j > 0) {
 #pragma unroll
@@ -844,11 +843,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t st = saddr(ring + s * stage_bytes);
 #pragma unroll
             for (int j = 0; j < NB; ++j) {
-                const int b = b0 + j, c = b & 3;
-                const uint32_t ss = st + (uint32_t)((b >> 2) * a.sub);
-                tile_block<MT, SPLIT, 128>(ss, ss + a.pt, ss + 2 * a.pt, (uint32_t)c,
-                                           ss + 2 * a.pt + a.at + (uint32_t)c * (8 * MT * 128), c, r0, g, t,
-                                           lut_base, lane4, a.M, acc);
+                /* block b: 64-k block c of slice u, whose rows start at row u RB of the
+                 * plane and absmax tiles; activation block 4 u + c */
+                const int b = b0 + j, c = b & 3, u = b >> 2, xb = b * a.xrows;
+                tile_block<MT, SPLIT, 128>(st, st + a.pt, st + 2 * a.pt, (uint32_t)c,
+                                           st + 2 * a.pt + a.at + (uint32_t)xb * 128u, (uint32_t)xb & 7u, c, r0,
+                                           u * a.RB, g, t, lut_base, lane4, a.M, acc);
             }
             __syncwarp();
             if (lane == 0)
@@ -929,6 +929,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder()
             cudaGetLastError();
     });
     return fn;
+}
+
+/* 3-D map: dims (d0, d1, d2) with byte strides s1, s2 for dims 1 and 2 (any order
+ * of sizes), box (b0, b1, b2). */
+bool make_map3(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
+               uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw)
+{
+    auto enc = encoder();
+    if (!enc)
+        return false;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows,
@@ -1068,7 +1084,10 @@ int launch_rows_t(const Maps &m, const RowArgs &a, int grid, cudaStream_t st, bo
 
 constexpr int align1k(int v) { return (v + 1023) & ~1023; }
 
-/* Row block, warp and ring layout of the row-owned kernel for R rows per CTA. */
+/* Row block, warp and ring layout of the row-owned kernel for R rows per CTA.
+ * Units take as many 256-k slices (UB = 4, 2, 1) as keep >= 3 ring stages, the
+ * consumer warps' plan valid and K whole; row blocks of more than 4 tiles take
+ * one (their requests are large already, and the shared tail needs UB = 1). */
 bool plan_rows(RowArgs &a, int R, int MT)
 {
     const int M = a.M, K = a.K;
@@ -1076,35 +1095,37 @@ bool plan_rows(RowArgs &a, int R, int MT)
     a.nb = (a.R + kRowBlockMax - 1) / kRowBlockMax;
     a.RB = (a.R + a.nb - 1) / a.nb;
     a.T = (a.RB + 15) / 16;
-    /* warps per tile and 256-k slices per unit: as many consumer warps as the 16
-     * allow, two blocks per warp and unit where that still fills them (MT 4: one,
-     * for registers), two slices per unit for row blocks of <= 4 tiles */
-    a.UB = (a.T <= 4 && MT <= 2 && K % 512 == 0) ? 2 : 1;
-    const int blocks = 4 * a.UB, scratch_warps = MT <= 2 ? 14 : 7;
-    int nbk = MT <= 2 ? 2 : 1;
-    a.KH = blocks / nbk;
-    while ((a.T * a.KH > kConsumers || a.T * (a.KH - 1) > scratch_warps) && nbk < blocks) {
-        nbk *= 2;
-        a.KH = blocks / nbk;
-    }
-    if (a.T * a.KH < kConsumers / 2 && nbk > 1 && a.T * a.KH * 2 <= kConsumers &&
-        a.T * (a.KH * 2 - 1) <= scratch_warps) {
-        nbk /= 2;
-        a.KH = blocks / nbk;
-    }
-    if (a.T * a.KH > kConsumers || a.T * (a.KH - 1) > scratch_warps || nbk > 2)
-        return false;
-    a.KU = K / (256 * a.UB);
     a.xrows = std::min(M, 8 * MT);
-    a.pt = align1k(a.RB * 128);
-    a.at = align1k(a.RB * 16);
-    a.sub = 2 * a.pt + a.at + (MT == 1 ? r_xsub<1>() : MT == 2 ? r_xsub<2>() : r_xsub<4>());
     const int ring = MT == 1 ? r_ring<1>() : MT == 2 ? r_ring<2>() : r_ring<4>();
-    a.S = std::min(kRMaxStages, ring / (a.UB * a.sub));
-    if (a.S < 2)
-        return false;
-    a.tx = (uint32_t)(a.UB * (2 * a.RB * 128 + a.RB * 16 + 4 * a.xrows * 128));
-    return true;
+    const int scratch_warps = MT <= 2 ? 14 : 7;
+    for (int ub = 4; ub >= 1; ub >>= 1) {
+        if (ub > 1 && (a.T > 4 || K % (256 * ub) != 0))
+            continue;
+        /* warps per tile: as many consumer warps as the 16 allow, two blocks per warp
+         * and unit where that still fills them (MT 4: one, for registers) */
+        const int blocks = 4 * ub;
+        int nbk = MT <= 2 ? 2 : 1, kh = blocks / nbk;
+        while ((a.T * kh > kConsumers || a.T * (kh - 1) > scratch_warps) && nbk < blocks) {
+            nbk *= 2;
+            kh = blocks / nbk;
+        }
+        if (a.T * kh < kConsumers / 2 && nbk > 1 && a.T * kh * 2 <= kConsumers && a.T * (kh * 2 - 1) <= scratch_warps) {
+            nbk /= 2;
+            kh = blocks / nbk;
+        }
+        if (a.T * kh > kConsumers || a.T * (kh - 1) > scratch_warps || nbk > 2)
+            continue;
+        const int pt = align1k(ub * a.RB * 128), at = align1k(ub * a.RB * 16), xt = align1k(4 * ub * a.xrows * 128);
+        const int stage = 2 * pt + at + xt;
+        const int S = std::min(kRMaxStages, ring / stage);
+        if (S < (ub > 1 ? 3 : 2))
+            continue;
+        a.UB = ub, a.KH = kh, a.pt = pt, a.at = at, a.xt = xt, a.stage = stage, a.S = S;
+        a.KU = K / (256 * ub);
+        a.tx = (uint32_t)(ub * (2 * a.RB * 128 + a.RB * 16 + 4 * a.xrows * 128));
+        return true;
+    }
+    return false;
 }
 
 /* The row-owned kernel for N >= 16 x SMs.  Where the 16-row tiles leave a
@@ -1146,15 +1167,17 @@ int launch_rows(const uint8_t *hole, const uint8_t *plug, const float *am, const
             return kLaunch;
         grid = (N + a.R - 1) / a.R;
     }
+    /* 3-D views (inner bytes, rows, k slices) of the row-major planes, absmax and
+     * activations: a box is [slices][rows][inner] in shared memory */
     Maps maps;
-    if (!make_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
-                  (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
-                  (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, (uint64_t)K / 64, (uint64_t)N, (uint64_t)K / 64 * 4,
-                  4, (uint32_t)a.RB, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64,
-                  (uint32_t)a.xrows, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_map3(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, 128, (uint64_t)N, (uint64_t)K / 256,
+                   (uint64_t)K / 2, 128, 128, (uint32_t)a.RB, (uint32_t)a.UB, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map3(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, 128, (uint64_t)N, (uint64_t)K / 256,
+                   (uint64_t)K / 2, 128, 128, (uint32_t)a.RB, (uint32_t)a.UB, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map3(&maps.am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, am, 4, (uint64_t)N, (uint64_t)K / 256,
+                   (uint64_t)K / 64 * 4, 16, 4, (uint32_t)a.RB, (uint32_t)a.UB, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map3(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, 64, (uint64_t)M, (uint64_t)K / 64, (uint64_t)K * 2,
+                   128, 64, (uint32_t)a.xrows, (uint32_t)(4 * a.UB), CU_TENSOR_MAP_SWIZZLE_128B))
         return kLaunch;
     if (a.tail_units) {
         if (!make_map(&maps.h16, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,

@@ -106,6 +106,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         "l"(map), "r"(saddr(bar)), "r"(x), "r"(y)
         : "memory");
 }
+/* 3-D tiled TMA load of this GPU's memory into shared memory (no multicast). */
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+            "r"(saddr(dst)),
+        "l"(map), "r"(saddr(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ uint2 lds64(uint32_t a)
