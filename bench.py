@@ -1,19 +1,27 @@
 #!/usr/bin/env python3
 """GLINT hot-path benchmark on B200 (one process per GPU).
 
-Headline: encode of a synthetic Llama-3-8B-shaped
-model, 225 BF16 tensors / 7,504,658,432 weights (N(0, 0.02), 0.1% x20
-outliers), blocksize 64, in GB/s of BF16 input.  Weak scaling: every rank
-converts its own copy of the model (the job is N models; tensors are placed per
-rank by LPT with no collective), value = BF16 bytes of all ranks / max-rank time.
+Headline: encode of ONE synthetic Llama-3-8B-shaped
+model, 225 BF16 tensors / 7,504,658,432 weights (N(0, 0.02), exactly
+floor(0.001 n) entries x20 per tensor, drawn without replacement), blocksize 64,
+in GB/s of BF16 input.  The model's tensors are placed on the N ranks by LPT on
+their weight counts with no collective (strong scaling: the job is one model
+whatever N is); value = the model's BF16 bytes / the max-rank time of a step.  At
+N > 1 a weak-scaling figure (every rank converts a whole model) is reported beside
+it.
 
-Sub-results in the same JSON line: expand of the same model to BF16, decode GEMV
-(configs[2]: M in {1,4,16}, K=4096/N=14336 and K=14336/N=4096) and prefill GEMM
-(configs[3]: M in {512,2048,8192}, K=4096, N in {4096,14336}), each with its
-roofline fraction against MEASURED_PEAKS.json.
+Sub-results in the same JSON line (kept short, so the whole line survives in a
+driver's output tail): expand of the same tensors back to BF16 (in
+roofline.others), decode GEMV and prefill GEMM on one
+GPU, the reference's own H-TILE entry point at the prefill shapes, the 80-layer
+Llama-3-70B decode linear stack column-parallel over the ranks at
+batch 1 / 8 / 32, plug streaming and the pin pipeline (one GPU).  After each timed
+region its outputs are checked against the CPU oracle (`checks`).
 
 --impl reference times the reference's CPU path (the oracle/ restatement of
-glint_np.encode_f32, all host cores) on bounded samples of the same workload.
+glint_np.encode_f32, all host cores) on bounded samples of the same workload, and
+the reference's own CUDA kernels (built for sm_100a into oracle/_ref) on the same
+B200 beside it.
 """
 from __future__ import annotations
 
@@ -33,7 +41,8 @@ BS = 64
 ENC_BYTES_PER_W = 2 + 0.5 + 0.5 + 4 / 64        # 3.0625: BF16 in, hole + plug out, absmax out
 # DRAM read+write bytes per weight of encode_stream_kernel from one ncu capture of
 # `bench.py --profile encode` (4 x 14336x4096 tensors, one launch): 686.1 MB for
-# 234,881,024 weights; scaled to the bench's launches by their weights
+# 234,881,024 weights; scaled to the bench's launches by their weights.  A lower
+# bound: writes still dirty in L2 when the kernel ends are not counted.
 ENC_DRAM_BYTES_PER_W = 2.92
 EXP_BYTES_PER_W = 0.5 + 0.5 + 4 / 64 + 2        # 3.0625: planes + absmax in, BF16 out
 
@@ -46,6 +55,17 @@ def peaks():
                 "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
                 "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (the `lscpu` model name, read from /proc/cpuinfo)."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 class Clocks:
@@ -128,29 +148,113 @@ def max_over_ranks(world, v: float) -> float:
     return float(t.item())
 
 
-def synth_model(specs, seed):
-    """BF16 N(0,0.02) with floor(0.001 n) entries x20 per tensor, generated on the GPU."""
+def sum_over_ranks(world, v: float) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def synth_tensor(n: int, seed: int):
+    """n BF16 weights N(0, 0.02) with exactly floor(0.001 n) of them x20 (indices drawn
+    without replacement), generated on the GPU from `seed` (the tensor's index in the
+    model, so a tensor has the same values on whichever rank holds it)."""
     import torch
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
-    out = []
-    for s in specs:
-        n = s.numel
-        w = torch.empty(n, dtype=torch.bfloat16, device="cuda")
-        step = 1 << 27
-        for i in range(0, n, step):
-            j = min(n, i + step)
-            w[i:j] = (torch.randn(j - i, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
-        k = n // 1000
-        if k:
-            idx = torch.randint(0, n, (k,), generator=g, device="cuda")
-            w[idx] = (w[idx].float() * 20).to(torch.bfloat16)
-        out.append(w)
-    return out
+    w = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    step = 1 << 27
+    for i in range(0, n, step):
+        j = min(n, i + step)
+        w[i:j] = (torch.randn(j - i, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    k = n // 1000
+    if k:
+        idx = torch.randperm(n, generator=g, device="cuda")[:k]
+        w[idx] = (w[idx].float() * 20).to(torch.bfloat16)
+        del idx
+    return w
 
 
 def batches(items, size=32):
     return [items[i:i + size] for i in range(0, len(items), size)]
+
+
+def _oracle():
+    """The CPU oracle (test infrastructure): only the CPU-baseline leg and the output
+    checks after the timed regions load it, never a timed region."""
+    if str(ROOT / "oracle") not in sys.path:
+        sys.path.insert(0, str(ROOT / "oracle"))
+    import glint_oracle as O
+    O.set_threads()
+    return O
+
+
+def check_encode_expand(w, planes, out_bf16):
+    """One encoded tensor's hole / plug / absmax bytes and its expanded BF16 against the
+    oracle's (bit-exact)."""
+    import numpy as np
+    import torch
+    O = _oracle()
+    bits = w.view(torch.int16).cpu().numpy().view(np.uint16)
+    ho, po, ao = O.encode_bf16(bits, BS)
+    enc_ok = (planes[0].cpu().numpy().tobytes() == ho.tobytes() and planes[1].cpu().numpy().tobytes() == po.tobytes()
+              and planes[2].cpu().numpy().tobytes() == ao.tobytes())
+    exp_ok = out_bf16.view(torch.int16).cpu().numpy().tobytes() == O.expand_bf16(ho, po, ao, bits.size, BS).tobytes()
+    return enc_ok, exp_ok
+
+
+def check_htile_rows(x, planes, y, N, rows):
+    """max |y - y_ref| / max(1, max |y_ref|) of the given y rows against the oracle's f32
+    dequant-then-matmul of the same x rows."""
+    import numpy as np
+    import torch
+    O = _oracle()
+    K = x.shape[1]
+    xr = x[rows].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    ref = O.htile(planes[0].cpu().numpy(), planes[1].cpu().numpy(), planes[2].cpu().numpy(), xr, len(rows), N, K,
+                  BS).astype(np.float64)
+    got = y[rows].float().cpu().numpy().astype(np.float64)
+    return float(np.max(np.abs(got - ref)) / max(1.0, float(np.max(np.abs(ref)))))
+
+
+def time_encode(ws, planes, groups, steps, warmup, world, nvtx=None):
+    """W untimed and K timed steps of the batched encode; returns (max-rank ms for the K
+    steps, this rank's summed launch ms, launches per step)."""
+    import torch
+    from glint_b200 import device as D
+
+    def step(events=None):
+        for gi, grp in enumerate(groups):
+            if events is not None:
+                events[gi][0].record()
+            D.encode_batch([ws[i] for i in grp], BS, outs=[planes[i] for i in grp])
+            if events is not None:
+                events[gi][1].record()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in groups]
+          for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if nvtx:
+        torch.cuda.nvtx.range_push(nvtx)  # ncu --nvtx-include "encode_timed/" selects these launches
+    t0.record()
+    for k in range(steps):
+        step(ev[k])
+    t1.record()
+    if nvtx:
+        torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(world, t0.elapsed_time(t1))
+    kern_ms = sum(a.elapsed_time(b) for st in ev for (a, b) in st)
+    return ms, kern_ms, len(groups)
 
 
 def bench_glint(args):
@@ -161,72 +265,45 @@ def bench_glint(args):
     world, rank, local = dist_init(args)
     pk = peaks()
     specs = shard.llama3_8b_tensors()
-    # weak scaling: the job is `world` copies of the model, LPT-placed (each rank gets one copy's worth)
-    job = [s for _ in range(world) for s in specs]
-    plan = shard.lpt_assign([s.numel for s in job], world)
-    mine = [job[i] for i in plan[rank]]
-    weights = sum(s.numel for s in mine)
-    total_weights = sum(s.numel for s in job)
-
-    ws = synth_model(mine, seed=1234 + rank)
+    total_weights = sum(s.numel for s in specs)
+    # strong scaling: the job is one model; its tensors are LPT-placed over the ranks
+    plan = shard.lpt_assign([s.numel for s in specs], world)
+    mine = plan[rank]
+    weights = sum(specs[i].numel for i in mine)
+    ws = [synth_tensor(specs[i].numel, 1234 + i) for i in mine]
     planes = [D.alloc_planes(w.numel(), BS, w.device) for w in ws]
     groups = batches(list(range(len(ws))))
     torch.cuda.synchronize()
 
-    def encode_step(events=None):
-        for gi, grp in enumerate(groups):
-            if events is not None:
-                events[gi][0].record()
-            D.encode_batch([ws[i] for i in grp], BS, outs=[planes[i] for i in grp])
-            if events is not None:
-                events[gi][1].record()
-
-    for _ in range(args.warmup):
-        encode_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in groups]
-          for _ in range(args.steps)]
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)  # let the sampler come up before the timed region
-    torch.cuda.synchronize()
-    barrier(world)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.nvtx.range_push("encode_timed")  # ncu --nvtx-include "encode_timed/" selects these launches
-    t0.record()
-    for k in range(args.steps):
-        encode_step(ev[k])
-    t1.record()
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    barrier(world)
+    ms, kern_ms, per_step = time_encode(ws, planes, groups, args.steps, args.warmup, world, nvtx="encode_timed")
     clk = clocks.stop()
-    ms_local = t0.elapsed_time(t1)
-    ms = max_over_ranks(world, ms_local)
-    kern_ms = sum(a.elapsed_time(b) for step in ev for (a, b) in step)
     value = total_weights * 2 / (ms / args.steps / 1e3) / 1e9
     achieved = weights * ENC_BYTES_PER_W * args.steps / (kern_ms / 1e3) / 1e9
 
     result = {
         "metric": "GLINT encode throughput, Llama-3-8B-shaped model (GB/s of BF16 input)",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16->u4+u4+f32 (f32 arithmetic)", "data": "synthetic",
-        "config": {"workload": "encode_llama3_8b (BASELINE configs[1])", "tensors_per_rank": len(mine),
-                   "weights_per_rank": weights, "blocksize": BS, "parallelism": f"per-tensor LPT x{world}, no collective",
-                   "l2": "inputs (15 GB per rank) far larger than L2; no flush needed"},
+        "config": {"workload": "encode_llama3_8b (BASELINE configs[1]): one model, 225 tensors LPT-sharded over "
+                               "the ranks, no collective", "weights": total_weights, "weights_rank0": weights,
+                   "tensors_rank0": len(mine), "blocksize": BS, "parallelism": f"per-tensor LPT x{world}",
+                   "lpt_imbalance": round(shard.imbalance([s.numel for s in specs], plan), 4),
+                   "l2": "inputs (15 GB) far larger than L2; no flush needed"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4),
-                     "traffic": round(weights / len(groups) * ENC_DRAM_BYTES_PER_W),
-                     "traffic_note": "DRAM bytes per launch: ncu bytes/weight of the profile case x mean weights per launch",
+                     "traffic": round(weights / per_step * ENC_DRAM_BYTES_PER_W),
+                     "traffic_note": "lower bound: ncu DRAM bytes/weight of the profile case x mean weights per "
+                                     "launch; writes still dirty in L2 at kernel end are not counted",
                      "peak_source": pk["source"], "bytes_per_weight": ENC_BYTES_PER_W},
         "clocks": clk,
-        "gpu_launches": args.steps * len(groups),
+        "gpu_launches": args.steps * per_step,
     }
 
-    # ---- expand the same model back to BF16 (sub-result)
+    # ---- expand the same tensors back to BF16
     outs = [torch.empty_like(w) for w in ws]
 
     def expand_step():
@@ -235,6 +312,7 @@ def bench_glint(args):
     for _ in range(args.warmup):
         expand_step()
     torch.cuda.synchronize()
+    barrier(world)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("expand_timed")
     a.record()
@@ -245,26 +323,45 @@ def bench_glint(args):
     torch.cuda.synchronize()
     ems = max_over_ranks(world, a.elapsed_time(b)) / args.steps
     eg = weights * EXP_BYTES_PER_W / (ems / 1e3) / 1e9
-    result["expand"] = {"ms_per_step": round(ems, 4), "bf16_out_gbs_all_ranks": round(total_weights * 2 / (ems / 1e3) / 1e9, 2),
-                        "hbm_gbs_per_gpu": round(eg, 1), "frac": round(eg / pk["hbm_gbs"], 4),
-                        "bytes_per_weight": EXP_BYTES_PER_W}
+    result["roofline"]["others"] = {
+        "expand": {"achieved": round(eg, 1), "frac": round(eg / pk["hbm_gbs"], 4), "ms_per_step": round(ems, 4),
+                   "bf16_out_gbs": round(total_weights * 2 / (ems / 1e3) / 1e9, 1), "bytes_per_weight": EXP_BYTES_PER_W}}
+
+    # ---- outputs of both timed regions against the oracle: this rank's smallest tensor
+    ci = min(range(len(ws)), key=lambda i: (ws[i].numel(), i))
+    enc_ok, exp_ok = check_encode_expand(ws[ci], planes[ci], outs[ci])
+    bad = max_over_ranks(world, 0.0 if (enc_ok and exp_ok) else 1.0)
+    checks = {"encode_expand_bits": bad == 0.0, "tensor": specs[mine[ci]].name}
     del outs
+
+    # ---- weak scaling beside the headline (N > 1): every rank converts a whole model
+    if world > 1:
+        rest = [i for i in range(len(specs)) if i not in set(mine)]
+        ws_all = ws + [synth_tensor(specs[i].numel, 1234 + i) for i in rest]
+        planes_all = planes + [D.alloc_planes(specs[i].numel, BS, "cuda") for i in rest]
+        wsteps = max(1, min(args.steps, 5))
+        wms, _k, wper = time_encode(ws_all, planes_all, batches(list(range(len(ws_all)))), wsteps, 2, world)
+        result["weak"] = {"value": round(world * total_weights * 2 / (wms / wsteps / 1e3) / 1e9, 2),
+                          "ms_per_step": round(wms / wsteps, 4), "steps": wsteps}
+        del ws_all, planes_all
 
     # ---- e2e through the reference-facing host ABI (pinned host buffers, PCIe inside the timing)
     result["e2e"] = e2e_encode(ws, args, world)
-    # host copies for the pin-pipeline sub-result: the 8 linears after the embedding (one
-    # layer's 7 and the next q_proj, 235 M weights, 0.47 GB BF16)
-    ws_pin = [(mine[i].name, mine[i].rows, mine[i].cols, ws[i].view(torch.int16).cpu().numpy())
-              for i in range(1, min(len(ws), 9))] if world == 1 else []
+    # host copies for the pin-pipeline sub-result: 8 linears of one layer and the next q_proj
+    ws_pin = []
+    if world == 1:
+        for i in range(1, min(len(ws), 9)):
+            s = specs[mine[i]]
+            ws_pin.append((s.name, s.rows, s.cols, ws[i].view(torch.int16).cpu().numpy()))
     del ws, planes
     torch.cuda.empty_cache()
 
     # ---- decode GEMV and prefill GEMM (per GPU)
-    result["htile"] = bench_htile(args, pk)
-    # ---- column-parallel decode of a 70B layer over the ranks (NCCL all-gathers when world > 1)
-    result["tp_decode"] = bench_tp_decode(args, world, rank, pk)
-    # ---- plugs in host memory, streamed through the two-slot ring (one GPU's PCIe link)
+    result["htile"] = bench_htile(args, pk, checks)
+    # ---- the 80-layer Llama-3-70B decode linear stack, column-parallel over the ranks
+    result["decode_stack"] = bench_decode_stack(args, world, rank, pk, checks)
     if world == 1:
+        # ---- plugs in host memory, streamed through the two-slot ring (one GPU's PCIe link)
         result["plug_stream"] = bench_plug_stream(pk)
         # ---- the pin pipeline: safetensors on disk -> GLINT pin files (file IO, PCIe, encode, rmse)
         try:
@@ -272,8 +369,9 @@ def bench_glint(args):
         except Exception as e:  # a sub-result; the headline stands without it
             result["pin_pipeline"] = {"error": f"{type(e).__name__}: {e}"}
         del ws_pin
-    # gpu_launches counts the headline's timed region (encode); the sub-results carry their own counts
-    result["expand"]["launches"] = args.steps * len(groups)
+    checks["ok"] = bool(checks["encode_expand_bits"] and checks.get("htile_max_rel_err", 1.0) <= 1e-2
+                        and checks.get("decode_stack_ok", True))
+    result["checks"] = checks
     barrier(world)
     if world > 1:
         import torch.distributed as dist
@@ -281,57 +379,13 @@ def bench_glint(args):
     return rank, result
 
 
-def bench_pin(tensors):
-    """glint_b200.pin.convert of a two-shard BF16 model written to a temporary
-    directory: wall clock of the second of two conversions (so the source is in the
-    page cache and the pipeline's staging exists), which covers reading the shards,
-    host->device and device->host copies, the GPU encode and rmse, and writing the pin;
-    then glint_b200.unpin.unpin of that pin back to BF16, timed the same way."""
-    import shutil
-    import tempfile
-    from glint_b200 import pin, st_io, unpin
-    root = Path(tempfile.mkdtemp(prefix="glint_pin_bench_"))
-    try:
-        src = root / "src"
-        src.mkdir()
-        half = (len(tensors) + 1) // 2
-        names = ["model-00001-of-00002.safetensors", "model-00002-of-00002.safetensors"]
-        weight_map = {}
-        for name, part in zip(names, (tensors[:half], tensors[half:])):
-            st_io.write_file(str(src / name), [(n, "BF16", (r, c), a) for n, r, c, a in part], {"format": "pt"})
-            weight_map.update({n: name for n, _r, _c, _a in part})
-        (src / pin.INDEX_NAME).write_text(json.dumps({"metadata": {}, "weight_map": weight_map}))
-        n_in = sum(a.nbytes for _n, _r, _c, a in tensors)
-        times = []
-        for k in range(2):
-            out = root / f"pin{k}"
-            t = time.perf_counter()
-            got = pin.convert(src, out, BS)
-            times.append(time.perf_counter() - t)
-        out_bytes = sum(p.stat().st_size for p in (root / "pin1").iterdir())
-        utimes = []
-        for k in range(2):
-            t = time.perf_counter()
-            unpin.unpin(root / "pin1", root / f"dense{k}", "BF16")
-            utimes.append(time.perf_counter() - t)
-        return {"gbs_bf16_in": round(n_in / times[-1] / 1e9, 2), "seconds": round(times[-1], 3),
-                "unpin_gbs_bf16_out": round(n_in / utimes[-1] / 1e9, 2), "unpin_seconds": round(utimes[-1], 3),
-                "first_run_seconds": round(times[0], 3), "bf16_in_bytes": n_in, "pin_bytes": out_bytes,
-                "linears": got["pin"]["n_converted"], "rmse_max": got["pin"]["rmse_max"],
-                "sample": f"{len(tensors)} BF16 linears in 2 shards on local disk",
-                "timing": "wall clock of convert() (and of unpin() of its pin), second of two runs each "
-                          "(inputs in the page cache)"}
-    finally:
-        shutil.rmtree(root, ignore_errors=True)
-
-
 def e2e_encode(ws, args, world):
-    """glint_encode_bf16_host on pinned host copies of the first layers' tensors:
-    H2D of the BF16 input and D2H of the planes are inside the timed region."""
+    """glint_encode_bf16_host on pinned host copies of up to 29 of this rank's tensors:
+    the H2D of the BF16 input and the D2H of the planes are inside the timed region."""
     import torch
     from glint_b200 import glint_cuda
     L = glint_cuda.load()
-    sample = ws[: min(len(ws), 1 + 7 * 4)]  # the embedding + 4 layers
+    sample = ws[: min(len(ws), 29)]
     hosts = []
     for w in sample:
         n = w.numel()
@@ -352,10 +406,11 @@ def e2e_encode(ws, args, world):
     t = time.perf_counter()
     for _ in range(steps):
         step()
-    dt = max_over_ranks(world, (time.perf_counter() - t) / steps)
-    return {"value": round(nbytes * world / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": nbytes,
-            "d2h_bytes_per_step": outbytes, "api": "glint_encode_bf16_host (pinned host buffers)",
-            "sample": f"{len(hosts)} tensors ({nbytes / 1e9:.2f} GB BF16) per rank"}
+    dt = max_over_ranks(world, time.perf_counter() - t) / steps
+    tin, tout = sum_over_ranks(world, nbytes), sum_over_ranks(world, outbytes)
+    return {"value": round(tin / dt / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": int(tin),
+            "d2h_bytes_per_step": int(tout), "api": "glint_encode_bf16_host (pinned host buffers)",
+            "sample": f"{len(hosts)} tensors on rank 0 ({nbytes / 1e9:.2f} GB BF16), all ranks' bytes counted"}
 
 
 def graph_time_us(fn, n_launch: int, reps: int = 5) -> float:
@@ -387,163 +442,163 @@ def graph_time_us(fn, n_launch: int, reps: int = 5) -> float:
     return statistics.median(ts)
 
 
-def bench_htile(args, pk):
-    """Decode GEMV and prefill GEMM on one GPU, fast mode.
-    Every launch reads a different copy of the GLINT planes (4 copies for the
-    GEMV: 250 MB > L2, so each launch streams its weights from HBM; 2 for the
-    GEMM), and launches run back to back in a CUDA graph, so the numbers are
-    device time with no host gaps.  The decode kernel uses programmatic
-    dependent launch: in the graph a launch's weight stream starts while the
-    previous one drains, as in a decode step of consecutive linears."""
+def bench_htile(args, pk, checks):
+    """Decode GEMV (configs[2], plus M = 32 for the decode stack's batch) and prefill
+    GEMM on one GPU, fast mode, and the reference's own entry point
+    (launch_glint_htile_s3_f32_stream, f32-class precise arithmetic) at the prefill
+    shapes.  Weights are drawn as the configs draw them (synth_tensor: N(0, 0.02) with
+    0.1 % x20 outliers).  Every launch reads a different copy of the GLINT planes (4
+    copies for the GEMV: 250 MB > L2, so each launch streams its weights from HBM; 2 for
+    the GEMM) and launches run back to back in a CUDA graph, median of 5 replays: device
+    time with no host gaps.  The decode kernels use programmatic dependent launch, so in
+    the graph a launch's weight stream starts while the previous one drains, as in a
+    decode step of consecutive linears.  After each shape, rows 0 and M-1 of y are
+    checked against the oracle (checks.htile_max_rel_err, bound 1e-2)."""
     import torch
     from glint_b200 import device as D
-    res = {}
-    cases = [(m, 4096, 14336) for m in (1, 4, 16)] + [(m, 14336, 4096) for m in (1, 4, 16)]
+    gemv = [(m, 4096, 14336) for m in (1, 4, 16, 32)] + [(m, 14336, 4096) for m in (1, 4, 16, 32)]
     gemm = [(m, 4096, n) for m in (512, 2048, 8192) for n in (4096, 14336)]
+    res = {"gemv": {}, "gemm": {}, "ref_abi": {}}
     g = torch.Generator(device="cuda")
     g.manual_seed(7)
-    launches = 0
-    for (M, K, N) in cases + gemm:
-        w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
-        base = D.encode(w, BS)
-        del w
-        ncopy = 4 if M <= 16 else 2
+    launches, worst = 0, 0.0
+    for ci, (M, K, N) in enumerate(gemv + gemm):
+        base = D.encode(synth_tensor(N * K, 77 + ci), BS)
+        ncopy = 4 if M <= 32 else 2
         copies = [base] + [tuple(t.clone() for t in base) for _ in range(ncopy - 1)]
         x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
         y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-        n_launch = 16 if M <= 16 else 6
+        n_launch = 16 if M <= 32 else 6
         t = graph_time_us(lambda i: D.htile(x, *copies[i % ncopy], N, BS, mode="fast", out=y), n_launch) / 1e6
-        launches += n_launch * (5 + 2)
-        if M <= 16:
+        launches += n_launch * 6
+        key = f"m{M}_k{K}_n{N}"
+        if M <= 32:
             byt = N * K * (1 + 4 / 64) + M * K * 2 + M * N * 4
-            gbs = byt / t / 1e9
-            res[f"gemv_m{M}_k{K}_n{N}"] = {"us": round(t * 1e6, 2), "hbm_gbs": round(gbs, 1),
-                                            "frac": round(gbs / pk["hbm_gbs"], 4), "mode": "fast"}
+            res["gemv"][key] = [round(t * 1e6, 2), round(byt / t / 1e9 / pk["hbm_gbs"], 4)]
         else:
             tf = 2.0 * M * N * K / t / 1e12
-            res[f"gemm_m{M}_k{K}_n{N}"] = {"us": round(t * 1e6, 1), "tflops": round(tf, 1),
-                                            "frac": round(tf / pk["bf16_tflops"], 4), "mode": "fast"}
+            res["gemm"][key] = [round(t * 1e6, 1), round(tf, 1), round(tf / pk["bf16_tflops"], 4),
+                                round(tf / pk["bf16_tflops_sustained"], 4)]
+            if M == 2048 or (M == 512 and N == 4096):
+                tr = graph_time_us(lambda i: D.htile_reference_abi(x, *copies[i % ncopy], N, BS, out=y), 2, reps=3) / 1e6
+                launches += 2 * 4
+                res["ref_abi"][key] = [round(tr * 1e6, 1), round(2.0 * M * N * K / tr / 1e12, 1)]
+        D.htile(x, *copies[0], N, BS, mode="fast", out=y)
+        worst = max(worst, check_htile_rows(x, copies[0], y, N, [0, M - 1]))
         del copies, base, x, y
     torch.cuda.empty_cache()
-    res["timing"] = ("CUDA graph of back-to-back launches over rotating plane copies; median of 5 replays; "
-                     "fractions of MEASURED_PEAKS hbm_gbs / bf16_tflops")
+    checks["htile_max_rel_err"] = round(worst, 6)
     res["launches"] = launches
     return res
 
 
-def bench_tp_decode(args, world, rank, pk, M: int = 1):
-    """configs[4]-style decode step of one Llama-3-70B layer, column-parallel over
-    the ranks (glint_b200/tp.py): every rank holds 1/world of each linear's packed
-    rows and runs the decode kernel on them.  Where a consumer needs whole rows the
-    output is gathered: with `fused`, inside the decode kernel (tp.PeerGather: each
-    rank stores its rows into every rank's buffer over NVLink) for o_proj, gate/up
-    (so every rank forms the whole down_proj input) and down_proj, with one NCCL
-    all-gather left for the attention output that feeds o_proj; without it, NCCL
-    all-gathers of the o_proj and down_proj inputs and outputs.  The layer is
-    captured once in a CUDA graph (kernels and collectives), replayed, timed with
-    CUDA events, max over ranks; tokens/s assumes the 80 identical layers."""
+def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
+    """the linear path of a decode step through all 80 layers of a
+    synthetic Llama-3-70B (q/k/v/o 8192x8192 / 1024x8192, gate/up 28672x8192, down
+    8192x28672; random-init BF16 N(0, 0.02), GLINT-packed: 68.4 G weights, 72.7 GB of
+    planes), column-parallel over the ranks (glint_b200/tp.py; 72.7 GB / world per
+    GPU).  Per layer: q/k/v on the hidden state; o_proj on a fixed attention output
+    (attention itself is not on the path); gate and up, silu(gate) * up, down_proj,
+    whose output is the next layer's hidden state.  At world > 1 the outputs a
+    consumer needs whole (o, gate, up, down) are gathered inside their decode kernels
+    (tp.PeerGather: peer stores over NVLink), and the attention output that feeds
+    o_proj with one NCCL all-gather.  The whole 80-layer step is one CUDA graph,
+    replayed; device time with CUDA events, max over ranks."""
     import torch
     import torch.nn.functional as F
     from glint_b200 import device as D
+    from glint_b200 import glint_cuda
     from glint_b200 import shard as SH
     from glint_b200 import tp
+    L = glint_cuda.load()
+    layers = SH.LLAMA3_70B_LAYERS
     g = torch.Generator(device="cuda")
-    g.manual_seed(99 + rank)
-    lin = {nm: (N, K) for nm, N, K in SH.LLAMA3_70B_LAYER}
-    shards = {}
-    local_bytes = 0
-    for nm, (N, K) in lin.items():
-        n0, n1 = SH.column_shard(N, world, rank)
-        w = (torch.randn((n1 - n0) * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
-        h, p, a = D.encode(w, BS)
-        del w
-        shards[nm] = tp.ColumnShard(n0, n1, N, K, BS, h, p, a)
-        local_bytes += (n1 - n0) * K * (1 + 4 / 64)
+    stack, local_bytes = [], 0
+    for l in range(layers):
+        lay = {}
+        for j, (nm, N, K) in enumerate(SH.LLAMA3_70B_LAYER):
+            n0, n1 = SH.column_shard(N, world, rank)
+            g.manual_seed(100000 + 16 * l + j * 2 + 1000003 * rank)
+            w = (torch.randn((n1 - n0) * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+            h, p, a = D.encode(w, BS)
+            del w
+            lay[nm] = tp.ColumnShard(n0, n1, N, K, BS, h, p, a)
+            local_bytes += h.numel() + p.numel() + a.numel() * 4
+        stack.append(lay)
+    torch.cuda.synchronize()
+    out = {"model": "Llama-3-70B linear stack, 80 layers x 7 GLINT decode linears (configs[4])", "tp": world,
+           "weight_bytes_per_gpu": int(local_bytes), "batches": {}}
     gx = torch.Generator(device="cuda")
     gx.manual_seed(7)  # activations replicated: the same on every rank
-    x = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
-    attn = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
-    act_full = torch.randn((M, 28672), generator=gx, device="cuda").to(torch.bfloat16)
-    pg = None
-    if world > 1:
-        pg = tp.PeerGather({"o": (M, 8192, torch.float32), "gate": (M, 28672, torch.float32),
-                            "up": (M, 28672, torch.float32), "down": (M, 8192, torch.float32)}, world, rank)
+    for M in batches_m:
+        x0 = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
+        attn = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
+        pg = None
+        if world > 1:
+            pg = tp.PeerGather({"o": (M, 8192, torch.float32), "gate": (M, 28672, torch.float32),
+                                "up": (M, 28672, torch.float32), "down": (M, 8192, torch.float32)}, world, rank)
+        hidden = torch.empty((M, 8192), dtype=torch.bfloat16, device="cuda")
 
-    def layer_nccl():
-        outs = []
-        for nm in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj"):
-            outs.append(tp.column_parallel(x, shards[nm], world, rank, gather=False))
-        if world == 1:  # nothing to gather: the seven decode calls back to back
-            return outs, tp.column_parallel(attn, shards["o_proj"], 1, 0), \
-                tp.column_parallel(act_full, shards["down_proj"], 1, 0)
-        # o_proj: gather its input shard (the attention output), then its output
-        o_in = tp.gather_columns(attn[:, shards["o_proj"].n0:shards["o_proj"].n1].float(), 8192, world, rank)
-        o = tp.column_parallel(o_in.to(torch.bfloat16), shards["o_proj"], world, rank)
-        # down_proj: gather the activation shard, then the output
-        n0, n1 = SH.column_shard(28672, world, rank)
-        d_in = tp.gather_columns(act_full[:, n0:n1].float(), 28672, world, rank)
-        d = tp.column_parallel(d_in.to(torch.bfloat16), shards["down_proj"], world, rank)
-        return outs, o, d
+        def step():
+            hidden.copy_(x0)
+            for lay in stack:
+                for nm in ("q_proj", "k_proj", "v_proj"):
+                    tp.column_parallel(hidden, lay[nm], world, rank, gather=False)
+                if pg is None:
+                    tp.column_parallel(attn, lay["o_proj"], 1, 0)
+                    gate = tp.column_parallel(hidden, lay["gate_proj"], 1, 0)
+                    up = tp.column_parallel(hidden, lay["up_proj"], 1, 0)
+                    act = (F.silu(gate) * up).to(torch.bfloat16)
+                    d = tp.column_parallel(act, lay["down_proj"], 1, 0)
+                else:
+                    sh_o = lay["o_proj"]
+                    o_in = tp.gather_columns(attn[:, sh_o.n0:sh_o.n1].float(), 8192, world, rank)
+                    pg.linear(o_in.to(torch.bfloat16), sh_o, "o")
+                    gate = pg.linear(hidden, lay["gate_proj"], "gate")
+                    up = pg.linear(hidden, lay["up_proj"], "up")
+                    act = (F.silu(gate) * up).to(torch.bfloat16)
+                    d = pg.linear(act, lay["down_proj"], "down")
+                hidden.copy_(d)
 
-    def layer_fused():
-        outs = [tp.column_parallel(x, shards[nm], world, rank, gather=False) for nm in ("q_proj", "k_proj", "v_proj")]
-        o_in = tp.gather_columns(attn[:, shards["o_proj"].n0:shards["o_proj"].n1].float(), 8192, world, rank)
-        o = pg.linear(o_in.to(torch.bfloat16), shards["o_proj"], "o")
-        gate = pg.linear(x, shards["gate_proj"], "gate")
-        up = pg.linear(x, shards["up_proj"], "up")
-        act = (F.silu(gate) * up).to(torch.bfloat16)
-        d = pg.linear(act, shards["down_proj"], "down")
-        return outs, o, d
-
-    def timed(layer):
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            for _ in range(3):
-                layer()
+            step()  # first calls on the capture stream set up its workspaces
         torch.cuda.synchronize()
         barrier(world)
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
             with torch.cuda.graph(gr, stream=s):
-                layer()
+                step()
         torch.cuda.synchronize()
         barrier(world)
-        reps = 50
-        for _ in range(3):
+        for _ in range(2):
             gr.replay()
         torch.cuda.synchronize()
         barrier(world)
+        reps = 5
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(reps):
             gr.replay()
         b.record()
         torch.cuda.synchronize()
-        us = max_over_ranks(world, a.elapsed_time(b) * 1e3 / reps)
+        ms = max_over_ranks(world, a.elapsed_time(b) / reps)
         barrier(world)
         del gr  # graphs holding NCCL calls go before the process group does
         torch.cuda.synchronize()
-        return us
-
-    res = {"model": "Llama-3-70B layer (configs[4] shapes)", "tp": world, "batch": M,
-           "weight_bytes_per_gpu_per_layer": int(local_bytes), "kernels_per_layer": 7,
-           "timing": "one layer in a CUDA graph (decode kernels + gathers), replayed; max over ranks"}
-    if pg is not None:
-        us = timed(layer_fused)  # first: the fused layer is not measured behind the all-NCCL graph
-        pg.close()
-        us_nccl = timed(layer_nccl)
-        res.update({"us_per_layer": round(us, 2), "gathers": "fused into o/gate/up/down decode (peer stores) + 1 NCCL",
-                    "us_per_layer_nccl_gathers": round(us_nccl, 2)})
-    else:
-        us = timed(layer_nccl)
-        res.update({"us_per_layer": round(us, 2), "gathers": "none (one GPU)"})
-    from glint_b200 import glint_cuda
-    res.update({"tokens_per_s_80_layers": round(M / (80 * us * 1e-6), 1),
-                "hbm_frac_per_gpu": round(local_bytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
-                # nonzero if any bounded wait (pipeline barrier or gather arrival) ran out
-                "kernel_error": int(max_over_ranks(world, float(glint_cuda.load().glint_kernel_error(1))))})
-    return res
+        if pg is not None:
+            pg.close()
+        out["batches"][str(M)] = {"ms_per_step": round(ms, 3), "tokens_per_s": round(M / (ms * 1e-3), 1),
+                                  "hbm_gbs_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9, 1),
+                                  "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+    kerr = int(max_over_ranks(world, float(L.glint_kernel_error(1))))
+    out["kernel_error"] = kerr
+    out["launches_per_step"] = layers * 7
+    checks["decode_stack_ok"] = kerr == 0
+    del stack
+    torch.cuda.empty_cache()
+    return out
 
 
 def bench_plug_stream(pk, passes: int = 3):
@@ -618,13 +673,49 @@ def bench_plug_stream(pk, passes: int = 3):
         pass_ms = statistics.median([timed_pass(True) for _ in range(passes + 1)][1:])
         stats = st.stats()
     streamed = n_layers * layer_plug
-    return {"model": "Llama-3-8B decode pass, M=1, 32 layers x 7 linears, fast mode",
-            "plug_bytes_per_layer": layer_plug, "layers": n_layers,
-            "pass_ms": round(pass_ms, 3), "h2d_gbs": round(streamed / (pass_ms * 1e-3) / 1e9, 2),
-            "copy_only_pass_ms": round(copy_ms, 3), "copy_only_h2d_gbs": round(streamed / (copy_ms * 1e-3) / 1e9, 2),
-            "frac_of_copy_only": round(copy_ms / pass_ms, 4),
-            "resident_pass_ms": round(resident_ms, 3), "stall_ms_last_pass": round(stats["total_stall_ms"], 3),
-            "timing": "CUDA events on the compute stream around start() .. last release, median of 3 passes"}
+    return {"pass_ms": round(pass_ms, 3), "h2d_gbs": round(streamed / (pass_ms * 1e-3) / 1e9, 2),
+            "copy_only_h2d_gbs": round(streamed / (copy_ms * 1e-3) / 1e9, 2), "resident_pass_ms": round(resident_ms, 3),
+            "stall_ms": round(stats["total_stall_ms"], 3)}
+
+
+def bench_pin(tensors):
+    """glint_b200.pin.convert of a two-shard BF16 model written to a temporary
+    directory: wall clock of the second of two conversions (so the source is in the
+    page cache and the pipeline's staging exists), which covers reading the shards,
+    host->device and device->host copies, the GPU encode and rmse, and writing the pin;
+    then glint_b200.unpin.unpin of that pin back to BF16, timed the same way."""
+    import shutil
+    import tempfile
+    from glint_b200 import pin, st_io, unpin
+    root = Path(tempfile.mkdtemp(prefix="glint_pin_bench_"))
+    try:
+        src = root / "src"
+        src.mkdir()
+        half = (len(tensors) + 1) // 2
+        names = ["model-00001-of-00002.safetensors", "model-00002-of-00002.safetensors"]
+        weight_map = {}
+        for name, part in zip(names, (tensors[:half], tensors[half:])):
+            st_io.write_file(str(src / name), [(n, "BF16", (r, c), a) for n, r, c, a in part], {"format": "pt"})
+            weight_map.update({n: name for n, _r, _c, _a in part})
+        (src / pin.INDEX_NAME).write_text(json.dumps({"metadata": {}, "weight_map": weight_map}))
+        n_in = sum(a.nbytes for _n, _r, _c, a in tensors)
+        times = []
+        for k in range(2):
+            out = root / f"pin{k}"
+            t = time.perf_counter()
+            got = pin.convert(src, out, BS)
+            times.append(time.perf_counter() - t)
+        out_bytes = sum(p.stat().st_size for p in (root / "pin1").iterdir())
+        utimes = []
+        for k in range(2):
+            t = time.perf_counter()
+            unpin.unpin(root / "pin1", root / f"dense{k}", "BF16")
+            utimes.append(time.perf_counter() - t)
+        return {"gbs_bf16_in": round(n_in / times[-1] / 1e9, 2), "unpin_gbs_bf16_out": round(n_in / utimes[-1] / 1e9, 2),
+                "first_run_s": round(times[0], 3), "linears": got["pin"]["n_converted"],
+                "rmse_max": round(got["pin"]["rmse_max"], 8)}
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
 
 
 # ------------------------------------------------------------------ CPU baselines
@@ -636,8 +727,7 @@ def _cpu_sample():
     global _CPU_SAMPLE
     if _CPU_SAMPLE is None:
         import numpy as np
-        sys.path.insert(0, str(ROOT / "oracle"))
-        import glint_oracle as O
+        O = _oracle()
         threads = O.set_threads()
         rng = np.random.default_rng(0)
         n = 4096 * 4096
@@ -663,6 +753,7 @@ def cpu_encode_sample(seconds: float = 10.0):
             break
     dt = time.perf_counter() - t0
     return {"value": round(done * 2 / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(),
             "sample": f"{done // n} x one 4096x4096 BF16 tensor of config 2 ({done / 1e6:.0f} M weights, {dt:.1f} s)"}
 
 
@@ -692,17 +783,91 @@ def cpu_other_paths(seconds: float = 3.0):
         if time.perf_counter() - t1 >= seconds:
             break
     dg = time.perf_counter() - t1
-    return {"expand_bf16": {"value": round(done * 2 / dt / 1e9, 4), "unit": "GB/s of BF16 output", "cores": threads,
-                            "kind": "port", "sample": f"{done // n} x the 4096x4096 sample ({dt:.1f} s)"},
-            "gemv_m1": {"us_per_call": round(dg / calls * 1e6, 1), "gweights_per_s": round(n * calls / dg / 1e9, 3),
-                        "kind": "numpy", "sample": f"{calls} x x[1,4096] @ W.T, W the expanded f32 4096x4096 "
-                                                   f"(64 MB), numpy's BLAS threads ({dg:.1f} s)"}}
+    return {"expand_bf16_gbs": round(done * 2 / dt / 1e9, 3), "gemv_m1_us": round(dg / calls * 1e6, 1)}
+
+
+def ref_gpu_kernels():
+    """The reference's own CUDA code, built unchanged for sm_100a into oracle/_ref by
+    oracle/Makefile, timed on this B200: its host encode API (glint_encode_bf16_host:
+    one synchronous call with its own allocations and PCIe copies, as glint_cuda.py
+    calls it), its device expand (glint_expand_packed_to_f32_device) and its H-TILE
+    (launch_glint_htile_s3_f32_stream) at the configs' shapes.  Device times with CUDA
+    events on the launching stream, median of a few launches."""
+    import ctypes
+    import numpy as np
+    import torch
+    from glint_b200 import device as D
+    O = _oracle()
+    enc_so, ht_so = O.ref_lib_path("libglint_encode.so"), O.ref_lib_path("libglint_htile.so")
+    if enc_so is None or ht_so is None:
+        return {"unavailable": "oracle/_ref not built"}
+    RE, RH = ctypes.CDLL(str(enc_so)), ctypes.CDLL(str(ht_so))
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    RE.glint_encode_bf16_host.argtypes = [vp, i64, i32, vp, vp, vp]
+    RE.glint_expand_packed_to_f32_device.argtypes = [vp, vp, vp, i64, i32, vp, vp]
+    RH.launch_glint_htile_s3_f32_stream.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]
+    torch.cuda.set_device(0)
+    out = {}
+    N, K = 14336, 4096
+    n = N * K
+    w = synth_tensor(n, 4242)
+    h, p, a = D.encode(w, BS)
+    # host encode API: pinned host buffers in and out, wall clock of the synchronous call
+    src = w.view(torch.int16).cpu().pin_memory()
+    hh, hp = torch.empty(n // 2, dtype=torch.uint8).pin_memory(), torch.empty(n // 2, dtype=torch.uint8).pin_memory()
+    ha = torch.empty(n // BS, dtype=torch.float32).pin_memory()
+    ts = []
+    for _ in range(3):
+        t = time.perf_counter()
+        rc = RE.glint_encode_bf16_host(src.data_ptr(), n, BS, hh.data_ptr(), hp.data_ptr(), ha.data_ptr())
+        ts.append(time.perf_counter() - t)
+        if rc != 0:
+            return {"unavailable": f"reference glint_encode_bf16_host rc={rc}"}
+    out["encode_host_api_gbs"] = round(n * 2 / min(ts) / 1e9, 2)
+    st = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+
+    def dev_us(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            ev[0].record()
+            fn()
+            ev[1].record()
+            torch.cuda.synchronize()
+            ts.append(ev[0].elapsed_time(ev[1]) * 1e3)
+        return statistics.median(ts)
+
+    yf = torch.empty(n, dtype=torch.float32, device="cuda")
+    us = dev_us(lambda: RE.glint_expand_packed_to_f32_device(h.data_ptr(), p.data_ptr(), a.data_ptr(), n, BS,
+                                                             yf.data_ptr(), ctypes.c_void_p(st.cuda_stream)), 5)
+    out["expand_f32_device_gbs"] = round(n * 5.0625 / (us * 1e-6) / 1e9, 1)
+    del yf
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    ht = {}
+    for (M, KK, NN) in [(1, 4096, 14336), (16, 4096, 14336), (1, 14336, 4096), (512, 4096, 4096),
+                        (2048, 4096, 14336)]:
+        x = torch.randn((M, KK), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, NN), dtype=torch.float32, device="cuda")
+        us = dev_us(lambda: RH.launch_glint_htile_s3_f32_stream(h.data_ptr(), p.data_ptr(), a.data_ptr(), x.data_ptr(),
+                                                                y.data_ptr(), M, NN, KK, BS,
+                                                                ctypes.c_void_p(st.cuda_stream)), 3 if M < 512 else 1)
+        key = f"m{M}_k{KK}_n{NN}"
+        if M <= 32:
+            ht[key] = [round(us, 1), round((NN * KK * 1.0625 + M * KK * 2 + M * NN * 4) / (us * 1e-6) / 1e9, 1)]
+        else:
+            ht[key] = [round(us, 1), round(2.0 * M * NN * KK / (us * 1e-6) / 1e12, 2)]
+    out["htile_us_and_gbs_or_tflops"] = ht
+    return out
 
 
 def bench_reference(args):
     """The reference arm: the CPU encode (oracle port on all host cores), W warm-up
     and K timed steps, each step a bounded sample of the workload; the whole run
-    is held to about a minute of CPU work whatever K is."""
+    is held to about a minute of CPU work whatever K is.  Beside it, the reference's
+    own CUDA kernels on this GPU (`reference_gpu`), where a GPU is present."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -726,13 +891,20 @@ def bench_reference(args):
         "impl": "reference",
         "metric": "GLINT encode throughput, Llama-3-8B-shaped model (GB/s of BF16 input)",
         "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16->u4+u4+f32 (f32 arithmetic)", "data": "synthetic",
-        "config": {"workload": "encode_llama3_8b (BASELINE configs[1])", "blocksize": BS,
+        "config": {"workload": "encode_llama3_8b (BASELINE configs[1]): one model, 225 tensors LPT-sharded over "
+                               "the ranks, no collective", "blocksize": BS,
                    "what": "reference CPU encode (glint_np.encode_f32 semantics) restated in oracle/glint_oracle.c"},
         "cpu_baseline": cb,
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    try:
+        import torch
+        if torch.cuda.is_available():
+            line["reference_gpu"] = ref_gpu_kernels()
+    except Exception as e:  # informational beside the CPU line; the line stands without it
+        line["reference_gpu"] = {"error": f"{type(e).__name__}: {e}"}
     print(json.dumps(line), flush=True)
 
 
@@ -790,11 +962,12 @@ def profile_case(case: str, iters: int = 5):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="glint_b200", choices=["glint_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", default=None, help="run one small kernel case (encode|expand|gemv<M>|gemm<M>) for ncu")
+    ap.add_argument("--profile", default=None,
+                    help="run one small kernel case (encode|expand|gemv<M>|gemvt<M>|gemm<M>) for ncu")
     args = ap.parse_args()
     if args.profile:
         profile_case(args.profile)
@@ -812,7 +985,7 @@ def main():
     rank, result = bench_glint(args)
     if rank == 0:
         result["cpu_baseline"] = cb
-        print(json.dumps(result), flush=True)
+        print(json.dumps(result, separators=(",", ":")), flush=True)
 
 
 if __name__ == "__main__":

@@ -80,7 +80,7 @@ int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const 
                                 HtileMode mode, cudaStream_t stream);
 
 /* Decode with the output gathered into every rank's y over peer memory
- * (1 <= M <= 16; kUnsupported otherwise). */
+ * (1 <= M <= 32; kUnsupported otherwise). */
 bool htile_gather_supported(int M, int N);
 int htile_decode_gather_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax,
                                const __nv_bfloat16 *x, void *const *y_ranks, uint32_t *const *flag_ranks,

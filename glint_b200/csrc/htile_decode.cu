@@ -1363,7 +1363,7 @@ int htile_decode_launch(const uint8_t *hole, const uint8_t *plug, const float *a
     return decode_launch_impl(hole, plug, am, x, y, yk, M, N, K, mode, st, nullptr);
 }
 
-bool htile_gather_supported(int M, int N) { return M >= 1 && M <= 16 && N >= 1; }
+bool htile_gather_supported(int M, int N) { return M >= 1 && M <= 32 && N >= 1; }
 
 int htile_decode_gather_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
                                void *const *y_ranks, uint32_t *const *flag_ranks, int world, int rank,

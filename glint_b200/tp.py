@@ -164,9 +164,9 @@ class PeerGather:
 
     @staticmethod
     def supported(M: int, rows: int) -> bool:
-        """Shapes the gathered kernel covers (the decode kernels, M <= 16; also
+        """Shapes the gathered kernel covers (the decode kernels, M <= 32; also
         bs == 64 and K % 256 == 0, as for the decode path)."""
-        return 1 <= M <= 16 and rows >= 1
+        return 1 <= M <= 32 and rows >= 1
 
     def linear(self, x: torch.Tensor, sh: ColumnShard, name: str, mode: str = "fast", stream=None) -> torch.Tensor:
         """y[M, N] = x . W^T on every rank: this rank's rows [n0, n1) computed here,

@@ -152,7 +152,8 @@ def _gather_worker(rank, world, port):
         hole, plug, am = D.encode(w, 64)
         sh = tp.ColumnShard.from_full(hole, plug, am, N, K, 64, rank, world)
         for M, dt, mode, tol in [(1, torch.float32, "precise", 1e-5), (4, torch.bfloat16, "fast", 1e-2),
-                                 (16, torch.float32, "fast", 1e-2)]:
+                                 (16, torch.float32, "fast", 1e-2), (32, torch.float32, "fast", 1e-2),
+                                 (32, torch.float32, "precise", 1e-5)]:
             pg = tp.PeerGather({"y": (M, N, dt)}, world, rank)
             for _ in range(3):  # consecutive calls alternate the buffers and reuse the counters
                 x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
