@@ -315,6 +315,21 @@ int htile_gemv_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
                             aligned_to(x, 16) && aligned_to(am, 4) && (int64_t)N * (K / 64) < (int64_t)0xFFFFFFFF;
     if (htile_decode_supported(hole, plug, am, x, M, N, K, bs))
         return htile_decode_launch(hole, plug, am, x, y, yk, M, N, K, mode, st);
+    if (M > 32 && htile_decode_supported(hole, plug, am, x, 32, N, K, bs)) {
+        /* larger M on the TMA-streamed decode kernels, 32 activation rows per launch
+         * (the precise path at prefill shapes; consecutive launches overlap through
+         * programmatic dependent launch, and the planes of layers up to ~100 MB stay
+         * in L2 between them) */
+        const size_t ysz = yk == kOutBF16 ? 2 : 4;
+        for (int m0 = 0; m0 < M; m0 += 32) {
+            const int rc = htile_decode_launch(hole, plug, am, x + (int64_t)m0 * K,
+                                               static_cast<char *>(y) + (size_t)m0 * N * ysz, yk,
+                                               std::min(32, M - m0), N, K, mode, st);
+            if (rc != kOk)
+                return rc;
+        }
+        return kOk;
+    }
     if (fast_shape) {
         if (mode == kPrecise)
             return yk == kOutBF16 ? launch_gemv_slices<true, true>(hole, plug, am, x, y, M, N, K, bs, st)
