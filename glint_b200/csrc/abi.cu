@@ -492,8 +492,9 @@ int htile_launch(const uint8_t *hole, const uint8_t *plug, const float *am, cons
         const size_t bytes = (size_t)M * N * (yk == kOutBF16 ? 2 : 4);
         return cudaMemsetAsync(y, 0, bytes, st) == cudaSuccess ? kOk : kLaunch;
     }
-    if (mode == kFast && htile_gemm_supported(hole, plug, am, x, y, yk == kOutBF16, M, N, K, bs))
-        return htile_gemm_launch(hole, plug, am, x, y, yk == kOutBF16, M, N, K, bs, st);
+    if (htile_gemm_supported(hole, plug, am, x, y, yk == kOutBF16, M, N, K, bs))
+        return mode == kFast ? htile_gemm_launch(hole, plug, am, x, y, yk == kOutBF16, M, N, K, bs, st)
+                             : htile_gemm_precise_launch(hole, plug, am, x, y, yk == kOutBF16, M, N, K, st);
     return htile_gemv_launch(hole, plug, am, x, y, yk, M, N, K, bs, mode, st);
 }
 

@@ -63,6 +63,10 @@ bool htile_gemm_supported(const uint8_t *hole, const uint8_t *plug, const float 
                           const void *y, bool y_bf16, int M, int N, int K, int blocksize);
 int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x, void *y,
                       bool y_bf16, int M, int N, int K, int blocksize, cudaStream_t stream);
+/* The same shapes in precise mode (f32-class: a fresh accumulator per 64-k block,
+ * BF16 hi + lo weight halves, the blocks scaled and added in f32). */
+int htile_gemm_precise_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
+                              void *y, bool y_bf16, int M, int N, int K, cudaStream_t stream);
 /* Sticky error words written by kernels whose bounded waits ran out (0 = none),
  * one per kernel file; read_kernel_error ORs them. */
 int read_kernel_error(bool clear);

@@ -625,6 +625,340 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
+/* ---- precise mode (the reference's f32-class accuracy) on tcgen05 ----------------
+ * The UMMA's f32 accumulation loses precision as the accumulator grows (against
+ * f64 sums of the same BF16 weights: 6e-7 at K = 256, 3e-5 at K = 4096, 2.6e-4 at
+ * K = 16384 for N(0, 0.02) x N(0, 1)), so here every 64-k absmax block gets a fresh
+ * accumulator and the blocks are added on the CUDA cores, in f32, after scaling:
+ *   y[n, m] = sum_b absmax[n, b] * (sum_{k in b} (hi + lo)[n, k] * x[m, k]),
+ * with hi = RN_bf16(cell), lo = RN_bf16(cell - hi) (about 17 significant bits of
+ * the cell) entering the tensor cores as two BF16 operands.  The weights need no
+ * scaling on the way in: a dequantiser thread looks each code up once (one 32-bit
+ * hi|lo entry of a per-lane codebook replica) and splits the pairs into a hi and a lo
+ * TMEM slice.  CTA pairs take tiles of 256 weight rows x 128 activations: TMEM holds
+ * two 128-column accumulators (one block while the epilogue drains the other) and a
+ * 4-slot ring of hi|lo weight slices (64 columns per K step).  Roles per CTA:
+ *   warp 0       activation producer ([64 rows x 64 k] BF16 per K step, pair-counted);
+ *   warp 1       TMEM owner; the leader's lane 0 issues 4 x (hi, lo) UMMAs
+ *                (M = 256, N = 128, K = 16) per K step into the block's accumulator;
+ *   warps 2-9    dequantisers (thread = weight row, 32 weights of the K step);
+ *   warps 10-25  epilogue: warp w reads 32 accumulator columns of TMEM lanes
+ *                32*(w%4).., scales them by the row's absmax (read from global, four
+ *                blocks at a time, one group ahead) and adds them to its running sums;
+ *                at a tile's end the sums go to y;
+ *   warp 26      plane producer (hole and plug [128 rows x 128 B] per 4 K steps).
+ * Tiles are whole (no split), round-robin over the pairs. */
+constexpr int PBMX = 128;                       /* activations per pair tile (UMMA N) */
+constexpr int PBMH = 64;                        /* activation rows held by one CTA */
+constexpr int PXSTAGES = 8;
+constexpr int PWSLOTS = 4;                      /* hi | lo weight slices, 64 TMEM columns each */
+constexpr int PDeq0 = 2, PDeqWarps = 8, PEpi0 = PDeq0 + PDeqWarps, PEpiWarps = 16;
+constexpr int PPlaneWarp = PEpi0 + PEpiWarps;
+constexpr int PThreads = (PPlaneWarp + 1) * 32; /* 864 */
+constexpr int PStageX = PBMH * BK * 2;          /* 8 KB */
+constexpr int PPStage = 2 * kPlaneBox;          /* 32 KB: hole and plug of 4 K steps */
+constexpr int PSmemBytes = kLutBytes + 1024 + PXSTAGES * PStageX + PSTAGES * PPStage + 512;
+constexpr uint32_t PWCol = 2 * PBMX;            /* weight ring after the two accumulators */
+static_assert(PWCol + PWSLOTS * BK <= 512, "TMEM columns");
+constexpr uint32_t kIdescP =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PBMX >> 3) << 17) | ((uint32_t)((2 * BN) >> 4) << 24);
+
+struct PreciseArgs {
+    void *y;
+    const float *am;
+    int M, N, K;
+    int y_bf16;
+    int mtiles, tiles;
+};
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                   "=r"(r[15])
+                 : "r"(taddr));
+}
+
+__device__ __forceinline__ uint32_t split_hilo(float c)
+{
+    const uint32_t hi = f32_to_bf16_bits(c);
+    const float rest = c - __uint_as_float(hi << 16);
+    return hi | (f32_to_bf16_bits(rest) << 16);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PThreads, 1)
+    htile_gemm_precise_kernel(const __grid_constant__ Maps maps, const PreciseArgs args)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint32_t *lut = reinterpret_cast<uint32_t *>(smem_raw);
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw + kLutBytes) + 1023) &
+                                                ~uintptr_t(1023));
+    uint8_t *xring = smem, *pring = smem + PXSTAGES * PStageX;
+    uint64_t *x_full = reinterpret_cast<uint64_t *>(pring + PSTAGES * PPStage); /* leader: both x halves */
+    uint64_t *x_empty = x_full + PXSTAGES;
+    uint64_t *p_full = x_empty + PXSTAGES;
+    uint64_t *p_empty = p_full + PSTAGES;
+    uint64_t *w_full = p_empty + PSTAGES;   /* leader: both CTAs' weight slices written */
+    uint64_t *w_empty = w_full + PWSLOTS;
+    uint64_t *acc_full = w_empty + PWSLOTS; /* [2]: block accumulator b complete */
+    uint64_t *acc_empty = acc_full + 2;     /* [2] leader: both CTAs' epilogues read it */
+    uint64_t *mma_done = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const uint32_t lane = lane_id();
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    const int KS = args.K / BK; /* K steps (absmax blocks) per tile */
+
+    /* hi | lo BF16 pairs of the codebook, one replica per lane, 256-byte entry stride;
+     * a 16-byte store fills a quarter of an entry's 32 replicas (no bank conflicts) */
+    for (int i = threadIdx.x; i < 256 * 8; i += PThreads) {
+        const uint32_t v = split_hilo((&g_cells[0][0])[i >> 3]);
+        reinterpret_cast<uint4 *>(lut + (i >> 3) * 64)[i & 7] = make_uint4(v, v, v, v);
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PXSTAGES; ++s) {
+            mbar_init(&x_full[s], 1);
+            mbar_init(&x_empty[s], 1);
+        }
+        for (int s = 0; s < PSTAGES; ++s) {
+            mbar_init(&p_full[s], 1);
+            mbar_init(&p_empty[s], PDeqWarps);
+        }
+        for (int a = 0; a < PWSLOTS; ++a) {
+            mbar_init(&w_full[a], 2 * PDeqWarps);
+            mbar_init(&w_empty[a], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * PEpiWarps);
+        }
+        mbar_init(mma_done, 1);
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync(); /* both CTAs' barriers initialised and TMEM allocated */
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool alive = true;
+
+    if (warp == 0) {
+        /* ---- activation producer (both CTAs): this CTA's 64 rows of the tile */
+        if (lane == 0) {
+            Ring st;
+            int64_t issued = 0;
+            for (int T = pair; T < args.tiles && alive; T += npairs) {
+                const int mr = (T % args.mtiles) * PBMX + (int)rank * PBMH;
+                for (int ks = 0; ks < KS && alive; ++ks, st.next<PXSTAGES>()) {
+                    if (!wait_or_fail(&x_empty[st.i], st.ph ^ 1u, alive))
+                        break;
+                    if (leader)
+                        mbar_expect_tx(&x_full[st.i], 2 * PStageX);
+                    tma_load_2d_pair(xring + st.i * PStageX, &maps.x, peer_addr(saddr(&x_full[st.i]), 0), ks * BK, mr);
+                    ++issued;
+                }
+            }
+            if (!alive && leader) {
+                bool drain = true;
+                for (int64_t j = issued > PXSTAGES ? issued - PXSTAGES : 0; j < issued && drain; ++j)
+                    drain = mbar_wait_bounded(&x_full[(int)(j % PXSTAGES)], (uint32_t)(j / PXSTAGES) & 1u,
+                                              &g_glint_kernel_error);
+            }
+        }
+    } else if (warp == PPlaneWarp) {
+        /* ---- plane producer (both CTAs): hole and plug of this CTA's 128 weight rows */
+        if (lane == 0) {
+            Ring st;
+            int64_t issued = 0;
+            for (int T = pair; T < args.tiles && alive; T += npairs) {
+                const int nr = (T / args.mtiles) * (2 * BN) + (int)rank * BN;
+                for (int ks = 0; ks < KS && alive; ks += PSTEPS, st.next<PSTAGES>()) {
+                    if (!wait_or_fail(&p_empty[st.i], st.ph ^ 1u, alive))
+                        break;
+                    uint8_t *sb = pring + st.i * PPStage;
+                    mbar_expect_tx(&p_full[st.i], PPStage);
+                    tma_load_2d(sb, &maps.h, &p_full[st.i], ks * (BK / 2), nr);
+                    tma_load_2d(sb + kPlaneBox, &maps.p, &p_full[st.i], ks * (BK / 2), nr);
+                    ++issued;
+                }
+            }
+            if (!alive) {
+                bool drain = true;
+                for (int64_t j = issued > PSTAGES ? issued - PSTAGES : 0; j < issued && drain; ++j)
+                    drain = mbar_wait_bounded(&p_full[(int)(j % PSTAGES)], (uint32_t)(j / PSTAGES) & 1u,
+                                              &g_glint_kernel_error);
+            }
+        }
+    } else if (warp == 1) {
+        /* ---- UMMA issuer (leader CTA only): one fresh accumulator per K step */
+        if (leader && lane == 0) {
+            Ring st, ws;
+            int64_t g = 0; /* K steps issued by this pair: accumulator g & 1, its use g >> 1 */
+            const uint32_t xe0 = peer_addr(saddr(&x_empty[0]), 0), xe1 = peer_addr(saddr(&x_empty[0]), 1);
+            const uint32_t we0 = peer_addr(saddr(&w_empty[0]), 0), we1 = peer_addr(saddr(&w_empty[0]), 1);
+            const uint32_t af0 = peer_addr(saddr(&acc_full[0]), 0), af1 = peer_addr(saddr(&acc_full[0]), 1);
+            for (int T = pair; T < args.tiles && alive; T += npairs) {
+                for (int ks = 0; ks < KS && alive; ++ks, ++g, st.next<PXSTAGES>(), ws.next<PWSLOTS>()) {
+                    const int b = (int)(g & 1);
+                    /* the first use of each accumulator waits on parity 1: returns at once */
+                    if (!wait_or_fail(&acc_empty[b], (uint32_t)((g >> 1) & 1) ^ 1u, alive) ||
+                        !wait_or_fail(&x_full[st.i], st.ph, alive) || !wait_or_fail(&w_full[ws.i], ws.ph, alive))
+                        break;
+                    tc_fence_after();
+                    const uint32_t xs = saddr(xring + st.i * PStageX);
+                    const uint32_t wa = tmem + PWCol + (uint32_t)ws.i * BK, d = tmem + (uint32_t)b * PBMX;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t bd = sw128_desc(xs + kk * 32);
+                        umma_pair_ts_bf16(d, wa + kk * 8, bd, kIdescP, kk > 0 ? 1u : 0u);      /* hi */
+                        umma_pair_ts_bf16(d, wa + 32 + kk * 8, bd, kIdescP, 1u);             /* lo */
+                    }
+                    umma_commit_to(xe0 + (uint32_t)st.i * 8u);
+                    umma_commit_to(xe1 + (uint32_t)st.i * 8u);
+                    umma_commit_to(we0 + (uint32_t)ws.i * 8u);
+                    umma_commit_to(we1 + (uint32_t)ws.i * 8u);
+                    umma_commit_to(af0 + (uint32_t)b * 8u);
+                    umma_commit_to(af1 + (uint32_t)b * 8u);
+                }
+            }
+            umma_commit_to(peer_addr(saddr(mma_done), 0));
+            mbar_wait_bounded(mma_done, 0, &g_glint_kernel_error);
+        }
+        __syncwarp();
+    } else if (warp < PEpi0) {
+        /* ---- dequantisers: thread -> weight row r (TMEM lane), 32 weights (K part kq) */
+        const int q = warp & 3, kq = (warp - PDeq0) >> 2;
+        const int r = q * 32 + (int)lane;
+        const uint32_t lutb = saddr(lut), lane4 = lane * 4u;
+        const uint32_t prow = (uint32_t)r * 128u, pswz = (uint32_t)(r & 7);
+        const uint32_t kb = (uint32_t)kq * 16u;
+        const uint32_t tw = tmem + ((uint32_t)(q * 32) << 16) + PWCol + (uint32_t)kq * 16u;
+        const uint32_t wfull0 = peer_addr(saddr(&w_full[0]), 0);
+        Ring st, ws;
+        for (int T = pair; T < args.tiles && alive; T += npairs) {
+            for (int ks = 0; ks < KS && alive; ++ks, ws.next<PWSLOTS>()) {
+                const int j = ks & (PSTEPS - 1);
+                if (j == 0 && !warp_wait(&p_full[st.i], st.ph, alive))
+                    break;
+                const uint32_t ps = saddr(pring + st.i * PPStage);
+                const uint32_t kbj = (uint32_t)j * (BK / 2) + kb;
+                const uint32_t pofs = prow + ((((kbj >> 4) ^ pswz) << 4) | (kbj & 15u));
+                const uint4 H = lds128(ps + pofs), P = lds128(ps + kPlaneBox + pofs);
+                const uint32_t hw[4] = {H.x, H.y, H.z, H.w}, pw[4] = {P.x, P.y, P.z, P.w};
+                if (j == PSTEPS - 1 || ks == KS - 1) {
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive(&p_empty[st.i]);
+                    st.next<PSTAGES>();
+                }
+                if (!warp_wait(&w_empty[ws.i], ws.ph ^ 1u, alive))
+                    break;
+                tc_fence_after();
+                uint32_t ohi[16], olo[16];
+#pragma unroll
+                for (int wq = 0; wq < 4; ++wq) {
+                    uint32_t E, O;
+                    codes4(hw[wq], pw[wq], E, O);
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        /* (code << 8) | (lane << 2): entry `code`, this lane's replica */
+                        const uint32_t e0 = lds32(lutb + __byte_perm(E, lane4, 0x5504u | (b << 4)));
+                        const uint32_t e1 = lds32(lutb + __byte_perm(O, lane4, 0x5504u | (b << 4)));
+                        ohi[wq * 4 + b] = __byte_perm(e0, e1, 0x5410);
+                        olo[wq * 4 + b] = __byte_perm(e0, e1, 0x7632);
+                    }
+                }
+                const uint32_t slot = tw + (uint32_t)ws.i * BK;
+                tmem_st(slot, ohi);
+                tmem_st(slot + 32u, olo);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_remote(wfull0 + (uint32_t)ws.i * 8u);
+            }
+        }
+    } else if (warp < PPlaneWarp) {
+        /* ---- epilogue: warp w -> TMEM lanes 32*(w%4) (weight rows), columns c0 .. c0+31 */
+        const int q = warp & 3, c0 = ((warp - PEpi0) >> 2) * 32;
+        const uint32_t ae0 = peer_addr(saddr(&acc_empty[0]), 0);
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+        const int kb4 = args.K / 256; /* float4 groups of absmax per row */
+        int64_t g = 0;
+        for (int T = pair; T < args.tiles && alive; T += npairs) {
+            const int m0 = (T % args.mtiles) * PBMX + c0;
+            const int n = (T / args.mtiles) * (2 * BN) + (int)rank * BN + q * 32 + (int)lane;
+            const bool nok = n < args.N;
+            /* this row's absmax, four blocks per load, the next group loaded a group ahead */
+            const float4 *amr = reinterpret_cast<const float4 *>(args.am + (size_t)(nok ? n : 0) * (args.K / 64));
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 a4 = nok ? __ldg(amr) : z4, a4n = (nok && kb4 > 1) ? __ldg(amr + 1) : z4;
+            float run[32];
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj)
+                run[jj] = 0.f;
+            for (int ks = 0; ks < KS && alive; ++ks, ++g) {
+                const int b = (int)(g & 1);
+                if ((ks & 3) == 0 && ks > 0) {
+                    a4 = a4n;
+                    a4n = (nok && (ks >> 2) + 1 < kb4) ? __ldg(amr + (ks >> 2) + 1) : z4;
+                }
+                const float s = (ks & 3) == 0 ? a4.x : (ks & 3) == 1 ? a4.y : (ks & 3) == 2 ? a4.z : a4.w;
+                if (!warp_wait(&acc_full[b], (uint32_t)(g >> 1) & 1u, alive))
+                    break;
+                tc_fence_after();
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t v[16];
+                    tmem_ld16(tb + (uint32_t)b * PBMX + (uint32_t)h * 16u, v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj)
+                        run[h * 16 + jj] = fmaf(s, __uint_as_float(v[jj]), run[h * 16 + jj]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_remote(ae0 + (uint32_t)b * 8u);
+            }
+            if (!alive || !nok)
+                continue;
+            const size_t step = (size_t)args.N;
+            const int jl = min(32, args.M - m0);
+            if (args.y_bf16) {
+                __nv_bfloat16 *yp = static_cast<__nv_bfloat16 *>(args.y) + (size_t)m0 * step + n;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj, yp += step)
+                    if (jj < jl)
+                        *yp = __float2bfloat16_rn(run[jj]);
+            } else {
+                float *yp = static_cast<float *>(args.y) + (size_t)m0 * step + n;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj, yp += step)
+                    if (jj < jl)
+                        *yp = run[jj];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync(); /* the peer no longer reads this CTA's TMEM or shared memory */
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
 {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -711,30 +1045,32 @@ bool gemm_scratch(cudaStream_t st, size_t ws_floats, size_t n_counters, float **
     return true;
 }
 
-/* CTA pairs that fit on the device at once (one pair per two SMs at most) */
-int max_pairs()
+/* CTA pairs of `kernel` that fit on the device at once (one pair per two SMs at
+ * most); cached per device and kernel kind (0 fast, 1 precise) */
+int max_pairs(int kind = 0)
 {
-    static int cached[64] = {0};
+    static int cached[64][2] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return std::max(1, sm_count() / 2);
-    if (cached[dev] > 0)
-        return cached[dev];
+    if (cached[dev][kind] > 0)
+        return cached[dev][kind];
     int n = 0;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * std::max(1, sm_count() / 2));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.blockDim = dim3(kind ? PThreads : kThreads);
+    cfg.dynamicSmemBytes = kind ? PSmemBytes : kSmemBytes;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void *)htile_gemm_kernel, &cfg) != cudaSuccess || n <= 0) {
+    const void *kern = kind ? (const void *)htile_gemm_precise_kernel : (const void *)htile_gemm_kernel;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
         cudaGetLastError();
         n = std::max(1, sm_count() / 2);
     }
-    cached[dev] = n;
+    cached[dev][kind] = n;
     return n;
 }
 } // namespace
@@ -774,6 +1110,31 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
     if (!gemm_scratch(st, (size_t)pairs * 2 * 2 * 4 * kPartFloats, (size_t)tiles * 8, &a.ws, &a.counters))
         return kLaunch;
     htile_gemm_kernel<<<2 * pairs, kThreads, kSmemBytes, st>>>(maps, a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+}
+
+/* Precise mode at prefill shapes: the tcgen05 kernel with one fresh accumulator per
+ * 64-k absmax block (htile_gemm_precise_kernel). */
+int htile_gemm_precise_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
+                              void *y, bool y_bf16, int M, int N, int K, cudaStream_t st)
+{
+    Maps maps;
+    if (!encode_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, PBMH,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_map(&maps.h, CU_TENSOR_MAP_DATA_TYPE_UINT8, hole, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                    PSTEPS * BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_map(&maps.p, CU_TENSOR_MAP_DATA_TYPE_UINT8, plug, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                    PSTEPS * BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+        return kLaunch;
+    maps.am = maps.h; /* not read: the epilogue loads absmax itself */
+    if (!ensure_smem((const void *)htile_gemm_precise_kernel, PSmemBytes))
+        return kLaunch;
+    PreciseArgs a{};
+    a.y = y, a.am = am, a.M = M, a.N = N, a.K = K, a.y_bf16 = y_bf16 ? 1 : 0;
+    a.mtiles = (M + PBMX - 1) / PBMX;
+    a.tiles = a.mtiles * ((N + 2 * BN - 1) / (2 * BN));
+    const int pairs = std::max(1, std::min(a.tiles, max_pairs(1)));
+    htile_gemm_precise_kernel<<<2 * pairs, PThreads, PSmemBytes, st>>>(maps, a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
 }
 

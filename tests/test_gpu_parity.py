@@ -510,6 +510,16 @@ def test_htile_prefill_full_config_vs_oracle(M, N):
     assert np.all(np.isfinite(got))
     assert rel_err(got, ref) <= FAST_TOL, rel_err(got, ref)
     assert rel_err(gotb, ref) <= FAST_TOL, rel_err(gotb, ref)
+    # the reference's own entry point (precise: the cell as BF16 hi + lo, a fresh
+    # tensor-core accumulator per 64-k block, the blocks scaled and added in f32)
+    # within 1e-5 of max(1, max|ref|), as the other precise checks at long K
+    yr = D().htile_reference_abi(dx, *dev, N, 64)
+    yr2 = D().htile_reference_abi(dx, *dev, N, 64)
+    torch.cuda.synchronize()
+    assert L.glint_kernel_error(1) == 0
+    assert torch.equal(yr, yr2)
+    gotr = yr.index_select(0, idx).cpu().numpy()
+    assert rel_err(gotr, ref) <= PRECISE_TOL, rel_err(gotr, ref)
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 100, 256), (3, 1000, 512), (16, 4096, 14336), (17, 384, 2048), (32, 200, 4096),
