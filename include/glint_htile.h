@@ -6,9 +6,12 @@
  *
  * The two reference entry points keep their signatures (Jadon-Fox/glint
  * include/glint_htile.h:11-19, cuda/glint_htile.cu:165-187) and f32-class
- * accuracy: every dequantised weight reaches the tensor cores as a BF16 hi/lo
- * pair, so y matches an f32 dot product to about 1e-6 relative.  Any M, N, K,
- * blocksize and pointer alignment is accepted.
+ * accuracy: each codebook cell reaches the tensor cores as a BF16 hi/lo pair
+ * (about 17 significant bits), every 64-k absmax block is summed in a fresh
+ * accumulator and the blocks are scaled and added in f32, so y is within
+ * 1e-5 * (1 + |y|) of an f32 dot product on the reference's device-test shapes
+ * and within 1e-5 * max(1, max|y|) at K up to 14336.  Any M, N, K, blocksize and
+ * pointer alignment is accepted.
  * Return codes: 0 ok, -1 null pointer or negative size, -2 blocksize <= 0,
  * -3 launch failure.
  */
