@@ -497,13 +497,16 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
     synthetic Llama-3-70B (q/k/v/o 8192x8192 / 1024x8192, gate/up 28672x8192, down
     8192x28672; random-init BF16 N(0, 0.02), GLINT-packed: 68.4 G weights, 72.7 GB of
     planes), column-parallel over the ranks (glint_b200/tp.py; 72.7 GB / world per
-    GPU).  Per layer: q/k/v on the hidden state; o_proj on a fixed attention output
-    (attention itself is not on the path); gate and up, silu(gate) * up, down_proj,
-    whose output is the next layer's hidden state.  At world > 1 the outputs a
-    consumer needs whole (o, gate, up, down) are gathered inside their decode kernels
-    (tp.PeerGather: peer stores over NVLink), and the attention output that feeds
-    o_proj with one NCCL all-gather.  The whole 80-layer step is one CUDA graph,
-    replayed; device time with CUDA events, max over ranks."""
+    GPU).  The linears that read the same input are one weight each, as serving
+    stacks store them: q|k|v (10240 x 8192) and gate|up (57344 x 8192), the same
+    weights and bytes in four decode calls per layer instead of seven.  Per layer:
+    q|k|v on the hidden state; o_proj on a fixed attention output (attention itself
+    is not on the path); gate|up, silu(gate) * up, down_proj, whose output is the next
+    layer's hidden state.  At world > 1 the outputs a consumer needs whole (o,
+    gate|up, down) are gathered inside their decode kernels (tp.PeerGather: peer
+    stores over NVLink), and the attention output that feeds o_proj with one NCCL
+    all-gather.  The whole 80-layer step is one CUDA graph, replayed; device time
+    with CUDA events, max over ranks."""
     import torch
     import torch.nn.functional as F
     from glint_b200 import device as D
@@ -512,11 +515,15 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
     from glint_b200 import tp
     L = glint_cuda.load()
     layers = SH.LLAMA3_70B_LAYERS
+    dims = {nm: (N, K) for nm, N, K in SH.LLAMA3_70B_LAYER}
+    hid, inter = dims["o_proj"][0], dims["gate_proj"][0]
+    fused = {"qkv": (dims["q_proj"][0] + dims["k_proj"][0] + dims["v_proj"][0], hid), "o": (hid, hid),
+             "gu": (2 * inter, hid), "down": (hid, inter)}
     g = torch.Generator(device="cuda")
     stack, local_bytes = [], 0
     for l in range(layers):
         lay = {}
-        for j, (nm, N, K) in enumerate(SH.LLAMA3_70B_LAYER):
+        for j, (nm, (N, K)) in enumerate(fused.items()):
             n0, n1 = SH.column_shard(N, world, rank)
             g.manual_seed(100000 + 16 * l + j * 2 + 1000003 * rank)
             w = (torch.randn((n1 - n0) * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
@@ -526,38 +533,35 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
             local_bytes += h.numel() + p.numel() + a.numel() * 4
         stack.append(lay)
     torch.cuda.synchronize()
-    out = {"model": "Llama-3-70B linear stack, 80 layers x 7 GLINT decode linears (configs[4])", "tp": world,
-           "weight_bytes_per_gpu": int(local_bytes), "batches": {}}
+    out = {"model": "Llama-3-70B linear stack, 80 layers, q|k|v, o, gate|up, down GLINT decode linears (configs[4])",
+           "tp": world, "weight_bytes_per_gpu": int(local_bytes), "batches": {}}
     gx = torch.Generator(device="cuda")
     gx.manual_seed(7)  # activations replicated: the same on every rank
     for M in batches_m:
-        x0 = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
-        attn = torch.randn((M, 8192), generator=gx, device="cuda").to(torch.bfloat16)
+        x0 = torch.randn((M, hid), generator=gx, device="cuda").to(torch.bfloat16)
+        attn = torch.randn((M, hid), generator=gx, device="cuda").to(torch.bfloat16)
         pg = None
         if world > 1:
-            pg = tp.PeerGather({"o": (M, 8192, torch.float32), "gate": (M, 28672, torch.float32),
-                                "up": (M, 28672, torch.float32), "down": (M, 8192, torch.float32)}, world, rank)
-        hidden = torch.empty((M, 8192), dtype=torch.bfloat16, device="cuda")
+            pg = tp.PeerGather({"o": (M, hid, torch.float32), "gu": (M, 2 * inter, torch.float32),
+                                "down": (M, hid, torch.float32)}, world, rank)
+        hidden = torch.empty((M, hid), dtype=torch.bfloat16, device="cuda")
 
         def step():
             hidden.copy_(x0)
             for lay in stack:
-                for nm in ("q_proj", "k_proj", "v_proj"):
-                    tp.column_parallel(hidden, lay[nm], world, rank, gather=False)
+                tp.column_parallel(hidden, lay["qkv"], world, rank, gather=False)
                 if pg is None:
-                    tp.column_parallel(attn, lay["o_proj"], 1, 0)
-                    gate = tp.column_parallel(hidden, lay["gate_proj"], 1, 0)
-                    up = tp.column_parallel(hidden, lay["up_proj"], 1, 0)
-                    act = (F.silu(gate) * up).to(torch.bfloat16)
-                    d = tp.column_parallel(act, lay["down_proj"], 1, 0)
+                    tp.column_parallel(attn, lay["o"], 1, 0)
+                    gu = tp.column_parallel(hidden, lay["gu"], 1, 0)
+                    act = (F.silu(gu[:, :inter]) * gu[:, inter:]).to(torch.bfloat16)
+                    d = tp.column_parallel(act, lay["down"], 1, 0)
                 else:
-                    sh_o = lay["o_proj"]
-                    o_in = tp.gather_columns(attn[:, sh_o.n0:sh_o.n1].float(), 8192, world, rank)
+                    sh_o = lay["o"]
+                    o_in = tp.gather_columns(attn[:, sh_o.n0:sh_o.n1].float(), hid, world, rank)
                     pg.linear(o_in.to(torch.bfloat16), sh_o, "o")
-                    gate = pg.linear(hidden, lay["gate_proj"], "gate")
-                    up = pg.linear(hidden, lay["up_proj"], "up")
-                    act = (F.silu(gate) * up).to(torch.bfloat16)
-                    d = pg.linear(act, lay["down_proj"], "down")
+                    gu = pg.linear(hidden, lay["gu"], "gu")
+                    act = (F.silu(gu[:, :inter]) * gu[:, inter:]).to(torch.bfloat16)
+                    d = pg.linear(act, lay["down"], "down")
                 hidden.copy_(d)
 
         s = torch.cuda.Stream()
@@ -594,7 +598,7 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
                                   "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
     kerr = int(max_over_ranks(world, float(L.glint_kernel_error(1))))
     out["kernel_error"] = kerr
-    out["launches_per_step"] = layers * 7
+    out["launches_per_step"] = layers * len(fused)
     checks["decode_stack_ok"] = kerr == 0
     del stack
     torch.cuda.empty_cache()
