@@ -930,6 +930,13 @@ def profile_case(case: str, iters: int = 5):
     elif case == "expand":
         outs = [torch.empty_like(w) for w in ws]
         fn = lambda: D.expand_batch(planes, outs, BS)  # noqa: E731
+    elif case.startswith("gemmp"):
+        # precise mode at prefill shapes (the reference symbols' path)
+        M = int(case[5:] or 2048)
+        x = torch.randn((M, 4096), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, 14336), dtype=torch.float32, device="cuda")
+        n = 14336 * 4096
+        fn = lambda: D.htile_reference_abi(x, *planes[0], 14336, BS, out=y)  # noqa: E731
     elif case.startswith("gemm"):
         M = int(case[4:] or 2048)
         x = torch.randn((M, 4096), generator=g, device="cuda").to(torch.bfloat16)
@@ -971,7 +978,7 @@ def main():
     ap.add_argument("--impl", default="glint_b200", choices=["glint_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default=None,
-                    help="run one small kernel case (encode|expand|gemv<M>|gemvt<M>|gemm<M>) for ncu")
+                    help="run one small kernel case (encode|expand|gemv<M>|gemvt<M>|gemm<M>|gemmp<M>) for ncu")
     args = ap.parse_args()
     if args.profile:
         profile_case(args.profile)
