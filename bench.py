@@ -13,7 +13,8 @@ it.
 Sub-results in the same JSON line (kept short, so the whole line survives in a
 driver's output tail): expand of the same tensors back to BF16 (in
 roofline.others), decode GEMV and prefill GEMM on one
-GPU, the reference's own H-TILE entry point at the prefill shapes, the 80-layer
+GPU, the reference's own H-TILE entry point at the prefill shapes, the prefill GEMM
+column-parallel over the ranks with its output all-gathered, the 80-layer
 Llama-3-70B decode linear stack column-parallel over the ranks at
 batch 1 / 8 / 32, plug streaming and the pin pipeline (one GPU).  After each timed
 region its outputs are checked against the CPU oracle (`checks`).
@@ -358,6 +359,8 @@ def bench_glint(args):
 
     # ---- decode GEMV and prefill GEMM (per GPU)
     result["htile"] = bench_htile(args, pk, checks)
+    # ---- the prefill GEMM column-parallel over the ranks with the output all-gathered
+    result["prefill_tp"] = bench_prefill_tp(args, world, rank, pk)
     # ---- the 80-layer Llama-3-70B decode linear stack, column-parallel over the ranks
     result["decode_stack"] = bench_decode_stack(args, world, rank, pk, checks)
     if world == 1:
@@ -490,6 +493,71 @@ def bench_htile(args, pk, checks):
     checks["htile_max_rel_err"] = round(worst, 6)
     res["launches"] = launches
     return res
+
+
+def bench_prefill_tp(args, world, rank, pk, M: int = 2048, K: int = 4096, N: int = 14336):
+    """configs[3] column-parallel: every rank holds rows shard.column_shard(N, world,
+    rank) of one GLINT-packed [N, K] weight (0.1 % x20 outliers), runs the fast
+    prefill GEMM on them for the replicated x [M, K] and the output is all-gathered
+    over NVLink (NCCL all_gather_into_tensor of the f32 shards, then the column
+    interleave that restores row-major y [M, N]).  The step, the GEMM alone and the
+    gather alone are each a CUDA graph, replayed; device time, max over ranks."""
+    import torch
+    from glint_b200 import device as D
+    from glint_b200 import shard as SH
+    from glint_b200 import tp
+    n0, n1 = SH.column_shard(N, world, rank)
+    w = synth_tensor(N * K, 9090)  # the same weight on every rank; each keeps its rows
+    h, p, a = D.encode(w[n0 * K:n1 * K].contiguous(), BS)
+    del w
+    sh = tp.ColumnShard(n0, n1, N, K, BS, h, p, a)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+    y_loc = torch.empty((M, n1 - n0), dtype=torch.float32, device="cuda")
+
+    def gemm():
+        D.htile(x, sh.hole, sh.plug, sh.absmax, sh.rows, BS, mode="fast", out=y_loc)
+
+    def gather():
+        return tp.gather_columns(y_loc, N, world, rank)
+
+    def step():
+        gemm()
+        return gather()
+
+    def timed(fn, reps=10):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gr, stream=s):
+                fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = max_over_ranks(world, e0.elapsed_time(e1) * 1e3 / reps)
+        barrier(world)
+        del gr  # graphs holding NCCL calls go before the process group does
+        torch.cuda.synchronize()
+        return us
+    us_step = timed(step)
+    us_gemm = timed(gemm)
+    us_gather = timed(gather) if world > 1 else 0.0
+    flop = 2.0 * M * N * K
+    return {"shape": f"M{M} K{K} N{N}", "tp": world, "us_step": round(us_step, 1),
+            "tflops_all_ranks": round(flop / (us_step * 1e-6) / 1e12, 1), "us_gemm": round(us_gemm, 1),
+            "us_gather": round(us_gather, 1), "y_bytes": M * N * 4}
 
 
 def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
