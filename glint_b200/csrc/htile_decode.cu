@@ -214,6 +214,57 @@ __device__ __forceinline__ int frag_row(int g)
     return ROWB == 128 ? (((g & 3) << 1) | (g >> 2)) : ((g & 1) | (((g >> 1) & 1) << 2) | ((g >> 2) << 1));
 }
 
+/* Arithmetic of one 64-k block (see tile_block): codes -> codebook -> MMAs -> the
+ * block's sums scaled by its absmax and added to acc. */
+template <int MT, bool SPLIT>
+__device__ __forceinline__ void tile_math(const uint32_t (&E)[2][2], const uint32_t (&O)[2][2], const float (&sc)[2],
+                                          const uint4 (&xb)[MT][2], uint32_t lut_base, uint32_t lane4,
+                                          float (&acc)[MT][4])
+{
+    /* two accumulators (even and odd MMA steps) keep the chains independent */
+    float part[2][MT][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+            part[h][mt][0] = part[h][mt][1] = part[h][mt][2] = part[h][mt][3] = 0.f;
+#pragma unroll
+    for (int st = 0; st < 4; ++st) {
+        const int wd = st >> 1, b0 = (st & 1) * 2;
+        uint32_t e[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            /* address = (code << 8) | (lane << 2): byte b0 or b0+1 of E / O into byte 1 */
+            e[r][0] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | (b0 << 4)));
+            e[r][1] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | (b0 << 4)));
+            e[r][2] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
+            e[r][3] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
+        }
+        const uint32_t ahi[4] = {__byte_perm(e[0][0], e[0][1], 0x5410), __byte_perm(e[1][0], e[1][1], 0x5410),
+                                 __byte_perm(e[0][2], e[0][3], 0x5410), __byte_perm(e[1][2], e[1][3], 0x5410)};
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+            const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
+            mma_bf16_16816(part[st & 1][mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+        }
+        if (SPLIT) {
+            const uint32_t alo[4] = {__byte_perm(e[0][0], e[0][1], 0x7632), __byte_perm(e[1][0], e[1][1], 0x7632),
+                                     __byte_perm(e[0][2], e[0][3], 0x7632), __byte_perm(e[1][2], e[1][3], 0x7632)};
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
+                mma_bf16_16816(part[st & 1][mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            acc[mt][q] = fmaf(sc[q >> 1], part[0][mt][q] + part[1][mt][q], acc[mt][q]);
+    }
+}
+
 /* One 64-k absmax block of a 16-row weight tile against the activations:
  * acc[mt] += absmax * (W[rows r0+g, r0+g+8][block] . x[mt*8+g'][block]).
  * `hole`/`plug`: plane tiles with ROWB-byte rows (128: 128B swizzle, 16-byte chunk j
@@ -261,48 +312,76 @@ __device__ __forceinline__ void tile_block(uint32_t hole, uint32_t plug, uint32_
         xb[mt][0] = lds128_if(rowb + (((uint32_t)(2 * t) ^ ph) << 4), live);
         xb[mt][1] = lds128_if(rowb + (((uint32_t)(2 * t + 1) ^ ph) << 4), live);
     }
-    /* two accumulators (even and odd MMA steps) keep the chains independent */
-    float part[2][MT][4];
+    tile_math<MT, SPLIT>(E, O, sc, xb, lut_base, lane4, acc);
+}
+
+/* Shared-memory byte offsets, within a ring stage, of one lane's operands of one 64-k
+ * block: its two plane rows, their absmax and its activation chunks.  They depend
+ * only on the warp, the lane and the block's place in the unit, so the row-owned
+ * kernel computes them once, outside its K loop (in the loop their arithmetic cost
+ * about half an instruction per weight at M = 1). */
+template <int MT>
+struct BlockOffs {
+    uint32_t pl[2];          /* plane bytes of rows frag_row(g) and frag_row(g) + 8 */
+    uint32_t am[2];          /* their absmax */
+    uint32_t x0[MT], x1[MT]; /* the lane's two 16-byte activation chunks per row group */
+    uint32_t live;           /* bit mt: activation row mt * 8 + g < M */
+};
+
+/* Offsets for 64-k block c of rows starting at row ro of 128-byte plane rows (128B
+ * swizzle), absmax rows of 16 bytes at am_off (column am_col) and activation rows of
+ * 128 bytes at x_off whose first row has swizzle phase xph (as tile_block reads them). */
+template <int MT>
+__device__ __forceinline__ BlockOffs<MT> block_offs(int c, int r0, int ro, int g, int t, uint32_t am_off,
+                                                    uint32_t am_col, uint32_t x_off, uint32_t xph, int M)
+{
+    BlockOffs<MT> o;
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-            part[h][mt][0] = part[h][mt][1] = part[h][mt][2] = part[h][mt][3] = 0.f;
-#pragma unroll
-    for (int st = 0; st < 4; ++st) {
-        const int wd = st >> 1, b0 = (st & 1) * 2;
-        uint32_t e[2][4];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            /* address = (code << 8) | (lane << 2): byte b0 or b0+1 of E / O into byte 1 */
-            e[r][0] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | (b0 << 4)));
-            e[r][1] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | (b0 << 4)));
-            e[r][2] = lds32(lut_base + __byte_perm(E[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
-            e[r][3] = lds32(lut_base + __byte_perm(O[r][wd], lane4, 0x5504 | ((b0 + 1) << 4)));
-        }
-        const uint32_t ahi[4] = {__byte_perm(e[0][0], e[0][1], 0x5410), __byte_perm(e[1][0], e[1][1], 0x5410),
-                                 __byte_perm(e[0][2], e[0][3], 0x5410), __byte_perm(e[1][2], e[1][3], 0x5410)};
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-            const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-            mma_bf16_16816(part[st & 1][mt], ahi, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
-        }
-        if (SPLIT) {
-            const uint32_t alo[4] = {__byte_perm(e[0][0], e[0][1], 0x7632), __byte_perm(e[1][0], e[1][1], 0x7632),
-                                     __byte_perm(e[0][2], e[0][3], 0x7632), __byte_perm(e[1][2], e[1][3], 0x7632)};
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-                const uint32_t xw[4] = {xb[mt][wd].x, xb[mt][wd].y, xb[mt][wd].z, xb[mt][wd].w};
-                mma_bf16_16816(part[st & 1][mt], alo, xw[(st & 1) * 2], xw[(st & 1) * 2 + 1]);
-            }
-        }
+    for (int r = 0; r < 2; ++r) {
+        const int row = ro + r0 + frag_row<128>(g) + 8 * r;
+        const uint32_t chunk = (uint32_t)(2 * c + (t >> 1)) ^ (uint32_t)(row & 7);
+        o.pl[r] = (uint32_t)row * 128u + (chunk << 4) + (uint32_t)(t & 1) * 8u;
+        o.am[r] = am_off + (uint32_t)row * 16u + am_col * 4u;
     }
+    o.live = 0u;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            acc[mt][q] = fmaf(sc[q >> 1], part[0][mt][q] + part[1][mt][q], acc[mt][q]);
+        const int m = mt * 8 + g;
+        const uint32_t ph = (xph + (uint32_t)m) & 7u;
+        o.x0[mt] = x_off + (uint32_t)m * 128u + (((uint32_t)(2 * t) ^ ph) << 4);
+        o.x1[mt] = x_off + (uint32_t)m * 128u + (((uint32_t)(2 * t + 1) ^ ph) << 4);
+        o.live |= (m < M ? 1u : 0u) << mt;
     }
+    return o;
+}
+
+/* tile_block with the operands at precomputed offsets from the stage base `st`
+ * (plug tile at st + pt). */
+template <int MT, bool SPLIT>
+__device__ __forceinline__ void tile_block_at(uint32_t st, uint32_t pt, const BlockOffs<MT> &o, uint32_t lut_base,
+                                              uint32_t lane4, float (&acc)[MT][4])
+{
+    uint32_t E[2][2], O[2][2];
+    float sc[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint2 hw = lds64(st + o.pl[r]), pw = lds64(st + pt + o.pl[r]);
+        const uint32_t hv[2] = {hw.x, hw.y}, pv[2] = {pw.x, pw.y};
+#pragma unroll
+        for (int wd = 0; wd < 2; ++wd) {
+            E[r][wd] = ((hv[wd] << 4) & 0xF0F0F0F0u) | (pv[wd] & 0x0F0F0F0Fu);
+            O[r][wd] = (hv[wd] & 0xF0F0F0F0u) | ((pv[wd] >> 4) & 0x0F0F0F0Fu);
+        }
+        sc[r] = __uint_as_float(lds32(st + o.am[r]));
+    }
+    uint4 xb[MT][2];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        const bool live = (o.live >> mt) & 1u;
+        xb[mt][0] = lds128_if(st + o.x0[mt], live);
+        xb[mt][1] = lds128_if(st + o.x1[mt], live);
+    }
+    tile_math<MT, SPLIT>(E, O, sc, xb, lut_base, lane4, acc);
 }
 
 template <int MT, bool SPLIT, bool BF16OUT>
@@ -826,6 +905,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     /* warp kh takes the unit's 64-k blocks [kh*NB, (kh+1)*NB) (block b: slice b/4, block b%4) */
     const int tile = warp / KH, kh = warp % KH, b0 = kh * NB, r0 = tile * 16;
+    /* block b of a unit: 64-k block c of slice u, whose rows start at row u RB of the
+     * plane and absmax tiles; activation block 4 u + c */
+    BlockOffs<MT> offs[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+        const int b = b0 + j, c = b & 3, u = b >> 2, xb = b * a.xrows;
+        offs[j] = block_offs<MT>(c, r0, u * a.RB, g, t, (uint32_t)(2 * a.pt), (uint32_t)c,
+                                 (uint32_t)(2 * a.pt + a.at + xb * 128), (uint32_t)xb & 7u, a.M);
+    }
     float acc[MT][4];
     bool alive = true;
     int s = 0;
@@ -842,14 +930,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const uint32_t st = saddr(ring + s * stage_bytes);
 #pragma unroll
-            for (int j = 0; j < NB; ++j) {
-                /* block b: 64-k block c of slice u, whose rows start at row u RB of the
-                 * plane and absmax tiles; activation block 4 u + c */
-                const int b = b0 + j, c = b & 3, u = b >> 2, xb = b * a.xrows;
-                tile_block<MT, SPLIT, 128>(st, st + a.pt, st + 2 * a.pt, (uint32_t)c,
-                                           st + 2 * a.pt + a.at + (uint32_t)xb * 128u, (uint32_t)xb & 7u, c, r0,
-                                           u * a.RB, g, t, lut_base, lane4, a.M, acc);
-            }
+            for (int j = 0; j < NB; ++j)
+                tile_block_at<MT, SPLIT>(st, (uint32_t)a.pt, offs[j], lut_base, lane4, acc);
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(&empty[s]);
