@@ -498,10 +498,13 @@ def bench_htile(args, pk, checks):
 def bench_prefill_tp(args, world, rank, pk, M: int = 2048, K: int = 4096, N: int = 14336):
     """configs[3] column-parallel: every rank holds rows shard.column_shard(N, world,
     rank) of one GLINT-packed [N, K] weight (0.1 % x20 outliers), runs the fast
-    prefill GEMM on them for the replicated x [M, K] and the output is all-gathered
-    over NVLink (NCCL all_gather_into_tensor of the f32 shards, then the column
-    interleave that restores row-major y [M, N]).  The step, the GEMM alone and the
-    gather alone are each a CUDA graph, replayed; device time, max over ranks."""
+    prefill GEMM on them for the replicated x [M, K], and every rank ends with the
+    whole row-major y [M, N] f32.  Two ways: the gather fused into the GEMM
+    (tp.PeerGather: the epilogue stores each tile into every rank's y over NVLink;
+    `us_step`), and the GEMM followed by NCCL all_gather_into_tensor of the f32
+    shards plus the column interleave (`us_step_nccl`, with `us_gemm` and
+    `us_gather_nccl` alone).  Each is a CUDA graph, replayed; device time, max over
+    ranks.  At one GPU the step is the GEMM."""
     import torch
     from glint_b200 import device as D
     from glint_b200 import shard as SH
@@ -525,6 +528,11 @@ def bench_prefill_tp(args, world, rank, pk, M: int = 2048, K: int = 4096, N: int
     def step():
         gemm()
         return gather()
+
+    pg = tp.PeerGather({"y": (M, N, torch.float32)}, world, rank) if world > 1 else None
+
+    def fused():
+        return pg.linear(x, sh, "y", mode="fast")
 
     def timed(fn, reps=10):
         s = torch.cuda.Stream()
@@ -551,13 +559,20 @@ def bench_prefill_tp(args, world, rank, pk, M: int = 2048, K: int = 4096, N: int
         del gr  # graphs holding NCCL calls go before the process group does
         torch.cuda.synchronize()
         return us
-    us_step = timed(step)
     us_gemm = timed(gemm)
-    us_gather = timed(gather) if world > 1 else 0.0
+    if world > 1:
+        us_step = timed(fused)
+        us_nccl = timed(step)
+        us_gather = timed(gather)
+        pg.close()
+    else:
+        us_step = us_nccl = us_gemm
+        us_gather = 0.0
     flop = 2.0 * M * N * K
     return {"shape": f"M{M} K{K} N{N}", "tp": world, "us_step": round(us_step, 1),
             "tflops_all_ranks": round(flop / (us_step * 1e-6) / 1e12, 1), "us_gemm": round(us_gemm, 1),
-            "us_gather": round(us_gather, 1), "y_bytes": M * N * 4}
+            "us_step_nccl": round(us_nccl, 1), "us_gather_nccl": round(us_gather, 1), "y_bytes": M * N * 4,
+            "gather": "fused into the GEMM epilogue (peer stores); NCCL all-gather + interleave beside it"}
 
 
 def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):

@@ -676,11 +676,16 @@ int glint_htile_gather_stream(const uint8_t *d_hole, const uint8_t *d_plug, cons
         return kBadBlocksize;
     if (M <= 0 || N <= 0 || K <= 0 || n0 < 0 || ld_y < n0 + N)
         return kBadArg;
-    if (!htile_decode_supported(d_hole, d_plug, d_absmax, d_x, M, N, K, blocksize) || !htile_gather_supported(M, N))
-        return kUnsupported;
-    return htile_decode_gather_launch(d_hole, d_plug, d_absmax, d_x, d_y_ranks, d_flag_ranks, world, rank,
-                                      y_dtype == GLINT_Y_BF16 ? kOutBF16 : kOutF32, M, N, K, ld_y, n0,
-                                      mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
+    const bool bf16 = y_dtype == GLINT_Y_BF16;
+    if (htile_decode_supported(d_hole, d_plug, d_absmax, d_x, M, N, K, blocksize) && htile_gather_supported(M, N))
+        return htile_decode_gather_launch(d_hole, d_plug, d_absmax, d_x, d_y_ranks, d_flag_ranks, world, rank,
+                                          bf16 ? kOutBF16 : kOutF32, M, N, K, ld_y, n0,
+                                          mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
+    /* prefill shapes: the tcgen05 GEMM stores its tiles into every rank's y */
+    if (mode == GLINT_HTILE_FAST && htile_gemm_supported(d_hole, d_plug, d_absmax, d_x, nullptr, bf16, M, N, K, blocksize))
+        return htile_gemm_gather_launch(d_hole, d_plug, d_absmax, d_x, d_y_ranks, d_flag_ranks, world, rank, bf16, M,
+                                        N, K, ld_y, n0, stream);
+    return kUnsupported;
 }
 
 int glint_device_alloc(size_t bytes, void **d_ptr)

@@ -63,6 +63,11 @@ bool htile_gemm_supported(const uint8_t *hole, const uint8_t *plug, const float 
                           const void *y, bool y_bf16, int M, int N, int K, int blocksize);
 int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x, void *y,
                       bool y_bf16, int M, int N, int K, int blocksize, cudaStream_t stream);
+/* The same with the output gathered into every rank's y over peer memory (the
+ * epilogue stores each tile into every rank's y[M, ldy] at column n0 + n). */
+int htile_gemm_gather_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
+                             void *const *y_ranks, uint32_t *const *flag_ranks, int world, int rank, bool y_bf16,
+                             int M, int N, int K, int ldy, int n0, cudaStream_t stream);
 /* The same shapes in precise mode (f32-class: a fresh accumulator per 64-k block,
  * BF16 hi + lo weight halves, the blocks scaled and added in f32). */
 int htile_gemm_precise_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,

@@ -42,6 +42,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "gather.cuh"
 #include "glint_internal.h"
 #include "ptx.cuh"
 
@@ -105,77 +106,6 @@ __device__ __forceinline__ void build_pair_lut(uint32_t *lut)
     }
 }
 
-/* Gathered output (world > 0): this call's rows [n0, n0 + N) of y[M, ldy] are
- * stored into every rank's y (yr[r], this rank's own included), then counted in
- * (gather_complete).  world == 0: plain y. */
-constexpr int kMaxGather = 8;
-struct GatherArgs {
-    int world, rank, ldy, n0;
-    uint32_t *flag; /* this rank's counters: [r] calls whose rows rank r has delivered here, [kMaxGather] warps done */
-    void *yr[kMaxGather];
-    uint32_t *fr[kMaxGather]; /* every rank's counters */
-};
-template <bool BF16OUT>
-__device__ __forceinline__ void gather_store(const GatherArgs &g, int col, int n, float v)
-{
-    /* every rank's y: NVLink stores to the peers, a local store for this rank */
-    const int64_t o = (int64_t)col * g.ldy + g.n0 + n;
-    for (int r = 0; r < g.world; ++r) {
-        if (BF16OUT)
-            static_cast<__nv_bfloat16 *>(g.yr[r])[o] = __float2bfloat16_rn(v);
-        else
-            static_cast<float *>(g.yr[r])[o] = v;
-    }
-}
-/* End of a gathered call, run by every active consumer warp after its last y
- * stores.  The warp counts itself in, first in its CTA (shared memory), the CTA's
- * last warp then in the rank (one global atomic per CTA); the rank's last warp
- * resets the count and, after a system-scope fence, adds one to its own slot in
- * every rank's counters, then waits (acquire, system scope), bounded,
- * for one arrival from every rank and takes it (subtracts one).  Each rank's
- * arrivals come in call order and a rank can be at most one call ahead (its next
- * call cannot finish before this rank's arrival), so taking one per rank per call
- * never confuses calls; nothing here depends on a call number, so the same launch
- * can be replayed (CUDA graphs).  The kernel completes only when this rank's y
- * holds every rank's rows.  Ranks run on different GPUs; inside a rank only this
- * one warp waits. */
-__device__ __forceinline__ void gather_complete(const GatherArgs &a, int active, uint32_t lane, uint32_t *cta_done)
-{
-    /* the counting chain orders every warp's stores before the rank's last warp
-     * with device-scope acquire-release fences (fence, count; observe the count,
-     * fence); that warp's one system-scope acquire-release fence followed by the
-     * signals forms a release pattern that covers them all (an sc fence, or a
-     * release on every signal, cost ~5 us more per call for the same ordering) */
-    __syncwarp();
-    if (lane != 0)
-        return;
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    if (atomicAdd(cta_done, 1u) + 1u != (uint32_t)active)
-        return;
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    if (atomicAdd(a.flag + kMaxGather, 1u) + 1u != gridDim.x)
-        return;
-    atomicExch(a.flag + kMaxGather, 0u);
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    for (int r = 0; r < a.world; ++r)
-        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(a.fr[r] + a.rank) : "memory");
-    const long long t0 = clock64();
-    for (int r = 0; r < a.world; ++r) {
-        while (true) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.flag + r) : "memory");
-            if (v != 0u) {
-                atomicSub(a.flag + r, 1u);
-                break;
-            }
-            if (clock64() - t0 > kWaitCycles) {
-                atomicOr(&g_decode_error, kErrTimeout);
-                return;
-            }
-            __nanosleep(128);
-        }
-    }
-}
 struct DecodeArgs {
     const __nv_bfloat16 *x;
     void *y;
@@ -625,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (cur_rb >= 0)
         flush(cur_rb, seg_k0, (int)(u1 - 1 - (int64_t)cur_rb * a.KU) + 1);
     if (a.ga.world > 0)
-        gather_complete(a.ga, kConsumers, lane, cta_done);
+        gather_complete(a.ga, kConsumers, lane, cta_done, &g_decode_error);
 }
 
 /* ---- row-owned decode for wide layers ------------------------------------------
@@ -994,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     if (a.ga.world > 0)
-        gather_complete(a.ga, active, lane, cta_done);
+        gather_complete(a.ga, active, lane, cta_done, &g_decode_error);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder()
@@ -1451,12 +1381,9 @@ int htile_decode_gather_launch(const uint8_t *hole, const uint8_t *plug, const f
                                void *const *y_ranks, uint32_t *const *flag_ranks, int world, int rank,
                                OutKind yk, int M, int N, int K, int ldy, int n0, HtileMode mode, cudaStream_t st)
 {
-    if (world < 1 || world > kMaxGather || rank < 0 || rank >= world || !htile_gather_supported(M, N))
+    GatherArgs g;
+    if (!htile_gather_supported(M, N) || !make_gather_args(&g, y_ranks, flag_ranks, world, rank, ldy, n0))
         return kUnsupported;
-    GatherArgs g{};
-    g.world = world, g.rank = rank, g.ldy = ldy, g.n0 = n0, g.flag = flag_ranks[rank];
-    for (int r = 0; r < world; ++r)
-        g.yr[r] = y_ranks[r], g.fr[r] = flag_ranks[r];
     return decode_launch_impl(hole, plug, am, x, y_ranks[rank], yk, M, N, K, mode, st, &g);
 }
 

@@ -49,6 +49,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "gather.cuh"
 #include "glint_internal.h"
 #include "ptx.cuh"
 
@@ -243,6 +244,7 @@ struct GemmArgs {
     int tiles;
     float *ws;    /* partial tiles of split tiles: [pair][slot 2][rank 2][quadrant 4][kPartFloats] */
     int *counters; /* per tile, rank and quadrant: contributors done (reset by the last) */
+    GatherArgs ga; /* world > 0: y[m, n] goes to every rank's y at [m, ga.n0 + n] (row stride ga.ldy) */
 };
 
 /* Work split (stream-K for the first S tiles, then data-parallel rounds): the
@@ -280,24 +282,40 @@ struct Maps {
     CUtensorMap x, h, p, am;
 };
 
-/* rows m0 .. m0+jl-1 of y at column n from 32 accumulator values (f32 bits) */
-__device__ __forceinline__ void store_y(const GemmArgs &args, const uint32_t (&v)[32], int m0, int jl, int n)
+/* rows m0 .. m0+jl-1 of a row-major y (row stride `step`) at column n from 32
+ * accumulator values (f32 bits) */
+__device__ __forceinline__ void store_rows(void *y, bool y_bf16, size_t step, const uint32_t (&v)[32], int m0,
+                                           int jl, int n)
 {
-    if (n >= args.N)
-        return;
-    const size_t step = (size_t)args.N;
-    if (args.y_bf16) {
-        __nv_bfloat16 *yp = static_cast<__nv_bfloat16 *>(args.y) + (size_t)m0 * step + n;
+    if (y_bf16) {
+        __nv_bfloat16 *yp = static_cast<__nv_bfloat16 *>(y) + (size_t)m0 * step + n;
 #pragma unroll
         for (int j = 0; j < 32; ++j, yp += step)
             if (j < jl)
                 *yp = __float2bfloat16_rn(__uint_as_float(v[j]));
     } else {
-        float *yp = static_cast<float *>(args.y) + (size_t)m0 * step + n;
+        float *yp = static_cast<float *>(y) + (size_t)m0 * step + n;
 #pragma unroll
         for (int j = 0; j < 32; ++j, yp += step)
             if (j < jl)
                 *yp = __uint_as_float(v[j]);
+    }
+}
+/* y rows m0 .. m0+jl-1 at column n: this call's y, or in a gathered call every
+ * rank's y (peers over NVLink, starting with the next rank so that the ranks'
+ * stores spread over the links) */
+__device__ __forceinline__ void store_y(const GemmArgs &args, const uint32_t (&v)[32], int m0, int jl, int n)
+{
+    if (n >= args.N)
+        return;
+    if (args.ga.world == 0) {
+        store_rows(args.y, args.y_bf16, (size_t)args.N, v, m0, jl, n);
+        return;
+    }
+#pragma unroll 1
+    for (int i = 1; i <= args.ga.world; ++i) {
+        const int r = (args.ga.rank + i) % args.ga.world;
+        store_rows(args.ga.yr[r], args.y_bf16, (size_t)args.ga.ldy, v, m0, jl, args.ga.n0 + n);
     }
 }
 
@@ -319,6 +337,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint64_t *acc_empty = acc_full + 1;  /* leader: both CTAs' epilogues drained */
     uint64_t *mma_done = acc_empty + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+    uint32_t *cta_done = tmem_slot + 1; /* gathered calls: epilogue warps done */
 
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = lane_id();
@@ -348,6 +367,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, 2 * kEpiWarps);
         mbar_init(mma_done, 1);
+        *cta_done = 0;
         mbar_init_fence();
     }
     if (warp == 1) {
@@ -615,6 +635,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 store_y(args, v, m0 + c * 32, min(32, mlim - c * 32), n);
             }
         }
+        if (args.ga.world > 0)
+            gather_complete(args.ga, kEpiWarps, lane, cta_done, &g_glint_kernel_error);
     }
     tc_fence_before();
     __syncthreads();
@@ -1075,10 +1097,10 @@ int max_pairs(int kind = 0)
 }
 } // namespace
 
-int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
-                      bool y_bf16, int M, int N, int K, int bs, cudaStream_t st)
+namespace {
+int gemm_launch_impl(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                     bool y_bf16, int M, int N, int K, cudaStream_t st, const GatherArgs *ga)
 {
-    (void)bs;
     Maps maps;
     if (!encode_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BMH,
                     CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1093,6 +1115,8 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
         return kLaunch;
     GemmArgs a{};
     a.y = y, a.M = M, a.N = N, a.K = K, a.y_bf16 = y_bf16 ? 1 : 0;
+    if (ga)
+        a.ga = *ga;
     a.mtiles = (M + BMX - 1) / BMX, a.ntiles = (N + 2 * BN - 1) / (2 * BN);
     a.G = K / (PSTEPS * BK);
     const int tiles = a.mtiles * a.ntiles;
@@ -1111,6 +1135,24 @@ int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am,
         return kLaunch;
     htile_gemm_kernel<<<2 * pairs, kThreads, kSmemBytes, st>>>(maps, a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+}
+} // namespace
+
+int htile_gemm_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x, void *y,
+                      bool y_bf16, int M, int N, int K, int bs, cudaStream_t st)
+{
+    (void)bs;
+    return gemm_launch_impl(hole, plug, am, x, y, y_bf16, M, N, K, st, nullptr);
+}
+
+int htile_gemm_gather_launch(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
+                             void *const *y_ranks, uint32_t *const *flag_ranks, int world, int rank, bool y_bf16,
+                             int M, int N, int K, int ldy, int n0, cudaStream_t st)
+{
+    GatherArgs g;
+    if (!make_gather_args(&g, y_ranks, flag_ranks, world, rank, ldy, n0))
+        return kUnsupported;
+    return gemm_launch_impl(hole, plug, am, x, y_ranks[rank], y_bf16, M, N, K, st, &g);
 }
 
 /* Precise mode at prefill shapes: the tcgen05 kernel with one fresh accumulator per

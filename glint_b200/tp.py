@@ -163,10 +163,13 @@ class PeerGather:
         dist.barrier(group=group)
 
     @staticmethod
-    def supported(M: int, rows: int) -> bool:
-        """Shapes the gathered kernel covers (the decode kernels, M <= 32; also
-        bs == 64 and K % 256 == 0, as for the decode path)."""
-        return 1 <= M <= 32 and rows >= 1
+    def supported(M: int, rows: int, mode: str = "fast") -> bool:
+        """Shapes a gathered call covers, given bs == 64, K % 256 == 0 and 16-byte
+        aligned operands: the decode kernels at M <= 32 (both modes) and the
+        tcgen05 prefill GEMM at M >= 128 (fast mode)."""
+        if rows < 1:
+            return False
+        return 1 <= M <= 32 or (M >= 128 and mode == "fast")
 
     def linear(self, x: torch.Tensor, sh: ColumnShard, name: str, mode: str = "fast", stream=None) -> torch.Tensor:
         """y[M, N] = x . W^T on every rank: this rank's rows [n0, n1) computed here,

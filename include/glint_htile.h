@@ -96,9 +96,11 @@ int glint_htile_stream_noalloc(
  * glint_kernel_error() = 1); the same launch may be replayed in a CUDA graph.
  * Peer buffers come from glint_device_alloc and are shared with
  * glint_ipc_handle / glint_ipc_open.
- * Covers 1 <= M <= 32, bs == 64, K % 256 == 0, 16-byte aligned operands,
- * world <= 8; else GLINT_ERR_UNSUPPORTED.  The calls of a group go on one stream
- * per rank. */
+ * Covers bs == 64, K % 256 == 0, 16-byte aligned operands, world <= 8, and
+ * 1 <= M <= 32 (the decode kernels, either mode) or M >= 128 in fast mode (the
+ * prefill GEMM, whose epilogue stores each finished tile into every rank's y
+ * while later tiles compute); else GLINT_ERR_UNSUPPORTED.  The calls of a group
+ * go on one stream per rank. */
 #define GLINT_ERR_UNSUPPORTED (-6)
 int glint_htile_gather_stream(
     const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax,

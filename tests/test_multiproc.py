@@ -185,3 +185,71 @@ def test_gathered_decode_two_gpus():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.spawn(_gather_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _prefill_gather_worker(rank, world, port):
+    import os
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist = _init(rank, world, port, backend="nccl")
+    from glint_b200 import device as D
+    from glint_b200 import glint_cuda
+    from glint_b200 import tp
+    L = glint_cuda.load()
+    L.glint_kernel_error(1)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(47)  # the same weights and activations on every rank
+    # (N, K, M): 7168 rows per rank at M = 2048 give 224 tiles on the CTA pairs, so
+    # the stream-K remainder (split tiles summed by their last contributor) runs
+    # gathered too; M = 320 leaves the second activation tile a quarter full
+    for N, K, M, dt in [(14336, 4096, 2048, torch.float32), (8192, 4096, 320, torch.bfloat16)]:
+        w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        hole, plug, am = D.encode(w, 64)
+        del w
+        sh = tp.ColumnShard.from_full(hole, plug, am, N, K, 64, rank, world)
+        assert tp.PeerGather.supported(M, sh.rows, "fast") and not tp.PeerGather.supported(M, sh.rows, "precise")
+        pg = tp.PeerGather({"y": (M, N, dt)}, world, rank)
+        for _ in range(3):  # consecutive calls alternate the buffers and reuse the counters
+            x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+            y = pg.linear(x, sh, "y", mode="fast")
+            mine = D.htile(x, sh.hole, sh.plug, sh.absmax, sh.rows, 64, mode="fast", out_dtype=dt)
+            full = D.htile(x, hole, plug, am, N, 64, mode="fast", out_dtype=dt)
+            torch.cuda.synchronize()
+            # this rank's columns: the same kernel on the same shard, bit for bit
+            assert torch.equal(y[:, sh.n0:sh.n0 + sh.rows], mine), (N, M)
+            # every column: the one-GPU GEMM's bound
+            err = float((y.float() - full.float()).abs().max() / max(1.0, float(full.float().abs().max())))
+            assert err <= 1e-2, (N, M, err)
+            # every rank holds the same y
+            sums = [torch.zeros(2, dtype=torch.float64, device="cuda") for _ in range(world)]
+            dist.all_gather(sums, torch.stack([y.double().sum(), y.double().abs().sum()]))
+            assert all(torch.equal(sums[0], t) for t in sums), (N, M)
+        pg.close()
+        del hole, plug, am, sh
+    assert L.glint_kernel_error(1) == 0
+    # a rank that skips a gathered prefill call: the other's GEMM gives up after
+    # about a second with the error word set, instead of hanging
+    N, K, M = 4096, 1024, 128
+    w = (torch.randn(N * K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    hole, plug, am = D.encode(w, 64)
+    sh = tp.ColumnShard.from_full(hole, plug, am, N, K, 64, rank, world)
+    pg = tp.PeerGather({"y": (M, N, torch.float32)}, world, rank)
+    if rank == 0:
+        x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+        pg.linear(x, sh, "y", mode="fast")
+        torch.cuda.synchronize()
+        assert L.glint_kernel_error(1) == 1
+    pg.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_gathered_prefill_two_gpus():
+    """Column-parallel prefill with the all-gather fused into the tcgen05 GEMM's
+    epilogue: every rank ends with the whole y; its own columns equal the
+    ungathered GEMM on its shard bit for bit and every column is within the fast
+    bound of the one-GPU GEMM, over repeated calls (data-parallel and stream-K
+    tiles, ragged M, f32 and BF16 y); a skipped call times out with an error."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_prefill_gather_worker, args=(2, _free_port()), nprocs=2, join=True)
