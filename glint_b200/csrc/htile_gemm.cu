@@ -301,10 +301,11 @@ __device__ __forceinline__ void store_rows(void *y, bool y_bf16, size_t step, co
                 *yp = __uint_as_float(v[j]);
     }
 }
-/* y rows m0 .. m0+jl-1 at column n: this call's y, or in a gathered call every
- * rank's y (peers over NVLink, starting with the next rank so that the ranks'
- * stores spread over the links) */
-__device__ __forceinline__ void store_y(const GemmArgs &args, const uint32_t (&v)[32], int m0, int jl, int n)
+/* y rows m0 .. m0+jl-1 at column n: this call's y; in a gathered call this
+ * rank's y and, with `peers`, every other rank's (over NVLink, starting with the
+ * next rank so that the ranks' stores spread over the links) */
+__device__ __forceinline__ void store_y(const GemmArgs &args, const uint32_t (&v)[32], int m0, int jl, int n,
+                                        bool peers)
 {
     if (n >= args.N)
         return;
@@ -312,10 +313,40 @@ __device__ __forceinline__ void store_y(const GemmArgs &args, const uint32_t (&v
         store_rows(args.y, args.y_bf16, (size_t)args.N, v, m0, jl, n);
         return;
     }
+    const size_t ld = (size_t)args.ga.ldy;
+    store_rows(args.ga.yr[args.ga.rank], args.y_bf16, ld, v, m0, jl, args.ga.n0 + n);
+    if (!peers)
+        return;
 #pragma unroll 1
-    for (int i = 1; i <= args.ga.world; ++i) {
-        const int r = (args.ga.rank + i) % args.ga.world;
-        store_rows(args.ga.yr[r], args.y_bf16, (size_t)args.ga.ldy, v, m0, jl, args.ga.n0 + n);
+    for (int i = 1; i < args.ga.world; ++i)
+        store_rows(args.ga.yr[(args.ga.rank + i) % args.ga.world], args.y_bf16, ld, v, m0, jl, args.ga.n0 + n);
+}
+/* Gathered call, after a whole tile's accumulator is released: rows m0 ..
+ * m0+rows-1 at column n, which this thread has just stored into this rank's y
+ * (still in L2), copied to every other rank's y.  The NVLink stores so run while
+ * the tensor cores work on the next tile instead of holding the accumulator. */
+template <typename T>
+__device__ __forceinline__ void copy_rows_to_peers(const GatherArgs &g, int m0, int rows, int col)
+{
+    const size_t ld = (size_t)g.ldy, o = (size_t)m0 * ld + col;
+    const T *src = static_cast<const T *>(g.yr[g.rank]) + o;
+#pragma unroll 1
+    for (int i = 1; i < g.world; ++i) {
+        int r = g.rank + i;
+        r = r >= g.world ? r - g.world : r;
+        T *dst = static_cast<T *>(g.yr[r]) + o;
+        const T *sp = src;
+        int j = 0;
+        /* four loads issued before their four stores: the compiler may not move a
+         * load past a store that could alias it, so the batch is explicit */
+#pragma unroll 1
+        for (; j + 4 <= rows; j += 4, sp += 4 * ld, dst += 4 * ld) {
+            const T a = sp[0], b = sp[ld], c = sp[2 * ld], e = sp[3 * ld];
+            dst[0] = a, dst[ld] = b, dst[2 * ld] = c, dst[3 * ld] = e;
+        }
+#pragma unroll 1
+        for (; j < rows; ++j, sp += ld, dst += ld)
+            *dst = *sp;
     }
 }
 
@@ -559,12 +590,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     uint32_t v[32];
                     tmem_ld32(tb + c * 32, v);
                     tmem_ld_wait();
-                    store_y(args, v, m0 + c * 32, min(32, mlim - c * 32), n);
+                    store_y(args, v, m0 + c * 32, min(32, mlim - c * 32), n, false);
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
                     mbar_arrive_remote(accempty0);
+                if (args.ga.world > 1 && n < args.N) {
+                    if (args.y_bf16)
+                        copy_rows_to_peers<__nv_bfloat16>(args.ga, m0, mlim, args.ga.n0 + n);
+                    else
+                        copy_rows_to_peers<float>(args.ga, m0, mlim, args.ga.n0 + n);
+                }
                 continue;
             }
             /* slot 0: the first segment of this pair's range, slot 1: its last */
@@ -632,7 +669,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 16; ++j)
                         v[h * 16 + j] = __float_as_uint(acc[j]);
                 }
-                store_y(args, v, m0 + c * 32, min(32, mlim - c * 32), n);
+                store_y(args, v, m0 + c * 32, min(32, mlim - c * 32), n, true);
             }
         }
         if (args.ga.world > 0)
