@@ -25,6 +25,7 @@
 #include "../../include/glint_b200.h"
 #include "../../include/glint_encode.h"
 #include "../../include/glint_htile.h"
+#include "../../include/glint_km.h"
 #include "common.cuh"
 #include "glint_internal.h"
 
@@ -460,6 +461,22 @@ int sm_count()
     return S.sms;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
 bool ensure_smem(const void *kernel, int bytes)
 {
     const int d = current_device();
@@ -754,6 +771,70 @@ int glint_htile_stream_noalloc(const uint8_t *d_hole, const uint8_t *d_plug, con
         return kBadArg;
     return htile_decode_launch_noalloc(d_hole, d_plug, d_absmax, d_x, d_y, y_dtype == GLINT_Y_BF16 ? kOutBF16 : kOutF32,
                                        M, N, K, mode == GLINT_HTILE_FAST ? kFast : kPrecise, stream);
+}
+
+/* ---- K-major decode (include/glint_km.h) ---- */
+/* The device address of a plug plane: device or managed memory as given, pinned
+ * host memory through its mapping; nullptr for memory the device cannot read
+ * (never handed to a kernel). */
+static const uint8_t *device_view(const uint8_t *p)
+{
+    cudaPointerAttributes at{};
+    if (!p || cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged)
+        return p;
+    if (at.type == cudaMemoryTypeHost && at.devicePointer)
+        return static_cast<const uint8_t *>(at.devicePointer);
+    return nullptr;
+}
+
+int glint_kmajor_from_rowmajor(const uint8_t *d_hole, const uint8_t *d_plug, const float *d_absmax, int n, int K,
+                               int blocksize, uint8_t *d_hole_k, uint8_t *d_plug_k, float *d_scales_k,
+                               cudaStream_t stream)
+{
+    if (!d_hole || !d_absmax || !d_hole_k || !d_scales_k || (!d_plug) != (!d_plug_k))
+        return kBadArg;
+    if (blocksize != 64)
+        return kBadBlocksize;
+    if (!km_supported(n, K, d_hole_k, d_scales_k) || (d_plug_k && !aligned_to(d_plug_k, 16)))
+        return kBadArg;
+    return km_layout_launch(d_hole, d_plug, d_absmax, n, K, d_hole_k, d_plug_k, d_scales_k, stream);
+}
+int glint_gemv_km_stream(const uint8_t *d_hole_k, const float *d_scales_k, const __nv_bfloat16 *d_x, float *d_y,
+                         int n, int K, cudaStream_t stream)
+{
+    if (!d_hole_k || !d_scales_k || !d_x || !d_y || !km_supported(n, K, d_hole_k, d_scales_k))
+        return kBadArg;
+    return km_gemv_launch(d_hole_k, d_scales_k, d_x, d_y, n, K, stream);
+}
+int glint_select_topk_stream(const __nv_bfloat16 *d_x, int K, int nsel, int *d_idx, int *d_cnt, cudaStream_t stream)
+{
+    if (!d_x || !d_idx || !d_cnt || K < 1 || K > kKmMaxK || nsel < 0)
+        return kBadArg;
+    return km_select_launch(d_x, K, nsel, d_idx, d_cnt, stream);
+}
+int glint_apply_corr_k_stream(const uint8_t *d_hole_k, const uint8_t *plug_k, const float *d_scales_k,
+                              const __nv_bfloat16 *d_x, const int *d_idx, const int *d_cnt, float *d_y, int n, int K,
+                              cudaStream_t stream)
+{
+    const uint8_t *pk = device_view(plug_k);
+    if (!d_hole_k || !pk || !d_scales_k || !d_x || !d_idx || !d_cnt || !d_y ||
+        !km_supported(n, K, d_hole_k, d_scales_k) || !aligned_to(pk, 16))
+        return kBadArg;
+    return km_corr_launch(d_hole_k, pk, d_scales_k, d_x, d_idx, d_cnt, d_y, n, K, stream);
+}
+int glint_gemv_select_stream(const uint8_t *d_hole_k, const uint8_t *plug_k, const float *d_scales_k,
+                             const __nv_bfloat16 *d_x, float *d_y, int n, int K, int nsel, int *d_idx, int *d_cnt,
+                             cudaStream_t stream)
+{
+    const uint8_t *pk = device_view(plug_k);
+    if (!d_hole_k || !pk || !d_scales_k || !d_x || !d_y || !d_idx || !d_cnt || nsel < 0 ||
+        !km_supported(n, K, d_hole_k, d_scales_k) || !aligned_to(pk, 16))
+        return kBadArg;
+    return km_gemv_select_launch(d_hole_k, pk, d_scales_k, d_x, d_y, n, K, nsel, d_idx, d_cnt, stream);
 }
 
 } /* extern "C" */

@@ -583,22 +583,6 @@ int launch_fast(const EncodeBatch &b, int bs_log2, cudaStream_t st)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
-
 /* BF16 tensor of n weights as [n / 32 rows][32] for 64-byte-swizzled TMA boxes of
  * 256 rows; false when the driver entry point is missing or the map is refused */
 bool bf16_row_map(CUtensorMap *m, const void *w, int64_t n)

@@ -3,6 +3,7 @@
 #define GLINT_B200_INTERNAL_H_
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -78,6 +79,7 @@ int read_kernel_error(bool clear);
 int encode_error_word(bool clear);
 int expand_error_word(bool clear);
 int decode_error_word(bool clear);
+int km_error_word(bool clear);
 /* Decode-shaped path streamed through TMA (bs == 64, K % 256 == 0, M <= 32). */
 bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const float *absmax, const __nv_bfloat16 *x,
                             int M, int N, int K, int blocksize);
@@ -95,6 +97,26 @@ int htile_decode_gather_launch(const uint8_t *hole, const uint8_t *plug, const f
                                const __nv_bfloat16 *x, void *const *y_ranks, uint32_t *const *flag_ranks,
                                int world, int rank, OutKind y_kind, int M, int N, int K, int ldy, int n0,
                                HtileMode mode, cudaStream_t stream);
+
+/* K-major layout, parent-only decode GEMV and activation-selected plug correction
+ * (kmajor.cu): n % 8 == 0, K % 64 == 0, K <= kKmMaxK, blocksize 64, 16-byte
+ * aligned planes and scales. */
+constexpr int kKmMaxK = 65536;
+bool km_supported(int n, int K, const void *hole_k, const void *scales_k);
+int km_layout_launch(const uint8_t *hole, const uint8_t *plug, const float *absmax, int n, int K, uint8_t *hole_k,
+                     uint8_t *plug_k, float *scales_k, cudaStream_t stream);
+int km_gemv_launch(const uint8_t *hole_k, const float *scales_k, const __nv_bfloat16 *x, float *y, int n, int K,
+                   cudaStream_t stream);
+int km_select_launch(const __nv_bfloat16 *x, int K, int nsel, int *idx, int *cnt, cudaStream_t stream);
+int km_corr_launch(const uint8_t *hole_k, const uint8_t *plug_k, const float *scales_k, const __nv_bfloat16 *x,
+                   const int *idx, const int *cnt, float *y, int n, int K, cudaStream_t stream);
+int km_gemv_select_launch(const uint8_t *hole_k, const uint8_t *plug_k, const float *scales_k,
+                          const __nv_bfloat16 *x, float *y, int n, int K, int nsel, int *idx, int *cnt,
+                          cudaStream_t stream);
+
+/* cuTensorMapEncodeTiled through the runtime's driver entry point (nullptr when the
+ * driver does not offer it); looked up once. */
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 /* SM count of the current device (cached per device). */
 int sm_count();

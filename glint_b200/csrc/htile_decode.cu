@@ -927,28 +927,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         gather_complete(a.ga, active, lane, cta_done, &g_decode_error);
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encoder()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
-
 /* 3-D map: dims (d0, d1, d2) with byte strides s1, s2 for dims 1 and 2 (any order
  * of sizes), box (b0, b1, b2). */
 bool make_map3(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
                uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw)
 {
-    auto enc = encoder();
+    auto enc = tensor_map_encoder();
     if (!enc)
         return false;
     cuuint64_t dims[3] = {d0, d1, d2};
@@ -962,7 +946,7 @@ bool make_map3(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_
 bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t cols, uint64_t rows,
               uint64_t row_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle sw)
 {
-    auto enc = encoder();
+    auto enc = tensor_map_encoder();
     if (!enc)
         return false;
     cuuint64_t dims[2] = {cols, rows};
@@ -1234,7 +1218,7 @@ bool htile_decode_supported(const uint8_t *hole, const uint8_t *plug, const floa
 {
     /* K % 256: the absmax rows (K/64 floats) must be a multiple of 16 bytes for TMA */
     return M >= 1 && M <= 32 && bs == 64 && K % 256 == 0 && aligned_to(hole, 16) && aligned_to(plug, 16) &&
-           aligned_to(am, 16) && aligned_to(x, 16) && N >= 1 && encoder() != nullptr;
+           aligned_to(am, 16) && aligned_to(x, 16) && N >= 1 && tensor_map_encoder() != nullptr;
 }
 
 /* tensor maps of one call: plane rows of kKU/2 bytes (64B or 128B swizzle) */

@@ -1018,22 +1018,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PThreads, 1)
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-        else
-            cudaGetLastError();
-    });
-    return fn;
-}
-
 } // namespace
 
 bool htile_gemm_supported(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
@@ -1222,10 +1206,11 @@ int read_kernel_error(bool clear)
     const int v = read_error_word(g_glint_kernel_error, g_glint_kernel_error_taken, clear);
     if (v < 0)
         return -1;
-    const int e = encode_error_word(clear), x = expand_error_word(clear), d = decode_error_word(clear);
-    if (e < 0 || x < 0 || d < 0)
+    const int e = encode_error_word(clear), x = expand_error_word(clear), d = decode_error_word(clear),
+              k = km_error_word(clear);
+    if (e < 0 || x < 0 || d < 0 || k < 0)
         return -1;
-    return v | e | x | d;
+    return v | e | x | d | k;
 }
 
 } // namespace glint

@@ -153,3 +153,93 @@ def htile_reference_abi(x: torch.Tensor, hole, plug, absmax, N: int, blocksize: 
                                                 out.data_ptr(), M, N, K, blocksize, _stream(stream))
     _check(rc, "launch_glint_htile_s3_f32_stream")
     return out
+
+
+# ---- K-major decode: parent-only GEMV + activation-selected plug correction ----
+# (include/glint_km.h; the reference's Mojo decoders' glint_gemv_km, select_topk,
+# apply_corr_k, transpose_plug / transpose_scales)
+
+def to_kmajor(hole: torch.Tensor, plug: torch.Tensor, absmax: torch.Tensor, N: int, K: int, blocksize: int = 64,
+              plug_out: Optional[torch.Tensor] = None, stream=None):
+    """(hole_k, plug_k, scales_k) of a GLINT weight [N, K]: planes [K, N/2] bytes
+    (row r of channel c in nibble r & 1 of byte c*N/2 + r/2), scales [K/64, N] f32.
+    plug_out may be a pinned host tensor to receive plug_k (copied after the
+    device transform), for a decode that reads plug rows from host memory."""
+    for t, nm in ((hole, "hole"), (plug, "plug"), (absmax, "absmax")):
+        _cuda(t, nm)
+    dev = hole.device
+    hk = torch.empty(K * N // 2, dtype=torch.uint8, device=dev)
+    pk = torch.empty(K * N // 2, dtype=torch.uint8, device=dev)
+    sk = torch.empty((K // 64) * N, dtype=torch.float32, device=dev)
+    rc = lib().glint_kmajor_from_rowmajor(hole.data_ptr(), plug.data_ptr(), absmax.data_ptr(), N, K, blocksize,
+                                          hk.data_ptr(), pk.data_ptr(), sk.data_ptr(), _stream(stream))
+    _check(rc, "glint_kmajor_from_rowmajor")
+    if plug_out is not None:
+        plug_out.copy_(pk, non_blocking=True)
+        pk = plug_out
+    return hk, pk, sk
+
+
+def _x_vec(x: torch.Tensor) -> torch.Tensor:
+    _cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.numel() != x.shape[-1] or x.dim() > 2:
+        raise ValueError("x must be one bfloat16 row [K] or [1, K]")
+    return x
+
+
+def _plug_ptr(plug_k: torch.Tensor) -> int:
+    if not (plug_k.is_cuda or plug_k.is_pinned()):
+        raise ValueError("plug_k must be a CUDA tensor or pinned host memory")
+    if not plug_k.is_contiguous():
+        raise ValueError("plug_k must be contiguous")
+    return plug_k.data_ptr()
+
+
+def gemv_km(x: torch.Tensor, hole_k: torch.Tensor, scales_k: torch.Tensor, N: int, out=None,
+            stream=None) -> torch.Tensor:
+    """Parent-only y[N] = sum_c PARENT[h] * scale * x[c] (M = 1), f32."""
+    x = _x_vec(x)
+    K = x.shape[-1]
+    y = out if out is not None else torch.empty(N, dtype=torch.float32, device=x.device)
+    rc = lib().glint_gemv_km_stream(hole_k.data_ptr(), scales_k.data_ptr(), x.data_ptr(), y.data_ptr(), N, K,
+                                    _stream(stream))
+    _check(rc, "glint_gemv_km_stream")
+    return y
+
+
+def select_topk(x: torch.Tensor, nsel: int, idx=None, cnt=None, stream=None):
+    """(idx [K] int32, cnt [1] int32): the channels kept by the |x| rule, ascending
+    in idx[:cnt]; both stay on the device."""
+    x = _x_vec(x)
+    K = x.shape[-1]
+    idx = idx if idx is not None else torch.empty(K, dtype=torch.int32, device=x.device)
+    cnt = cnt if cnt is not None else torch.empty(1, dtype=torch.int32, device=x.device)
+    rc = lib().glint_select_topk_stream(x.data_ptr(), K, nsel, idx.data_ptr(), cnt.data_ptr(), _stream(stream))
+    _check(rc, "glint_select_topk_stream")
+    return idx, cnt
+
+
+def apply_corr_k(y: torch.Tensor, x: torch.Tensor, hole_k, plug_k, scales_k, idx, cnt, N: int,
+                 stream=None) -> torch.Tensor:
+    """y += sum over the selected channels of (CELLS - PARENT)[h][p] * scale * x[c], in place."""
+    x = _x_vec(x)
+    K = x.shape[-1]
+    rc = lib().glint_apply_corr_k_stream(hole_k.data_ptr(), _plug_ptr(plug_k), scales_k.data_ptr(), x.data_ptr(),
+                                         idx.data_ptr(), cnt.data_ptr(), y.data_ptr(), N, K, _stream(stream))
+    _check(rc, "glint_apply_corr_k_stream")
+    return y
+
+
+def gemv_select(x: torch.Tensor, hole_k, plug_k, scales_k, N: int, nsel: int, out=None, idx=None, cnt=None,
+                stream=None):
+    """One decode step: select the channels, parent GEMV, plug correction.
+    Returns (y [N] f32, idx, cnt)."""
+    x = _x_vec(x)
+    K = x.shape[-1]
+    y = out if out is not None else torch.empty(N, dtype=torch.float32, device=x.device)
+    idx = idx if idx is not None else torch.empty(K, dtype=torch.int32, device=x.device)
+    cnt = cnt if cnt is not None else torch.empty(1, dtype=torch.int32, device=x.device)
+    rc = lib().glint_gemv_select_stream(hole_k.data_ptr(), _plug_ptr(plug_k), scales_k.data_ptr(), x.data_ptr(),
+                                        y.data_ptr(), N, K, nsel, idx.data_ptr(), cnt.data_ptr(), _stream(stream))
+    _check(rc, "glint_gemv_select_stream")
+    return y, idx, cnt

@@ -84,6 +84,15 @@ def _bind(lib):
     lib.glint_ipc_open.restype = i32
     lib.glint_ipc_close.argtypes = [vp]
     lib.glint_ipc_close.restype = i32
+    # K-major decode (include/glint_km.h, additive)
+    lib.glint_kmajor_from_rowmajor.argtypes = [vp, vp, vp, i32, i32, i32, vp, vp, vp, vp]
+    lib.glint_gemv_km_stream.argtypes = [vp, vp, vp, vp, i32, i32, vp]
+    lib.glint_select_topk_stream.argtypes = [vp, i32, i32, vp, vp, vp]
+    lib.glint_apply_corr_k_stream.argtypes = [vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]
+    lib.glint_gemv_select_stream.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]
+    for f in (lib.glint_kmajor_from_rowmajor, lib.glint_gemv_km_stream, lib.glint_select_topk_stream,
+              lib.glint_apply_corr_k_stream, lib.glint_gemv_select_stream):
+        f.restype = i32
     # plug streamer (include/glint_plug_streamer.h)
     lib.glint_plug_streamer_create.argtypes = [ctypes.POINTER(vp), i32, ctypes.POINTER(ctypes.c_uint64), vp, vp]
     lib.glint_plug_streamer_create.restype = i32

@@ -17,6 +17,13 @@
  *   - H-TILE reference    cuda/glint_htile.cu:124-164 (weights dequantised in
  *                         f32, products accumulated in f64 as in
  *                         tests/test_htile_k_bounds_device.cu:90-95)
+ *   - K-major layout, parent-only GEMV, channel selection, plug correction
+ *                         mojo/p7_glint_select_decode.mojo:120-143,
+ *                         mojo/p7_glint_gemv_km.mojo:17-95,
+ *                         mojo/p7_select_device.mojo:15-153, 197-238
+ *                         (no Mojo toolchain here: these are pinned through the
+ *                         identity parent + full correction == H-TILE, and the
+ *                         selection rule against a sort-based definition)
  * Parity is pinned against golden vectors that tests/golden/make_golden.py wrote
  * by running the reference's own glint_np.py / glint_htile_sim.py.
  *
@@ -240,6 +247,121 @@ int orc_htile(const uint8_t *hole, const uint8_t *plug, const float *am, const u
             }
             y[(int64_t)m * N + nn] = (float)acc;
         }
+    }
+    return 0;
+}
+
+/* ---- K-major layout, parent-only GEMV, activation-selected plug correction ----
+ * The reference's Mojo decoders (mojo/p7_glint_gemv_km.mojo, mojo/p7_select_device.mojo,
+ * mojo/p7_glint_select_decode.mojo).  A weight [n, K] (bs 64, K % 64 == 0, n even)
+ * in K-major form: plane_k[c * n/2 + r/2] holds row r of input channel c in nibble
+ * r & 1 (low nibble first); scales_k[(c / 64) * n + r] = absmax[r * K/64 + c / 64]. */
+
+/* transpose_plug (mojo/p7_glint_select_decode.mojo:120-135), applied to both planes,
+ * and transpose_scales (mojo/p7_select_device.mojo:197-208). */
+int orc_to_kmajor(const uint8_t *hole, const uint8_t *plug, const float *am, int n, int K, uint8_t *hole_k,
+                  uint8_t *plug_k, float *scales_k)
+{
+    if (n <= 0 || K <= 0 || (n & 1) || K % 64)
+        return -1;
+    const int64_t half = n / 2;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int64_t g = 0; g < (int64_t)K * half; ++g) {
+        const int64_t c = g / half, b = g - c * half;
+        const int64_t j0 = (2 * b) * (int64_t)K + c, j1 = (2 * b + 1) * (int64_t)K + c;
+        hole_k[g] = (uint8_t)(((hole[j0 >> 1] >> (4 * (j0 & 1))) & 15) | (((hole[j1 >> 1] >> (4 * (j1 & 1))) & 15) << 4));
+        if (plug && plug_k)
+            plug_k[g] =
+                (uint8_t)(((plug[j0 >> 1] >> (4 * (j0 & 1))) & 15) | (((plug[j1 >> 1] >> (4 * (j1 & 1))) & 15) << 4));
+    }
+    const int cb_n = K / 64;
+    for (int64_t g = 0; g < (int64_t)n * cb_n; ++g) {
+        const int64_t r = g / cb_n, cb = g - r * cb_n;
+        scales_k[cb * n + r] = am[g];
+    }
+    return 0;
+}
+
+static inline int nib_k(const uint8_t *plane_k, int64_t half, int64_t c, int64_t r)
+{
+    return (plane_k[c * half + (r >> 1)] >> (4 * (r & 1))) & 15;
+}
+
+/* glint_gemv_km + gemv_km_combine (mojo/p7_glint_gemv_km.mojo:17-95): y[r] =
+ * sum_c (PARENT[h] * scales_k[c/64][r]) * x[c], M = 1, in the reference's order:
+ * channels ascending within each of ksg equal slices (f32, one product rounded,
+ * then the multiply by x, then the add), slices added in order.  The reference
+ * takes its 16 parent values from a table built as t0[h*16 + p] = PARENT[h]
+ * (make_tables, mojo/p7_glint_select_decode.mojo:136-143). */
+int orc_gemv_km(const uint8_t *hole_k, const float *scales_k, const uint16_t *x, float *y, int n, int K, int ksg)
+{
+    if (n <= 0 || K <= 0 || (n % 8) || ksg <= 0 || K % (64 * ksg))
+        return -1;
+    const int64_t half = n / 2;
+    const int kslice = K / ksg;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int r = 0; r < n; ++r) {
+        float tot = 0.f;
+        for (int s = 0; s < ksg; ++s) {
+            float a = 0.f;
+            for (int c = s * kslice; c < (s + 1) * kslice; ++c) {
+                const float t = GLINT_PARENT[nib_k(hole_k, half, c, r)] * scales_k[(int64_t)(c / 64) * n + r];
+                a += t * bf16_to_f32(x[c]);
+            }
+            tot = s == 0 ? a : tot + a;
+        }
+        y[r] = tot;
+    }
+    return 0;
+}
+
+/* select_topk with its default rule (mojo/p7_select_device.mojo:15-153, tkey = 0,
+ * nfloor = 0): key = BF16 bits & 0x7FFF; T = the largest 15-bit value such that at
+ * least nsel keys are >= T (T = 0 when fewer than nsel channels exist); nsel == 0
+ * selects nothing.  Every channel with key >= T is kept (ties all kept), indices
+ * ascending.  Returns the count, or -1 for nsel < 0. */
+int orc_select_topk(const uint16_t *x, int K, int nsel, int32_t *idx)
+{
+    if (nsel < 0 || K < 0)
+        return -1;
+    int thr = 0;
+    for (int bi = 0; bi < 15; ++bi) {
+        const int cand = thr | (1 << (14 - bi));
+        int c = 0;
+        for (int i = 0; i < K; ++i)
+            c += (x[i] & 0x7FFF) >= cand;
+        if (c >= nsel)
+            thr = cand;
+    }
+    if (nsel == 0)
+        thr = 32768;
+    int cnt = 0;
+    for (int i = 0; i < K; ++i)
+        if ((x[i] & 0x7FFF) >= thr)
+            idx[cnt++] = i;
+    return cnt;
+}
+
+/* apply_corr_k (mojo/p7_select_device.mojo:210-238) with the staged plug rows read
+ * in place from plug_k: y[r] = y[r] + sum_{i < cnt} (delta[h][p] * scales_k[c/64][r])
+ * * x[c], c = idx[i] in list order, f32, delta = CELLS[h][p] - PARENT[h] (make_tables,
+ * mojo/p7_glint_select_decode.mojo:136-143). */
+int orc_apply_corr_k(const uint8_t *hole_k, const uint8_t *plug_k, const float *scales_k, const uint16_t *x,
+                     const int32_t *idx, int cnt, float *y, int n, int K)
+{
+    if (n <= 0 || K <= 0 || (n & 1) || cnt < 0)
+        return -1;
+    const int64_t half = n / 2;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int r = 0; r < n; ++r) {
+        float acc = 0.f;
+        for (int i = 0; i < cnt; ++i) {
+            const int64_t c = idx[i];
+            const int h = nib_k(hole_k, half, c, r), p = nib_k(plug_k, half, c, r);
+            const float d = GLINT_CELLS[h][p] - GLINT_PARENT[h];
+            acc += (d * scales_k[(c / 64) * n + r]) * bf16_to_f32(x[c]);
+        }
+        y[r] = y[r] + acc;
     }
     return 0;
 }

@@ -63,6 +63,12 @@ def lib():
     L.orc_f32_to_bf16.restype = ctypes.c_uint16
     L.orc_htile.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32]
     L.orc_htile.restype = i32
+    L.orc_to_kmajor.argtypes = [vp, vp, vp, i32, i32, vp, vp, vp]
+    L.orc_gemv_km.argtypes = [vp, vp, vp, vp, i32, i32, i32]
+    L.orc_select_topk.argtypes = [vp, i32, i32, vp]
+    L.orc_apply_corr_k.argtypes = [vp, vp, vp, vp, vp, i32, vp, i32, i32]
+    for f in (L.orc_to_kmajor, L.orc_gemv_km, L.orc_select_topk, L.orc_apply_corr_k):
+        f.restype = i32
     _LIB = L
     return L
 
@@ -134,6 +140,58 @@ def htile(hole, plug, am, x_bf16: np.ndarray, M: int, N: int, K: int, blocksize:
     if rc:
         raise ValueError(f"orc_htile rc={rc}")
     return y
+
+
+def to_kmajor(hole, plug, am, n: int, K: int):
+    """(hole_k, plug_k, scales_k): planes [K, n/2] bytes (row r of channel c in
+    nibble r & 1 of byte c*n/2 + r/2), scales [K/64, n] f32 (transpose_plug /
+    transpose_scales of the reference's Mojo decoder)."""
+    hole = np.ascontiguousarray(hole, np.uint8)
+    plug = np.ascontiguousarray(plug, np.uint8)
+    am = np.ascontiguousarray(am, np.float32)
+    hk = np.empty(K * n // 2, np.uint8)
+    pk = np.empty(K * n // 2, np.uint8)
+    sk = np.empty(K // 64 * n, np.float32)
+    if lib().orc_to_kmajor(_ptr(hole), _ptr(plug), _ptr(am), n, K, _ptr(hk), _ptr(pk), _ptr(sk)):
+        raise ValueError("to_kmajor: n must be even and K a multiple of 64")
+    return hk, pk, sk
+
+
+def gemv_km(hole_k, scales_k, x_bf16: np.ndarray, n: int, K: int, ksg: int = 1) -> np.ndarray:
+    """Parent-only y[n] = sum_c PARENT[h] * scale * x[c] (M = 1), the reference's
+    f32 order over ksg channel slices."""
+    y = np.empty(n, np.float32)
+    hk = np.ascontiguousarray(hole_k, np.uint8)
+    sk = np.ascontiguousarray(scales_k, np.float32)
+    x = np.ascontiguousarray(x_bf16, np.uint16).reshape(-1)
+    if lib().orc_gemv_km(_ptr(hk), _ptr(sk), _ptr(x), _ptr(y), n, K, ksg):
+        raise ValueError("gemv_km: n % 8 == 0 and K % (64 ksg) == 0 required")
+    return y
+
+
+def select_topk(x_bf16: np.ndarray, nsel: int) -> np.ndarray:
+    """Selected input channels (int32, ascending) by the reference's |x| rule."""
+    x = np.ascontiguousarray(x_bf16, np.uint16).reshape(-1)
+    idx = np.empty(max(1, x.size), np.int32)
+    cnt = lib().orc_select_topk(_ptr(x), x.size, nsel, _ptr(idx))
+    if cnt < 0:
+        raise ValueError("nsel must be >= 0")
+    return idx[:cnt].copy()
+
+
+def apply_corr_k(y: np.ndarray, hole_k, plug_k, scales_k, x_bf16: np.ndarray, idx: np.ndarray, n: int,
+                 K: int) -> np.ndarray:
+    """y + sum over the selected channels of (CELLS - PARENT)[h][p] * scale * x[c]."""
+    out = np.array(y, np.float32, copy=True)
+    hk = np.ascontiguousarray(hole_k, np.uint8)
+    pk = np.ascontiguousarray(plug_k, np.uint8)
+    sk = np.ascontiguousarray(scales_k, np.float32)
+    x = np.ascontiguousarray(x_bf16, np.uint16).reshape(-1)
+    ix = np.ascontiguousarray(idx, np.int32)
+    if lib().orc_apply_corr_k(_ptr(hk), _ptr(pk), _ptr(sk), _ptr(x), _ptr(ix) if ix.size else None, ix.size,
+                              _ptr(out), n, K):
+        raise ValueError("apply_corr_k: bad arguments")
+    return out
 
 
 def codes_for_bits(lo: int, count: int) -> np.ndarray:
