@@ -233,7 +233,10 @@ constexpr int kSStages = 6;
 constexpr int kSCons = 16;   /* consumer warps: two halves of 8, each on half of a stage's channels */
 constexpr int kSThreads = (kSCons + 1) * 32;
 constexpr int kStageBytes = kSCh * kSegBytes; /* 16 KB */
-constexpr int kSSmem = kPairBytes + kSStages * kStageBytes + kSStages * 32 + 2 * kSStages * 8 + 16;
+/* dynamic shared memory: pair table, stage ring (TMA destinations: 128-byte aligned
+ * offsets), x values, barriers, the 16 parents; no static shared memory in the
+ * kernel, so the dynamic area starts at the base */
+constexpr int kSSmem = kPairBytes + kSStages * kStageBytes + kSStages * 32 + 2 * kSStages * 8 + 16 * 4;
 
 __device__ __forceinline__ uint64_t lds64u(uint32_t a)
 {
@@ -280,6 +283,7 @@ __global__ void __launch_bounds__(kSThreads, 1) gemv_km_stream_kernel(const __gr
     uint8_t *xring = ring + kSStages * kStageBytes;
     uint64_t *full = reinterpret_cast<uint64_t *>(xring + kSStages * 32);
     uint64_t *empty = full + kSStages;
+    float *par = reinterpret_cast<float *>(empty + kSStages);
     const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
     const int p = (int)blockIdx.x;
     const int64_t ub = km_unit_begin(a, p), ue = km_unit_begin(a, p + 1);
@@ -290,9 +294,18 @@ __global__ void __launch_bounds__(kSThreads, 1) gemv_km_stream_kernel(const __gr
         }
         mbar_init_fence();
     }
+    if ((smem_u32(ring) & 127u) != 0u) {
+        /* a tensor copy needs a 128-byte aligned destination: report, never issue */
+        if (threadIdx.x == 0)
+            atomicOr(&g_km_error, 2);
+        return;
+    }
+    if (threadIdx.x < 16)
+        par[threadIdx.x] = g_parent[threadIdx.x];
+    __syncthreads();
     for (int i = threadIdx.x; i < 256 * 32 / 2; i += kSThreads) {
         const int e = i >> 4;
-        const float2 pr = make_float2(g_parent[e & 15], g_parent[e >> 4]);
+        const float2 pr = make_float2(par[e & 15], par[e >> 4]);
         reinterpret_cast<float4 *>(pairs)[i] = make_float4(pr.x, pr.y, pr.x, pr.y);
     }
     __syncthreads();
@@ -408,7 +421,7 @@ __global__ void __launch_bounds__(kSThreads, 1) gemv_km_stream_kernel(const __gr
 }
 
 /* ---- channel selection ------------------------------------------------------- */
-constexpr int kSelThreads = 1024;
+constexpr int kSelThreads = 256; /* small enough to share an SM with the parent GEMV */
 
 /* exclusive prefix sum of v over the block's threads in thread order; the block's
  * total goes to *total (every thread calls it) */
@@ -425,19 +438,21 @@ __device__ __forceinline__ int block_excl_scan(int v, int *wsum, int *total)
     if (lane == 31)
         wsum[warp] = s;
     __syncthreads();
+    constexpr int kWarps = kSelThreads / 32;
     if (warp == 0) {
-        int ws = wsum[lane];
+        int ws = lane < kWarps ? wsum[lane] : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int t = __shfl_up_sync(0xFFFFFFFFu, ws, o);
             if (lane >= o)
                 ws += t;
         }
-        wsum[lane] = ws; /* inclusive over warps */
+        if (lane < kWarps)
+            wsum[lane] = ws; /* inclusive over warps */
     }
     __syncthreads();
     const int before = (warp ? wsum[warp - 1] : 0) + s - v;
-    *total = wsum[31];
+    *total = wsum[kWarps - 1];
     __syncthreads();
     return before;
 }
@@ -543,9 +558,10 @@ __global__ void __launch_bounds__(kSelThreads) select_topk_kernel(const uint16_t
 
 /* ---- plug correction ---------------------------------------------------------- */
 
-/* part[blockIdx.y][r] = sum over list entries [(blockIdx.y*8 + warp)*8, +8) of this
- * CTA's warps (in order) of (delta[h][p] * scale) * x[c].  Two load rounds per warp:
- * the chunk's channel numbers, then every entry's hole word, plug word and scales. */
+/* part[sl][r] = sum over list entries [(sl*8 + warp)*8, +8) of this
+ * CTA's warps (in order) of (delta[h][p] * scale) * x[c], for every slice this CTA
+ * walks.  Two load rounds per warp: the chunk's channel numbers, then every entry's
+ * hole word, plug word and scales. */
 __global__ void __launch_bounds__(kCorrThreads) apply_corr_kernel(const uint32_t *__restrict__ hole_k,
                                                                   const uint32_t *plug_k,
                                                                   const float *__restrict__ sk,
@@ -554,73 +570,71 @@ __global__ void __launch_bounds__(kCorrThreads) apply_corr_kernel(const uint32_t
                                                                   const int *__restrict__ cnt_p,
                                                                   float *__restrict__ part, int n)
 {
-    __shared__ __align__(16) float delta[256 * 32]; /* entry code = h*16 + p, lane l at code*128 + l*4 */
+    __shared__ float dl[256]; /* CELLS - PARENT by code h*16 + p */
     __shared__ __align__(16) float red[8 * 256];
     const int cnt = *cnt_p;
-    const int first = (int)blockIdx.y * 8 * kCorrChunk;
-    if (first >= cnt)
-        return; /* a slice past the list: the combine does not read it */
+    if ((int)blockIdx.y * 8 * kCorrChunk >= cnt)
+        return; /* no slice of the list for this CTA: the combine reads none */
     const int lane = (int)(threadIdx.x & 31), warp = (int)(threadIdx.x >> 5);
     const int nw = n / 8;
     const int wi = (int)blockIdx.x * 32 + lane;
-    const int i0 = first + warp * kCorrChunk;
-    const int m = max(0, min(kCorrChunk, cnt - i0)); /* this warp's entries */
-    const bool live = wi < nw && m > 0;
-    int c[kCorrChunk];
-    uint32_t wh[kCorrChunk], wp[kCorrChunk];
-    float4 s0[kCorrChunk], s1[kCorrChunk];
-    float xv[kCorrChunk];
-    if (live) {
+    for (int e = threadIdx.x; e < 256; e += kCorrThreads)
+        dl[e] = g_cells[e >> 4][e & 15] - g_parent[e >> 4];
+    /* slices blockIdx.y, blockIdx.y + gridDim.y, ... of 64 list entries while the list lasts */
+    for (int sl = (int)blockIdx.y; sl * 8 * kCorrChunk < cnt; sl += (int)gridDim.y) {
+        const int i0 = sl * 8 * kCorrChunk + warp * kCorrChunk;
+        const int m = max(0, min(kCorrChunk, cnt - i0)); /* this warp's entries */
+        const bool live = wi < nw && m > 0;
+        int c[kCorrChunk];
+        uint32_t wh[kCorrChunk], wp[kCorrChunk];
+        float4 s0[kCorrChunk], s1[kCorrChunk];
+        float xv[kCorrChunk];
+        if (live) {
 #pragma unroll
-        for (int u = 0; u < kCorrChunk; ++u)
-            c[u] = u < m ? idx[i0 + u] : 0;
+            for (int u = 0; u < kCorrChunk; ++u)
+                c[u] = u < m ? idx[i0 + u] : 0;
 #pragma unroll
-        for (int u = 0; u < kCorrChunk; ++u) {
-            if (u < m) {
-                wh[u] = hole_k[(int64_t)c[u] * nw + wi];
-                wp[u] = plug_k[(int64_t)c[u] * nw + wi];
-                const float *sp = sk + (int64_t)(c[u] >> 6) * n + 8 * wi;
-                s0[u] = __ldg(reinterpret_cast<const float4 *>(sp));
-                s1[u] = __ldg(reinterpret_cast<const float4 *>(sp + 4));
-                xv[u] = __bfloat162float(x[c[u]]);
-            }
-        }
-    }
-    for (int i = threadIdx.x; i < 256 * 32; i += kCorrThreads) {
-        const int e = i >> 5;
-        delta[i] = g_cells[e >> 4][e & 15] - g_parent[e >> 4];
-    }
-    __syncthreads();
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        acc[j] = 0.f;
-    if (live) {
-        const uint32_t db = smem_u32(delta) + (uint32_t)lane * 4u;
-#pragma unroll
-        for (int u = 0; u < kCorrChunk; ++u) {
-            if (u < m) {
-                const float sv[8] = {s0[u].x, s0[u].y, s0[u].z, s0[u].w, s1[u].x, s1[u].y, s1[u].z, s1[u].w};
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t code = (((wh[u] >> (4 * j)) & 15u) << 4) | ((wp[u] >> (4 * j)) & 15u);
-                    const float d = __uint_as_float(lds32(db + (code << 7)));
-                    acc[j] = fmaf(d * sv[j], xv[u], acc[j]);
+            for (int u = 0; u < kCorrChunk; ++u) {
+                if (u < m) {
+                    wh[u] = hole_k[(int64_t)c[u] * nw + wi];
+                    wp[u] = plug_k[(int64_t)c[u] * nw + wi];
+                    const float *sp = sk + (int64_t)(c[u] >> 6) * n + 8 * wi;
+                    s0[u] = __ldg(reinterpret_cast<const float4 *>(sp));
+                    s1[u] = __ldg(reinterpret_cast<const float4 *>(sp + 4));
+                    xv[u] = __bfloat162float(x[c[u]]);
                 }
             }
         }
-    }
-    float4 *rw = reinterpret_cast<float4 *>(red + warp * 256 + lane * 8);
-    rw[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    rw[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    __syncthreads();
-    const int row = (int)blockIdx.x * 256 + (int)threadIdx.x;
-    if (row < n) {
-        float v = red[threadIdx.x];
+        __syncthreads(); /* dl filled; red free from the previous slice */
+        float acc[8];
 #pragma unroll
-        for (int u = 1; u < 8; ++u)
-            v += red[u * 256 + threadIdx.x];
-        part[(int64_t)blockIdx.y * n + row] = v;
+        for (int j = 0; j < 8; ++j)
+            acc[j] = 0.f;
+        if (live) {
+#pragma unroll
+            for (int u = 0; u < kCorrChunk; ++u) {
+                if (u < m) {
+                    const float sv[8] = {s0[u].x, s0[u].y, s0[u].z, s0[u].w, s1[u].x, s1[u].y, s1[u].z, s1[u].w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t code = (((wh[u] >> (4 * j)) & 15u) << 4) | ((wp[u] >> (4 * j)) & 15u);
+                        acc[j] = fmaf(dl[code] * sv[j], xv[u], acc[j]);
+                    }
+                }
+            }
+        }
+        float4 *rw = reinterpret_cast<float4 *>(red + warp * 256 + lane * 8);
+        rw[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        rw[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        __syncthreads();
+        const int row = (int)blockIdx.x * 256 + (int)threadIdx.x;
+        if (row < n) {
+            float v = red[threadIdx.x];
+#pragma unroll
+            for (int u = 1; u < 8; ++u)
+                v += red[u * 256 + threadIdx.x];
+            part[(int64_t)sl * n + row] = v;
+        }
     }
 }
 
@@ -703,6 +717,36 @@ struct KmScratch {
 };
 std::mutex g_km_mu;
 std::unordered_map<uint64_t, KmScratch> g_km_scratch;
+
+/* A side stream and two events per (device, stream): the channel selection runs
+ * beside the parent GEMV (it needs only x), joined before the correction.  Event
+ * records and waits are captured into CUDA graphs as a parallel branch. */
+struct KmFork {
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::unordered_map<uint64_t, KmFork> g_km_fork;
+
+bool km_fork(cudaStream_t st, KmFork *out)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return false;
+    const uint64_t key = (reinterpret_cast<uint64_t>(st) << 8) ^ (uint64_t)dev;
+    std::lock_guard<std::mutex> lk(g_km_mu);
+    KmFork &f = g_km_fork[key];
+    if (!f.side) {
+        if (cudaStreamCreateWithFlags(&f.side, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&f.join, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            f = KmFork{};
+            return false;
+        }
+    }
+    *out = f;
+    return true;
+}
 
 float *km_scratch(cudaStream_t st, size_t floats)
 {
@@ -874,7 +918,10 @@ namespace {
 int corr_parts(const uint8_t *hole_k, const uint8_t *plug_k, const float *sk, const __nv_bfloat16 *x,
                const int *idx, const int *cnt, int n, int K, float *cpart, cudaStream_t st)
 {
-    apply_corr_kernel<<<dim3((n + 255) / 256, corr_slices(K)), kCorrThreads, 0, st>>>(
+    /* a small fixed grid whose CTAs walk the list's slices (the count is on the device) */
+    const int rg = (n + 255) / 256;
+    const int ys = std::min(corr_slices(K), std::max(1, 2 * sm_count() / rg));
+    apply_corr_kernel<<<dim3(rg, ys), kCorrThreads, 0, st>>>(
         reinterpret_cast<const uint32_t *>(hole_k), reinterpret_cast<const uint32_t *>(plug_k), sk, x, idx, cnt,
         cpart, n);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
@@ -896,21 +943,30 @@ int km_corr_launch(const uint8_t *hole_k, const uint8_t *plug_k, const float *sk
 int km_gemv_select_launch(const uint8_t *hole_k, const uint8_t *plug_k, const float *sk, const __nv_bfloat16 *x,
                           float *y, int n, int K, int nsel, int *idx, int *cnt, cudaStream_t st)
 {
-    int rc = km_select_launch(x, K, nsel, idx, cnt, st);
-    if (rc != kOk)
-        return rc;
     KmStream a;
     if (km_stream_split(n, K, x, &a)) {
         const size_t pf = km_stream_part_floats(a);
         float *part = km_scratch(st, pf + (size_t)corr_slices(K) * n);
-        if (!part)
+        KmFork f;
+        if (!part || !km_fork(st, &f))
             return kLaunch;
+        /* selection on the side stream, beside the parent GEMV */
+        if (cudaEventRecord(f.fork, st) != cudaSuccess || cudaStreamWaitEvent(f.side, f.fork, 0) != cudaSuccess)
+            return kLaunch;
+        int rc = km_select_launch(x, K, nsel, idx, cnt, f.side);
+        if (rc != kOk || cudaEventRecord(f.join, f.side) != cudaSuccess)
+            return rc != kOk ? rc : kLaunch;
         if ((rc = km_stream_launch(hole_k, sk, x, a, part, st)) != kOk)
             return rc;
+        if (cudaStreamWaitEvent(st, f.join, 0) != cudaSuccess)
+            return kLaunch;
         if ((rc = corr_parts(hole_k, plug_k, sk, x, idx, cnt, n, K, part + pf, st)) != kOk)
             return rc;
         return combine(part, 2, 0, &a, part + pf, cnt, y, n, st);
     }
+    int rc = km_select_launch(x, K, nsel, idx, cnt, st);
+    if (rc != kOk)
+        return rc;
     int s = 1, bps = 1;
     km_split(n, K, &s, &bps);
     /* scratch: [s][n] GEMV slices (when s > 1), then the correction slices */
