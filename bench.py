@@ -364,6 +364,8 @@ def bench_glint(args):
     # ---- the 80-layer Llama-3-70B decode linear stack, column-parallel over the ranks
     result["decode_stack"] = bench_decode_stack(args, world, rank, pk, checks)
     if world == 1:
+        # ---- K-major decode: parent-only GEMV + activation-selected plug correction
+        result["kmajor"] = bench_kmajor(pk, checks)
         # ---- plugs in host memory, streamed through the two-slot ring (one GPU's PCIe link)
         result["plug_stream"] = bench_plug_stream(pk)
         # ---- the pin pipeline: safetensors on disk -> GLINT pin files (file IO, PCIe, encode, rmse)
@@ -373,7 +375,7 @@ def bench_glint(args):
             result["pin_pipeline"] = {"error": f"{type(e).__name__}: {e}"}
         del ws_pin
     checks["ok"] = bool(checks["encode_expand_bits"] and checks.get("htile_max_rel_err", 1.0) <= 1e-2
-                        and checks.get("decode_stack_ok", True))
+                        and checks.get("decode_stack_ok", True) and checks.get("kmajor_max_rel_err", 0.0) <= 3e-5)
     result["checks"] = checks
     barrier(world)
     if world > 1:
@@ -685,6 +687,62 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
     checks["decode_stack_ok"] = kerr == 0
     del stack
     torch.cuda.empty_cache()
+    return out
+
+
+def bench_kmajor(pk, checks, shapes=((14336, 4096), (4096, 14336)), pcts=(1, 10, 25)):
+    """The K-major decode (include/glint_km.h) at configs[2]'s decode shapes, M = 1:
+    the parent-only GEMV (roofline: N*K/2 hole + N*K/16 scales + 2K + 4N bytes), and
+    the decode step (channel selection beside the parent GEMV, plug correction,
+    closing sums) at a few selected fractions, with the plug rows in device memory
+    and, at 10 %, read in place from pinned host memory.  Device time of back-to-back
+    launches in a CUDA graph over 4 rotating copies (> L2).  The 10 % step's output
+    is checked against the oracle's f32 restatement of the reference's sequential
+    order (3e-5 normwise: each of the two sums is within 1e-5 of an f64 one)."""
+    import torch
+    from glint_b200 import device as D
+    out = {}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(77)
+    for si, (N, K) in enumerate(shapes):
+        w = synth_tensor(N * K, 4242 + si)
+        h, p, a = D.encode(w, BS)
+        del w
+        base = D.to_kmajor(h, p, a, N, K)
+        copies = [base] + [tuple(t.clone() for t in base) for _ in range(3)]
+        x = torch.randn(K, generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty(N, dtype=torch.float32, device="cuda")
+        idx = torch.empty(K, dtype=torch.int32, device="cuda")
+        cnt = torch.empty(1, dtype=torch.int32, device="cuda")
+        t = graph_time_us(lambda i: D.gemv_km(x, copies[i % 4][0], copies[i % 4][2], N, out=y), 16)
+        byt = N * K / 2 + N * K / 16 + 2 * K + 4 * N
+        r = {"gemv_parent_us": round(t, 2), "frac": round(byt / (t * 1e-6) / 1e9 / pk["hbm_gbs"], 4)}
+        for pct in pcts:
+            nsel = (pct * K + 99) // 100
+            r[f"step_{pct}pct_us"] = round(graph_time_us(
+                lambda i: D.gemv_select(x, copies[i % 4][0], copies[i % 4][1], copies[i % 4][2], N, nsel, out=y,
+                                        idx=idx, cnt=cnt), 16), 2)
+        plug_host = torch.empty(K * N // 2, dtype=torch.uint8).pin_memory()
+        plug_host.copy_(base[1].cpu())
+        nsel = (10 * K + 99) // 100
+        r["step_10pct_host_plugs_us"] = round(graph_time_us(
+            lambda i: D.gemv_select(x, copies[i % 4][0], plug_host, copies[i % 4][2], N, nsel, out=y, idx=idx,
+                                    cnt=cnt), 16), 2)
+        if si == 0:
+            D.gemv_select(x, base[0], base[1], base[2], N, nsel, out=y, idx=idx, cnt=cnt)
+            hk, pkk, sk = (t_.cpu().numpy() for t_ in base)
+            xb = x.view(torch.int16).cpu().numpy().view("uint16")
+            O = _oracle()
+            sel = O.select_topk(xb, nsel)
+            want = O.apply_corr_k(O.gemv_km(hk, sk, xb, N, K), hk, pkk, sk, xb, sel, N, K).astype("float64")
+            got = y.cpu().numpy().astype("float64")
+            err = float(abs(got - want).max() / max(1.0, float(abs(want).max())))
+            checks["kmajor_max_rel_err"] = round(err, 9)
+            checks["kmajor_selected"] = [int(cnt.item()), len(sel)]
+        out[f"n{N}_k{K}"] = r
+        del copies, base, h, p, a, plug_host
+    torch.cuda.empty_cache()
+    out["timing"] = "CUDA graph of back-to-back steps over 4 rotating copies; median of 5 replays"
     return out
 
 
@@ -1039,6 +1097,18 @@ def profile_case(case: str, iters: int = 5):
         y = torch.empty((M, 14336), dtype=torch.float32, device="cuda")
         n = 14336 * 4096
         fn = lambda: D.htile(x, *planes[0], 14336, BS, mode="fast", out=y)  # noqa: E731
+    elif case in ("km", "kmstep"):
+        # K-major decode at N = 14336, K = 4096: the parent-only GEMV, or the whole
+        # step at 10 % of the channels selected
+        N, K = 14336, 4096
+        hk, pk_, sk = D.to_kmajor(*planes[0], N, K)
+        x = torch.randn(K, generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty(N, dtype=torch.float32, device="cuda")
+        n = N * K
+        if case == "km":
+            fn = lambda: D.gemv_km(x, hk, sk, N, out=y)  # noqa: E731
+        else:
+            fn = lambda: D.gemv_select(x, hk, pk_, sk, N, K // 10, out=y)  # noqa: E731
     else:
         raise SystemExit(f"unknown case {case}")
     for _ in range(2):
@@ -1061,7 +1131,7 @@ def main():
     ap.add_argument("--impl", default="glint_b200", choices=["glint_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default=None,
-                    help="run one small kernel case (encode|expand|gemv<M>|gemvt<M>|gemm<M>|gemmp<M>) for ncu")
+                    help="run one small kernel case (encode|expand|gemv<M>|gemvt<M>|gemm<M>|gemmp<M>|km|kmstep) for ncu")
     args = ap.parse_args()
     if args.profile:
         profile_case(args.profile)

@@ -21,9 +21,10 @@
  *                         mojo/p7_glint_select_decode.mojo:120-143,
  *                         mojo/p7_glint_gemv_km.mojo:17-95,
  *                         mojo/p7_select_device.mojo:15-153, 197-238
- *                         (no Mojo toolchain here: these are pinned through the
- *                         identity parent + full correction == H-TILE, and the
- *                         selection rule against a sort-based definition)
+ *                         (no Mojo toolchain here and no reference vectors: the sum
+ *                         parent + full correction is pinned to the H-TILE goldens;
+ *                         the parent-only values and the selection rule are parity
+ *                         unpinned against the reference's own outputs)
  * Parity is pinned against golden vectors that tests/golden/make_golden.py wrote
  * by running the reference's own glint_np.py / glint_htile_sim.py.
  *
