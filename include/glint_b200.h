@@ -12,9 +12,10 @@ extern "C" {
 const char *p7_abi_version(void);
 /* "glint_b200 <version> sm_100a" */
 const char *glint_b200_version(void);
-/* Error word of the current device, set by a kernel whose bounded wait on a
- * pipeline barrier ran out (1 = timeout); 0 when none.  Synchronous.  clear != 0
- * resets it. */
+/* Error word of the current device, ORed by kernels that stopped instead of
+ * hanging or faulting: 1 = a bounded wait on a pipeline barrier or a peer's signal
+ * ran out; 2 = a kernel found its shared-memory ring misaligned for a tensor copy
+ * and issued none.  0 when none.  Synchronous.  clear != 0 resets it. */
 int glint_kernel_error(int clear);
 #ifdef __cplusplus
 }
