@@ -589,8 +589,9 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
     is not on the path); gate|up, silu(gate) * up, down_proj, whose output is the next
     layer's hidden state.  At world > 1 the outputs a consumer needs whole (o,
     gate|up, down) are gathered inside their decode kernels (tp.PeerGather: peer
-    stores over NVLink), and the attention output that feeds o_proj with one NCCL
-    all-gather.  The whole 80-layer step is one CUDA graph, replayed; device time
+    stores over NVLink), and each rank's heads of the attention output that feeds
+    o_proj with the same peer-store protocol (PeerGather.gather), no NCCL call on the
+    path.  The whole 80-layer step is one CUDA graph, replayed; device time
     with CUDA events, max over ranks."""
     import torch
     import torch.nn.functional as F
@@ -627,8 +628,8 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
         attn = torch.randn((M, hid), generator=gx, device="cuda").to(torch.bfloat16)
         pg = None
         if world > 1:
-            pg = tp.PeerGather({"o": (M, hid, torch.float32), "gu": (M, 2 * inter, torch.float32),
-                                "down": (M, hid, torch.float32)}, world, rank)
+            pg = tp.PeerGather({"attn": (M, hid, torch.bfloat16), "o": (M, hid, torch.float32),
+                                "gu": (M, 2 * inter, torch.float32), "down": (M, hid, torch.float32)}, world, rank)
         hidden = torch.empty((M, hid), dtype=torch.bfloat16, device="cuda")
 
         def step():
@@ -642,8 +643,8 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
                     d = tp.column_parallel(act, lay["down"], 1, 0)
                 else:
                     sh_o = lay["o"]
-                    o_in = tp.gather_columns(attn[:, sh_o.n0:sh_o.n1].float(), hid, world, rank)
-                    pg.linear(o_in.to(torch.bfloat16), sh_o, "o")
+                    o_in = pg.gather(attn[:, sh_o.n0:sh_o.n1], "attn", sh_o.n0)  # this rank's heads
+                    pg.linear(o_in, sh_o, "o")
                     gu = pg.linear(hidden, lay["gu"], "gu")
                     act = (F.silu(gu[:, :inter]) * gu[:, inter:]).to(torch.bfloat16)
                     d = pg.linear(act, lay["down"], "down")

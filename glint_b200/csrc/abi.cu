@@ -705,6 +705,20 @@ int glint_htile_gather_stream(const uint8_t *d_hole, const uint8_t *d_plug, cons
     return kUnsupported;
 }
 
+int glint_gather_stream(const void *d_src, int elem_bytes, int M, int cols, int ld_src, void *const *d_y_ranks,
+                        unsigned int *const *d_flag_ranks, int world, int rank, int ld_y, int n0,
+                        cudaStream_t stream)
+{
+    if (!d_src || !d_y_ranks || !d_flag_ranks || world < 1 || rank < 0 || rank >= world || M < 1 || cols < 1 ||
+        ld_src < cols || n0 < 0 || ld_y < n0 + cols)
+        return kBadArg;
+    for (int r = 0; r < world; ++r)
+        if (!d_y_ranks[r] || !d_flag_ranks[r])
+            return kBadArg;
+    return gather_copy_launch(d_src, elem_bytes, M, cols, ld_src, d_y_ranks, d_flag_ranks, world, rank, ld_y, n0,
+                              stream);
+}
+
 int glint_device_alloc(size_t bytes, void **d_ptr)
 {
     if (!d_ptr || bytes == 0)

@@ -118,6 +118,11 @@ int km_gemv_select_launch(const uint8_t *hole_k, const uint8_t *plug_k, const fl
  * driver does not offer it); looked up once. */
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
+/* A [M, cols] column shard stored into every rank's y [M, ldy] at column n0 over
+ * peer memory, with the gathered decode's completion protocol. */
+int gather_copy_launch(const void *src, int elem_bytes, int M, int cols, int ld_src, void *const *y_ranks,
+                       uint32_t *const *flag_ranks, int world, int rank, int ldy, int n0, cudaStream_t stream);
+
 /* SM count of the current device (cached per device). */
 int sm_count();
 /* Raise a kernel's dynamic shared memory limit once per device. */

@@ -1371,6 +1371,46 @@ int htile_decode_gather_launch(const uint8_t *hole, const uint8_t *plug, const f
     return decode_launch_impl(hole, plug, am, x, y_ranks[rank], yk, M, N, K, mode, st, &g);
 }
 
+namespace {
+/* A column shard gathered into every rank's buffer: src [M, cols] (row stride
+ * ld_src elements, elem_bytes 2 or 4) goes to columns [n0, n0 + cols) of every
+ * rank's y [M, ldy], then the CTA counts in (gather_complete).  One warp per 32
+ * consecutive elements of a row; 8 warps per CTA. */
+__global__ void __launch_bounds__(256) gather_copy_kernel(const GatherArgs g, const uint8_t *__restrict__ src,
+                                                          int elem_bytes, int M, int cols, int ld_src)
+{
+    __shared__ uint32_t cta_done;
+    if (threadIdx.x == 0)
+        cta_done = 0;
+    __syncthreads();
+    const int64_t total = (int64_t)M * cols;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int m = (int)(e / cols), c = (int)(e - (int64_t)m * cols);
+        const int64_t si = (int64_t)m * ld_src + c, di = (int64_t)m * g.ldy + g.n0 + c;
+        for (int i = 1; i <= g.world; ++i) {
+            const int r = (g.rank + i) % g.world;
+            if (elem_bytes == 2)
+                reinterpret_cast<uint16_t *>(g.yr[r])[di] = reinterpret_cast<const uint16_t *>(src)[si];
+            else
+                reinterpret_cast<uint32_t *>(g.yr[r])[di] = reinterpret_cast<const uint32_t *>(src)[si];
+        }
+    }
+    gather_complete(g, (int)(blockDim.x >> 5), threadIdx.x & 31u, &cta_done, &g_decode_error);
+}
+} // namespace
+
+int gather_copy_launch(const void *src, int elem_bytes, int M, int cols, int ld_src, void *const *y_ranks,
+                       uint32_t *const *flag_ranks, int world, int rank, int ldy, int n0, cudaStream_t st)
+{
+    GatherArgs g;
+    if ((elem_bytes != 2 && elem_bytes != 4) || !make_gather_args(&g, y_ranks, flag_ranks, world, rank, ldy, n0))
+        return kUnsupported;
+    const int64_t total = (int64_t)M * cols;
+    const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 2 * sm_count()));
+    gather_copy_kernel<<<ctas, 256, 0, st>>>(g, static_cast<const uint8_t *>(src), elem_bytes, M, cols, ld_src);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+}
+
 int htile_decode_launch_noalloc(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
                                 void *y, OutKind yk, int M, int N, int K, HtileMode mode, cudaStream_t st)
 {

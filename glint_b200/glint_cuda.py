@@ -74,6 +74,9 @@ def _bind(lib):
     lib.glint_htile_gather_stream.argtypes = [vp, vp, vp, vp, ctypes.POINTER(vp), ctypes.POINTER(vp), i32, i32, i32,
                                               i32, i32, i32, i32, i32, i32, i32, vp]
     lib.glint_htile_gather_stream.restype = i32
+    lib.glint_gather_stream.argtypes = [vp, i32, i32, i32, i32, ctypes.POINTER(vp), ctypes.POINTER(vp), i32, i32,
+                                        i32, i32, vp]
+    lib.glint_gather_stream.restype = i32
     lib.glint_device_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
     lib.glint_device_alloc.restype = i32
     lib.glint_device_free.argtypes = [vp]

@@ -197,6 +197,27 @@ class PeerGather:
         self._calls[name] += 1
         return self.y[name][buf]
 
+    def gather(self, shard: torch.Tensor, name: str, n0: int, stream=None) -> torch.Tensor:
+        """Columns [n0, n0 + cols) of the named output from this rank's shard
+        [M, cols] (any row stride; the output's dtype, BF16 or f32), stored into every
+        rank's buffer over NVLink (glint_gather_stream).  Returns one of the name's two
+        shared local buffers, whole once the call completes on the stream; the same
+        rules as linear() (every rank gathers, in the same order)."""
+        M, N, dt = self.shapes[name]
+        if shard.dtype != dt or shard.dim() != 2 or shard.shape[0] != M or not shard.is_cuda:
+            raise ValueError("shard must be a CUDA [M, cols] tensor of the output's dtype")
+        if shard.stride(1) != 1 or n0 < 0 or n0 + shard.shape[1] > N:
+            raise ValueError("shard rows must be contiguous and fit the output's columns")
+        buf = self._calls[name] & 1
+        s = stream if stream is not None else torch.cuda.current_stream()
+        rc = self._lib.glint_gather_stream(shard.data_ptr(), shard.element_size(), M, shard.shape[1],
+                                           shard.stride(0), self._yptrs[name][buf], self._flags, self.world,
+                                           self.rank, N, n0, ctypes.c_void_p(s.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(f"glint_gather_stream rc={rc}")
+        self._calls[name] += 1
+        return self.y[name][buf]
+
     def close(self, group=None) -> None:
         """Unmap the peers' buffers and free this rank's (after every rank is done with them)."""
         import torch.distributed as dist

@@ -107,6 +107,15 @@ int glint_htile_gather_stream(
     const glint_bf16_t *d_x, void *const *d_y_ranks, unsigned int *const *d_flag_ranks,
     int world, int rank, int y_dtype, int M, int N, int K, int ld_y, int n0,
     int blocksize, int mode, cudaStream_t stream);
+/* A column shard gathered into every rank's buffer, on the same counters and with the
+ * same rules as glint_htile_gather_stream: src [M, cols] (row stride ld_src elements,
+ * elem_bytes 2 or 4) is stored into columns [n0, n0 + cols) of every rank's
+ * y [M, ld_y]; when the call completes on `stream`, this rank's y holds every rank's
+ * columns.  For activations that feed a column-parallel linear (e.g. the heads of an
+ * attention output).  -6 for another element size. */
+int glint_gather_stream(const void *d_src, int elem_bytes, int M, int cols, int ld_src, void *const *d_y_ranks,
+                        unsigned int *const *d_flag_ranks, int world, int rank, int ld_y, int n0,
+                        cudaStream_t stream);
 /* Zero-initialised device memory that can be shared with other processes
  * (cudaMalloc'd, so glint_ipc_handle covers exactly this range). */
 int glint_device_alloc(size_t bytes, void **d_ptr);

@@ -226,6 +226,19 @@ def _prefill_gather_worker(rank, world, port):
             assert all(torch.equal(sums[0], t) for t in sums), (N, M)
         pg.close()
         del hole, plug, am, sh
+    # a column shard gathered on its own (glint_gather_stream): BF16 from a strided view
+    # and f32, repeated, every rank ends with the whole [M, N]
+    from glint_b200 import shard as SH
+    for dt, M, N in [(torch.bfloat16, 4, 8192), (torch.float32, 32, 1024)]:
+        full = torch.randn((M, N), generator=g, device="cuda").to(dt)  # the same on every rank
+        n0, n1 = SH.column_shard(N, world, rank)
+        pg = tp.PeerGather({"a": (M, N, dt)}, world, rank)
+        for _ in range(3):
+            got = pg.gather(full[:, n0:n1], "a", n0)
+            torch.cuda.synchronize()
+            assert torch.equal(got, full), (dt, M, N)
+            full = full * 2
+        pg.close()
     assert L.glint_kernel_error(1) == 0
     # a rank that skips a gathered prefill call: the other's GEMM gives up after
     # about a second with the error word set, instead of hanging
