@@ -17,6 +17,9 @@
  *   - H-TILE reference    cuda/glint_htile.cu:124-164 (weights dequantised in
  *                         f32, products accumulated in f64 as in
  *                         tests/test_htile_k_bounds_device.cu:90-95)
+ *   - INT8 W8A8 GEMM, res4 plug cuda/int8_mma_gemm.cu:10-240 (activation quantization,
+ *                         per-block int32 dots, f32 scaling order); checked on the GPU
+ *                         against that file built unchanged for sm_100a (oracle/_ref)
  *   - K-major layout, parent-only GEMV, channel selection, plug correction
  *                         mojo/p7_glint_select_decode.mojo:120-143,
  *                         mojo/p7_glint_gemv_km.mojo:17-95,
@@ -363,6 +366,74 @@ int orc_apply_corr_k(const uint8_t *hole_k, const uint8_t *plug_k, const float *
             acc += (d * scales_k[(c / 64) * n + r]) * bf16_to_f32(x[c]);
         }
         y[r] = y[r] + acc;
+    }
+    return 0;
+}
+
+/* ---- INT8 W8A8 GEMM and the res4 late plug (cuda/int8_mma_gemm.cu) ------------ */
+
+/* k_quant_act (cuda/int8_mma_gemm.cu:10-29); with xq_prev, k_quant_act_resid
+ * (:170-189), whose x - xq * sx the reference's compiler fuses into one step.  Per
+ * (row, 64-block): s = amax / 127 (1 when amax == 0), q = rint(w / s) clamped to
+ * +-127. */
+int orc_int8_quant(const uint16_t *x, const int8_t *xq_prev, const float *sx_prev, int m, int k, int8_t *q,
+                   float *s)
+{
+    if (m < 1 || k < 64 || k % 64)
+        return -1;
+    const int nkb = k / 64;
+#pragma omp parallel for num_threads(g_threads) schedule(static)
+    for (int item = 0; item < m * nkb; ++item) {
+        const int row = item / nkb, kb = item % nkb;
+        float w[64], am = 0.f;
+        for (int j = 0; j < 64; ++j) {
+            const int64_t i = (int64_t)row * k + kb * 64 + j;
+            w[j] = bf16_to_f32(x[i]);
+            if (xq_prev)
+                w[j] = fmaf(-(float)xq_prev[i], sx_prev[item], w[j]);
+            am = fmaxf(am, fabsf(w[j]));
+        }
+        const float sc = am > 0.f ? am / 127.f : 1.f;
+        s[item] = sc;
+        for (int j = 0; j < 64; ++j) {
+            int v = (int)rintf(w[j] / sc);
+            v = v > 127 ? 127 : (v < -127 ? -127 : v);
+            q[(int64_t)row * k + kb * 64 + j] = (int8_t)v;
+        }
+    }
+    return 0;
+}
+
+/* k_int8_mma_gemm (cuda/int8_mma_gemm.cu:40-156): per 64-block the exact int32 dot,
+ * then acc = fma((float)dot * sx, sw, acc) (the reference's `acc += (dot * x0) * w0`
+ * as its compiler emits it), the fused plug's term (nibble - 8, element 2i in the low
+ * nibble) right after the base's; y = (accumulate ? y : 0) + acc. */
+int orc_int8_gemm(const int8_t *xq, const float *sx, const int8_t *wq, const float *sw, float *y, int m, int n, int k,
+                  int accumulate, const uint8_t *pq4, const float *psc)
+{
+    if (m < 1 || n < 1 || k < 64 || k % 64)
+        return -1;
+    const int nkb = k / 64;
+#pragma omp parallel for num_threads(g_threads) schedule(static) collapse(2)
+    for (int r = 0; r < m; ++r) {
+        for (int c = 0; c < n; ++c) {
+            float acc = 0.f;
+            for (int kb = 0; kb < nkb; ++kb) {
+                int ic = 0, ip = 0;
+                for (int j = 0; j < 64; ++j) {
+                    const int64_t kk = (int64_t)kb * 64 + j, wi = (int64_t)c * k + kk;
+                    ic += (int)xq[(int64_t)r * k + kk] * (int)wq[wi];
+                    if (pq4)
+                        ip += (int)xq[(int64_t)r * k + kk] * ((int)((pq4[wi >> 1] >> ((wi & 1) * 4)) & 15) - 8);
+                }
+                const float xs = sx[(int64_t)r * nkb + kb];
+                acc = fmaf((float)ic * xs, sw[(int64_t)c * nkb + kb], acc);
+                if (pq4)
+                    acc = fmaf((float)ip * xs, psc[(int64_t)c * nkb + kb], acc);
+            }
+            float *yy = y + (int64_t)r * n + c;
+            *yy = (accumulate ? *yy : 0.f) + acc;
+        }
     }
     return 0;
 }

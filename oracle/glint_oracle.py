@@ -69,6 +69,10 @@ def lib():
     L.orc_apply_corr_k.argtypes = [vp, vp, vp, vp, vp, i32, vp, i32, i32]
     for f in (L.orc_to_kmajor, L.orc_gemv_km, L.orc_select_topk, L.orc_apply_corr_k):
         f.restype = i32
+    L.orc_int8_quant.argtypes = [vp, vp, vp, i32, i32, vp, vp]
+    L.orc_int8_gemm.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp]
+    for f in (L.orc_int8_quant, L.orc_int8_gemm):
+        f.restype = i32
     _LIB = L
     return L
 
@@ -191,6 +195,34 @@ def apply_corr_k(y: np.ndarray, hole_k, plug_k, scales_k, x_bf16: np.ndarray, id
     if lib().orc_apply_corr_k(_ptr(hk), _ptr(pk), _ptr(sk), _ptr(x), _ptr(ix) if ix.size else None, ix.size,
                               _ptr(out), n, K):
         raise ValueError("apply_corr_k: bad arguments")
+    return out
+
+
+def int8_quant(x_bf16: np.ndarray, m: int, k: int, prev=None):
+    """(q int8 [m*k], s f32 [m*k/64]) of the activation rule; prev = (q, s) of the
+    first pass quantizes its residual (the resolve pass)."""
+    x = np.ascontiguousarray(x_bf16, np.uint16).reshape(-1)
+    q = np.empty(m * k, np.int8)
+    s = np.empty(m * (k // 64), np.float32)
+    pq, ps = (None, None) if prev is None else (np.ascontiguousarray(prev[0], np.int8),
+                                                np.ascontiguousarray(prev[1], np.float32))
+    if lib().orc_int8_quant(_ptr(x), _ptr(pq) if pq is not None else None, _ptr(ps) if ps is not None else None,
+                            m, k, _ptr(q), _ptr(s)):
+        raise ValueError("int8_quant: k % 64 == 0 and k >= 64 required")
+    return q, s
+
+
+def int8_gemm(xq, sx, wq, sw, m: int, n: int, k: int, y=None, accumulate: bool = False, plug=None) -> np.ndarray:
+    """y [m, n] f32 of the INT8 GEMM (plug = (q4 bytes, scales) for the fused late plug)."""
+    out = np.zeros((m, n), np.float32) if y is None else np.array(y, np.float32, copy=True)
+    args = [np.ascontiguousarray(xq, np.int8), np.ascontiguousarray(sx, np.float32),
+            np.ascontiguousarray(wq, np.int8), np.ascontiguousarray(sw, np.float32)]
+    pq = ps = None
+    if plug is not None:
+        pq, ps = np.ascontiguousarray(plug[0], np.uint8), np.ascontiguousarray(plug[1], np.float32)
+    if lib().orc_int8_gemm(*[_ptr(a) for a in args], _ptr(out), m, n, k, int(accumulate),
+                           _ptr(pq) if pq is not None else None, _ptr(ps) if ps is not None else None):
+        raise ValueError("int8_gemm: bad shape")
     return out
 
 
