@@ -366,6 +366,8 @@ def bench_glint(args):
     if world == 1:
         # ---- K-major decode: parent-only GEMV + activation-selected plug correction
         result["kmajor"] = bench_kmajor(pk, checks)
+        # ---- INT8 W8A8 GEMM with the res4 late plug, beside the reference's own kernel
+        result["int8"] = bench_int8(pk, checks)
         # ---- plugs in host memory, streamed through the two-slot ring (one GPU's PCIe link)
         result["plug_stream"] = bench_plug_stream(pk)
         # ---- the pin pipeline: safetensors on disk -> GLINT pin files (file IO, PCIe, encode, rmse)
@@ -375,6 +377,7 @@ def bench_glint(args):
             result["pin_pipeline"] = {"error": f"{type(e).__name__}: {e}"}
         del ws_pin
     checks["ok"] = bool(checks["encode_expand_bits"] and checks.get("htile_max_rel_err", 1.0) <= 1e-2
+                        and checks.get("int8_bits_equal_reference", True)
                         and checks.get("decode_stack_ok", True) and checks.get("kmajor_max_rel_err", 0.0) <= 3e-5)
     result["checks"] = checks
     barrier(world)
@@ -744,6 +747,52 @@ def bench_kmajor(pk, checks, shapes=((14336, 4096), (4096, 14336)), pcts=(1, 10,
         del copies, base, h, p, a, plug_host
     torch.cuda.empty_cache()
     out["timing"] = "CUDA graph of back-to-back steps over 4 rotating copies; median of 5 replays"
+    return out
+
+
+def bench_int8(pk, checks, shapes=((1, 14336, 4096), (32, 14336, 4096), (2048, 14336, 4096))):
+    """The INT8 W8A8 GEMM (include/int8_mma_gemm.h) at configs[2]/[3]-shaped linears
+    (M x N x K), plain and with the fused res4 plug, each call including its activation
+    quantization; beside it the reference's cuda/int8_mma_gemm.cu built unchanged for
+    sm_100a (oracle/_ref/libp7_int8.so) on the same GPU and inputs.  Device time of
+    back-to-back calls in a CUDA graph over 2 rotating weight copies; int8 TOPS =
+    2 M N K / time.  The reference's outputs are compared bit for bit."""
+    import ctypes
+    import torch
+    from glint_b200 import int8 as I8
+    ref_so = ROOT / "oracle" / "_ref" / "libp7_int8.so"
+    ref = I8.bind(ctypes.CDLL(str(ref_so))) if ref_so.is_file() else None
+    g = torch.Generator(device="cuda")
+    g.manual_seed(91)
+    out, same = {}, True
+    for (M, N, K) in shapes:
+        x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+        ws = [(torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int8),
+               torch.rand(N * K // 64, generator=g, device="cuda") * 2e-4 + 1e-5) for _ in range(2)]
+        q4 = torch.randint(0, 256, (N * K // 2,), generator=g, device="cuda", dtype=torch.uint8)
+        ps = torch.rand(N * K // 64, generator=g, device="cuda") * 2e-5
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        sc = {}
+        r = {}
+        for kind, plug in (("gemm", None), ("fused", (q4, ps))):
+            for who, lib in (("", None), ("ref_", ref)):
+                if who and lib is None:
+                    continue
+                t = graph_time_us(lambda i: I8.gemm(x, ws[i % 2][0], ws[i % 2][1], plug=plug, kind=kind, out=y,
+                                                    scratch=sc, lib=lib), 8)
+                r[f"{who}{kind}_us"] = round(t, 2)
+                r[f"{who}{kind}_tops"] = round(2.0 * M * N * K / (t * 1e-6) / 1e12, 1)
+            if ref is not None:
+                a, _ = I8.gemm(x, ws[0][0], ws[0][1], plug=plug, kind=kind)
+                b, _ = I8.gemm(x, ws[0][0], ws[0][1], plug=plug, kind=kind, lib=ref)
+                torch.cuda.synchronize()
+                same = same and bool(torch.equal(a.view(torch.int32), b.view(torch.int32)))
+        out[f"m{M}_n{N}_k{K}"] = r
+        del ws, q4, ps, x, y, sc
+    torch.cuda.empty_cache()
+    if ref is not None:
+        checks["int8_bits_equal_reference"] = same
+    out["timing"] = "CUDA graph of back-to-back calls (quantization + GEMM) over 2 weight copies; median of 5 replays"
     return out
 
 

@@ -12,10 +12,11 @@
  * fused multiply-add per block and output), so the outputs match it bit for bit
  * whatever the tiling.
  *
- * On sm_100a: `mma.sync` m16n8k32 s8 tiles of 64 activation rows x 128 weight rows,
- * 8 warps (16 x 64 each), two-stage shared-memory ring filled with 16-byte
- * asynchronous copies (the next block's x and weight slices land while this one
- * multiplies), plug nibbles unpacked in shared memory.  No kernel here waits on
+ * On sm_100a: `mma.sync` m16n8k32 s8 tiles (64 activation rows x 128 weight rows
+ * with a two-stage ring, or for M <= 16, 16 x 64 with an eight-stage ring), 8 warps,
+ * shared-memory rings filled with 16-byte asynchronous copies (later K slices land
+ * while this one multiplies), plug nibbles unpacked in shared memory.  No split over
+ * K: each output's blocks are added in K order, as the reference adds them.  No kernel here waits on
  * another CTA, so nothing can hang.
  */
 #include <algorithm>
@@ -102,72 +103,87 @@ struct Int8Args {
     const float *psc;
 };
 
+/* one K slice of a tile: x rows, weight rows, packed plug nibbles, the slice's scales */
+template <int BM, int BN>
 struct __align__(16) Int8Stage {
-    int8_t a[kIBM][kIPad];
-    int8_t b[kIBN][kIPad];
-    uint8_t pp[kIBN][32]; /* packed plug nibbles of the slice */
-    float sx[kIBM], sw[kIBN], sp[kIBN];
+    int8_t a[BM][kIPad];
+    int8_t b[BN][kIPad];
+    uint8_t pp[BN][32];
+    float sx[BM], sw[BN], sp[BN];
 };
 
 /* the 64-wide K slice kb of this tile into stage st (x, weights, packed plug: 16-byte
- * asynchronous copies; scales: plain loads) */
-template <bool PLUG>
-__device__ __forceinline__ void load_slice(const Int8Args &a, Int8Stage &st, int m0, int n0, int kb, int nkb)
+ * asynchronous copies, zero-filled past m / n; scales: plain loads) */
+template <bool PLUG, int BM, int BN>
+__device__ __forceinline__ void load_slice(const Int8Args &a, Int8Stage<BM, BN> &st, int m0, int n0, int kb, int nkb)
 {
     const int tid = (int)threadIdx.x;
-    {
-        const int r = tid >> 2, c = (tid & 3) * 16; /* 64 rows x 4 chunks */
+    for (int idx = tid; idx < BM * 4; idx += kIThreads) {
+        const int r = idx >> 2, c = (idx & 3) * 16;
         const bool ok = m0 + r < a.m;
         cp_async16(&st.a[r][c], ok ? a.xq + (int64_t)(m0 + r) * a.k + (int64_t)kb * kIBK + c : a.xq, ok);
     }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int idx = tid + h * kIThreads, r = idx >> 2, c = (idx & 3) * 16; /* 128 rows x 4 chunks */
+    for (int idx = tid; idx < BN * 4; idx += kIThreads) {
+        const int r = idx >> 2, c = (idx & 3) * 16;
         const bool ok = n0 + r < a.n;
         cp_async16(&st.b[r][c], ok ? a.wq + (int64_t)(n0 + r) * a.k + (int64_t)kb * kIBK + c : a.wq, ok);
     }
     if (PLUG) {
-        const int r = tid >> 1, c = (tid & 1) * 16; /* 128 rows x 2 chunks of packed nibbles */
-        const bool ok = n0 + r < a.n;
-        cp_async16(&st.pp[r][c], ok ? a.pq4 + (((int64_t)(n0 + r) * a.k + (int64_t)kb * kIBK) >> 1) + c : a.pq4, ok);
+        for (int idx = tid; idx < BN * 2; idx += kIThreads) {
+            const int r = idx >> 1, c = (idx & 1) * 16;
+            const bool ok = n0 + r < a.n;
+            cp_async16(&st.pp[r][c], ok ? a.pq4 + (((int64_t)(n0 + r) * a.k + (int64_t)kb * kIBK) >> 1) + c : a.pq4,
+                       ok);
+        }
     }
-    if (tid < kIBM)
+    if (tid < BM)
         st.sx[tid] = m0 + tid < a.m ? a.sx[(int64_t)(m0 + tid) * nkb + kb] : 0.f;
-    if (tid < kIBN) {
+    if (tid < BN) {
         st.sw[tid] = n0 + tid < a.n ? a.sw[(int64_t)(n0 + tid) * nkb + kb] : 0.f;
         if (PLUG)
             st.sp[tid] = n0 + tid < a.n ? a.psc[(int64_t)(n0 + tid) * nkb + kb] : 0.f;
     }
 }
 
-template <bool PLUG>
+/* Tiles of BM activation rows x BN weight rows; the 8 warps split them into BM / 16
+ * row groups x (8 / (BM / 16)) column groups of NTW 8-column MMA tiles; STAGES K
+ * slices in flight.  Large M: 64 x 128, 2 stages; decode (M <= 16): 16 x 64, 8
+ * stages, so that there are enough CTAs and bytes in flight to stream the weights. */
+template <bool PLUG, int BM, int BN, int STAGES>
 __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
 {
+    constexpr int MW = BM / 16, NW = 8 / MW, NTW = BN / NW / 8;
+    static_assert(MW * NW == 8 && NTW >= 1, "warp layout");
+    using Stage = Int8Stage<BM, BN>;
     extern __shared__ __align__(16) uint8_t smem[];
-    Int8Stage *stages = reinterpret_cast<Int8Stage *>(smem);
-    __shared__ __align__(16) int8_t sP[PLUG ? kIBN : 1][kIPad]; /* the slice's plug, unpacked */
+    Stage *stages = reinterpret_cast<Stage *>(smem);
+    __shared__ __align__(16) int8_t sP[PLUG ? BN : 1][kIPad]; /* the slice's plug, unpacked */
     const int tid = (int)threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-    const int m0 = (int)blockIdx.y * kIBM, n0 = (int)blockIdx.x * kIBN;
-    const int rb = (warp & 3) * 16, cb = (warp >> 2) * 64; /* this warp's 16 x 64 */
+    const int m0 = (int)blockIdx.y * BM, n0 = (int)blockIdx.x * BN;
+    const int rb = (warp % MW) * 16, cb = (warp / MW) * (NTW * 8); /* this warp's 16 x 8 NTW */
     const int nkb = a.k / kIBK;
 
-    float acc[8][4];
+    float acc[NTW][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < NTW; ++i)
         acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
-    load_slice<PLUG>(a, stages[0], m0, n0, 0, nkb);
-    cp_async_commit();
-    for (int kb = 0; kb < nkb; ++kb) {
-        Int8Stage &st = stages[kb & 1];
-        if (kb + 1 < nkb)
-            load_slice<PLUG>(a, stages[(kb + 1) & 1], m0, n0, kb + 1, nkb);
+#pragma unroll
+    for (int s0 = 0; s0 < STAGES - 1; ++s0) {
+        if (s0 < nkb)
+            load_slice<PLUG, BM, BN>(a, stages[s0], m0, n0, s0, nkb);
         cp_async_commit();
-        cp_async_wait<1>(); /* this slice's copies have landed */
+    }
+    for (int kb = 0; kb < nkb; ++kb) {
+        Stage &st = stages[kb % STAGES];
+        if (kb + STAGES - 1 < nkb)
+            load_slice<PLUG, BM, BN>(a, stages[(kb + STAGES - 1) % STAGES], m0, n0, kb + STAGES - 1, nkb);
+        cp_async_commit();
+        cp_async_wait<STAGES - 1>(); /* this slice's copies have landed */
         __syncthreads();
         if (PLUG) {
             /* unpack: row r, packed byte b -> elements 2b (low nibble), 2b + 1 */
-            for (int i = tid; i < kIBN * 32; i += kIThreads) {
+            for (int i = tid; i < BN * 32; i += kIThreads) {
                 const int r = i >> 5, b = i & 31;
                 const uint32_t v = st.pp[r][b];
                 sP[r][2 * b] = (int8_t)((int)(v & 15u) - 8);
@@ -175,9 +191,9 @@ __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
             }
             __syncthreads();
         }
-        int ic[8][4], ip[8][4];
+        int ic[NTW][4], ip[NTW][4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < NTW; ++i) {
             ic[i][0] = ic[i][1] = ic[i][2] = ic[i][3] = 0;
             ip[i][0] = ip[i][1] = ip[i][2] = ip[i][3] = 0;
         }
@@ -188,7 +204,7 @@ __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
             const uint32_t a2 = *reinterpret_cast<const uint32_t *>(&st.a[rb + g][ks * 32 + 16 + t * 4]);
             const uint32_t a3 = *reinterpret_cast<const uint32_t *>(&st.a[rb + g + 8][ks * 32 + 16 + t * 4]);
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
+            for (int nt = 0; nt < NTW; ++nt) {
                 const int nr = cb + nt * 8 + g;
                 mma_s8(ic[nt], a0, a1, a2, a3, *reinterpret_cast<const uint32_t *>(&st.b[nr][ks * 32 + t * 4]),
                        *reinterpret_cast<const uint32_t *>(&st.b[nr][ks * 32 + 16 + t * 4]));
@@ -199,7 +215,7 @@ __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
         }
         const float x0 = st.sx[rb + g], x1 = st.sx[rb + g + 8];
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int nt = 0; nt < NTW; ++nt) {
             const int c = cb + nt * 8 + t * 2;
             const float w0 = st.sw[c], w1 = st.sw[c + 1];
             acc[nt][0] = __fmaf_rn(__fmul_rn((float)ic[nt][0], x0), w0, acc[nt][0]);
@@ -218,7 +234,7 @@ __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
     }
     cp_async_wait<0>();
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < NTW; ++nt) {
         const int col = n0 + cb + nt * 8 + t * 2;
         const int r0 = m0 + rb + g, r1 = r0 + 8;
         float *y0 = a.y + (int64_t)r0 * a.n + col, *y1 = a.y + (int64_t)r1 * a.n + col;
@@ -237,7 +253,16 @@ __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
     }
 }
 
-constexpr int kISmem = 2 * (int)sizeof(Int8Stage);
+template <bool PLUG, int BM, int BN, int STAGES>
+cudaError_t launch_gemm(const Int8Args &a, cudaStream_t st)
+{
+    constexpr int smem = STAGES * (int)sizeof(Int8Stage<BM, BN>);
+    auto kern = int8_gemm_kernel<PLUG, BM, BN, STAGES>;
+    if (!ensure_smem((const void *)kern, smem))
+        return cudaErrorInvalidValue;
+    kern<<<dim3((a.n + BN - 1) / BN, (a.m + BM - 1) / BM), kIThreads, smem, st>>>(a);
+    return cudaGetLastError();
+}
 
 cudaError_t quant(const __nv_bfloat16 *x, const int8_t *xq_prev, const float *sx_prev, int m, int k, int8_t *q,
                   float *s, cudaStream_t st)
@@ -251,17 +276,9 @@ cudaError_t gemm(const int8_t *xq, const float *sx, const int8_t *wq, const floa
                  int accumulate, const uint8_t *pq4, const float *psc, cudaStream_t st)
 {
     Int8Args a{xq, sx, wq, sw, y, m, n, k, accumulate, pq4, psc};
-    const dim3 grid((n + kIBN - 1) / kIBN, (m + kIBM - 1) / kIBM);
-    if (pq4) {
-        if (!ensure_smem((const void *)int8_gemm_kernel<true>, kISmem))
-            return cudaErrorInvalidValue;
-        int8_gemm_kernel<true><<<grid, kIThreads, kISmem, st>>>(a);
-    } else {
-        if (!ensure_smem((const void *)int8_gemm_kernel<false>, kISmem))
-            return cudaErrorInvalidValue;
-        int8_gemm_kernel<false><<<grid, kIThreads, kISmem, st>>>(a);
-    }
-    return cudaGetLastError();
+    if (m <= 16)
+        return pq4 ? launch_gemm<true, 16, 64, 8>(a, st) : launch_gemm<false, 16, 64, 8>(a, st);
+    return pq4 ? launch_gemm<true, 64, 128, 2>(a, st) : launch_gemm<false, 64, 128, 2>(a, st);
 }
 
 cudaError_t unpack(const uint8_t *q4, int8_t *out, int64_t n, cudaStream_t st)
