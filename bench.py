@@ -1147,6 +1147,23 @@ def profile_case(case: str, iters: int = 5):
         y = torch.empty((M, 14336), dtype=torch.float32, device="cuda")
         n = 14336 * 4096
         fn = lambda: D.htile(x, *planes[0], 14336, BS, mode="fast", out=y)  # noqa: E731
+    elif case in ("int8", "int8d"):
+        # INT8 W8A8 GEMM on a 14336 x 4096 int8 linear: M = 2048 plain, or M = 1 with the fused plug
+        from glint_b200 import int8 as I8
+        N, K = 14336, 4096
+        M = 2048 if case == "int8" else 1
+        q = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int8)
+        sc_w = torch.rand(N * K // 64, generator=g, device="cuda") * 2e-4 + 1e-5
+        q4 = torch.randint(0, 256, (N * K // 2,), generator=g, device="cuda", dtype=torch.uint8)
+        ps = torch.rand(N * K // 64, generator=g, device="cuda") * 2e-5
+        x = torch.randn((M, K), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        scr = {}
+        n = N * K
+        if case == "int8":
+            fn = lambda: I8.gemm(x, q, sc_w, out=y, scratch=scr)  # noqa: E731
+        else:
+            fn = lambda: I8.gemm(x, q, sc_w, plug=(q4, ps), kind="fused", out=y, scratch=scr)  # noqa: E731
     elif case in ("km", "kmstep"):
         # K-major decode at N = 14336, K = 4096: the parent-only GEMV, or the whole
         # step at 10 % of the channels selected
@@ -1181,7 +1198,8 @@ def main():
     ap.add_argument("--impl", default="glint_b200", choices=["glint_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default=None,
-                    help="run one small kernel case (encode|expand|gemv<M>|gemvt<M>|gemm<M>|gemmp<M>|km|kmstep) for ncu")
+                    help="run one small kernel case (encode|expand|gemv<M>|gemvt<M>|gemm<M>|gemmp<M>|km|kmstep|int8|int8d) "
+                         "for ncu")
     args = ap.parse_args()
     if args.profile:
         profile_case(args.profile)
