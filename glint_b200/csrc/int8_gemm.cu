@@ -13,7 +13,7 @@
  * whatever the tiling.
  *
  * On sm_100a: `mma.sync` m16n8k32 s8 tiles (64 activation rows x 128 weight rows
- * with a two-stage ring, or for M <= 16, 16 x 64 with an eight-stage ring), 8 warps,
+ * with a three-stage ring, or for M <= 16, 16 x 64 with an eight-stage ring), 8 warps,
  * shared-memory rings filled with 16-byte asynchronous copies (later K slices land
  * while this one multiplies), plug nibbles unpacked in shared memory.  No split over
  * K: each output's blocks are added in K order, as the reference adds them.  No kernel here waits on
@@ -147,8 +147,9 @@ __device__ __forceinline__ void load_slice(const Int8Args &a, Int8Stage<BM, BN> 
 
 /* Tiles of BM activation rows x BN weight rows; the 8 warps split them into BM / 16
  * row groups x (8 / (BM / 16)) column groups of NTW 8-column MMA tiles; STAGES K
- * slices in flight.  Large M: 64 x 128, 2 stages; decode (M <= 16): 16 x 64, 8
- * stages, so that there are enough CTAs and bytes in flight to stream the weights. */
+ * slices in flight.  Large M: 64 x 128, 3 stages; decode (M <= 16): 16 x 64, 8
+ * stages, so that there are enough CTAs and bytes in flight to stream the weights.
+ * One barrier per slice (two with a plug, whose unpacked copy is shared). */
 template <bool PLUG, int BM, int BN, int STAGES>
 __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
 {
@@ -176,11 +177,13 @@ __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
     }
     for (int kb = 0; kb < nkb; ++kb) {
         Stage &st = stages[kb % STAGES];
+        cp_async_wait<STAGES - 2>(); /* this slice's copies have landed */
+        /* every thread's copies of slice kb are visible, and every thread is done with
+         * slice kb - 1, whose stage the next load reuses */
+        __syncthreads();
         if (kb + STAGES - 1 < nkb)
             load_slice<PLUG, BM, BN>(a, stages[(kb + STAGES - 1) % STAGES], m0, n0, kb + STAGES - 1, nkb);
         cp_async_commit();
-        cp_async_wait<STAGES - 1>(); /* this slice's copies have landed */
-        __syncthreads();
         if (PLUG) {
             /* unpack: row r, packed byte b -> elements 2b (low nibble), 2b + 1 */
             for (int i = tid; i < BN * 32; i += kIThreads) {
@@ -230,7 +233,6 @@ __global__ void __launch_bounds__(kIThreads) int8_gemm_kernel(const Int8Args a)
                 acc[nt][3] = __fmaf_rn(__fmul_rn((float)ip[nt][3], x1), q1, acc[nt][3]);
             }
         }
-        __syncthreads(); /* the stage (and sP) may be refilled */
     }
     cp_async_wait<0>();
 #pragma unroll
@@ -278,7 +280,7 @@ cudaError_t gemm(const int8_t *xq, const float *sx, const int8_t *wq, const floa
     Int8Args a{xq, sx, wq, sw, y, m, n, k, accumulate, pq4, psc};
     if (m <= 16)
         return pq4 ? launch_gemm<true, 16, 64, 8>(a, st) : launch_gemm<false, 16, 64, 8>(a, st);
-    return pq4 ? launch_gemm<true, 64, 128, 2>(a, st) : launch_gemm<false, 64, 128, 2>(a, st);
+    return pq4 ? launch_gemm<true, 64, 128, 3>(a, st) : launch_gemm<false, 64, 128, 3>(a, st);
 }
 
 cudaError_t unpack(const uint8_t *q4, int8_t *out, int64_t n, cudaStream_t st)
