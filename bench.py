@@ -632,26 +632,30 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
         pg = None
         if world > 1:
             pg = tp.PeerGather({"attn": (M, hid, torch.bfloat16), "o": (M, hid, torch.float32),
-                                "gu": (M, 2 * inter, torch.float32), "down": (M, hid, torch.float32)}, world, rank)
+                                "gu": (M, 2 * inter, torch.float32), "down": (M, hid, torch.bfloat16)}, world, rank)
         hidden = torch.empty((M, hid), dtype=torch.bfloat16, device="cuda")
+        act = torch.empty((M, inter), dtype=torch.bfloat16, device="cuda")
+        downs = [torch.empty((M, hid), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
 
         def step():
             hidden.copy_(x0)
-            for lay in stack:
-                tp.column_parallel(hidden, lay["qkv"], world, rank, gather=False)
+            h = hidden
+            for li, lay in enumerate(stack):
+                tp.column_parallel(h, lay["qkv"], world, rank, gather=False)
                 if pg is None:
                     tp.column_parallel(attn, lay["o"], 1, 0)
-                    gu = tp.column_parallel(hidden, lay["gu"], 1, 0)
-                    act = (F.silu(gu[:, :inter]) * gu[:, inter:]).to(torch.bfloat16)
-                    d = tp.column_parallel(act, lay["down"], 1, 0)
+                    gu = tp.column_parallel(h, lay["gu"], 1, 0)
+                    torch.mul(F.silu(gu[:, :inter]), gu[:, inter:], out=act)  # silu(gate) * up, stored BF16
+                    sd = lay["down"]
+                    # down writes the next layer's BF16 hidden state itself
+                    h = D.htile(act, sd.hole, sd.plug, sd.absmax, sd.rows, BS, mode="fast", out=downs[li & 1])
                 else:
                     sh_o = lay["o"]
                     o_in = pg.gather(attn[:, sh_o.n0:sh_o.n1], "attn", sh_o.n0)  # this rank's heads
                     pg.linear(o_in, sh_o, "o")
-                    gu = pg.linear(hidden, lay["gu"], "gu")
-                    act = (F.silu(gu[:, :inter]) * gu[:, inter:]).to(torch.bfloat16)
-                    d = pg.linear(act, lay["down"], "down")
-                hidden.copy_(d)
+                    gu = pg.linear(h, lay["gu"], "gu")
+                    torch.mul(F.silu(gu[:, :inter]), gu[:, inter:], out=act)
+                    h = pg.linear(act, lay["down"], "down")  # BF16, gathered: the next layer's hidden state
 
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -687,7 +691,8 @@ def bench_decode_stack(args, world, rank, pk, checks, batches_m=(1, 8, 32)):
                                   "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
     kerr = int(max_over_ranks(world, float(L.glint_kernel_error(1))))
     out["kernel_error"] = kerr
-    out["launches_per_step"] = layers * len(fused)
+    # the four decode kernels per layer, and at world > 1 the attention-output gather
+    out["launches_per_step"] = layers * (len(fused) + (1 if world > 1 else 0))
     checks["decode_stack_ok"] = kerr == 0
     del stack
     torch.cuda.empty_cache()
