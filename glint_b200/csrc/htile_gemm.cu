@@ -250,9 +250,10 @@ struct GemmArgs {
 /* Work split (stream-K for the first S tiles, then data-parallel rounds): the
  * units (tile, K group) of tiles 0 .. S-1 are cut into P equal ranges, pair p
  * owning [unit_begin(p), unit_begin(p + 1)); the remaining R * P tiles go
- * whole, round-robin.  S = tiles mod P + P (or all tiles when there are fewer
- * than 2P), so every pair ends at the same time, a shared tile has at most a
- * few contributors, and their sums are done while the whole tiles run. */
+ * whole, round-robin.  S = tiles mod P + P with two or more rounds, or tiles - P
+ * between one and two (R = 1 there), so every pair ends at the same time, a shared
+ * tile has at most a few contributors, and their sums are done while whole tiles
+ * run. */
 __device__ __forceinline__ int unit_begin(const GemmArgs &a, int p, int P) { return (int)((int64_t)p * a.U / P); }
 __device__ __forceinline__ int pair_of(const GemmArgs &a, int u, int P)
 {
@@ -1142,14 +1143,19 @@ int gemm_launch_impl(const uint8_t *hole, const uint8_t *plug, const float *am, 
     a.G = K / (PSTEPS * BK);
     const int tiles = a.mtiles * a.ntiles;
     /* whole tiles only, unless the last data-parallel round would leave more than
-     * 2% of the pairs' time idle and there are at least two rounds, so that the
-     * shared tiles' sums overlap whole tiles */
+     * 2% of the pairs' time idle; then the remainder is shared stream-K: with two or
+     * more rounds, (tiles mod P) + P tiles, after which whole rounds follow (their
+     * sums overlap whole tiles); between one and two rounds, the tiles beyond one
+     * round (e.g. 512 x 14336: 112 tiles on 74 pairs, 86.8 -> 76.9 us; sharing all
+     * tiles instead cost more in split-tile sums than it saved) */
     const int maxp = max_pairs();
     const int rounds = (tiles + maxp - 1) / maxp;
-    const bool split = tiles >= 2 * maxp && (double)(rounds * maxp - tiles) > 0.02 * rounds * maxp;
+    const bool idle = (double)(rounds * maxp - tiles) > 0.02 * rounds * maxp;
+    const bool split1 = tiles > maxp && tiles < 2 * maxp && idle;
+    const bool split = split1 || (tiles >= 2 * maxp && idle);
     const int pairs = split ? maxp : std::max(1, std::min(tiles, maxp));
     a.tiles = tiles;
-    a.R = split ? tiles / pairs - 1 : (tiles + pairs - 1) / pairs;
+    a.R = split ? (split1 ? 1 : tiles / pairs - 1) : (tiles + pairs - 1) / pairs;
     a.S = split ? tiles - a.R * pairs : 0;
     a.U = a.S * a.G;
     if (!gemm_scratch(st, (size_t)pairs * 2 * 2 * 4 * kPartFloats, (size_t)tiles * 8, &a.ws, &a.counters))
