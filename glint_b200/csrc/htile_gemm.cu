@@ -1019,6 +1019,337 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PThreads, 1)
     }
 }
 
+/* ---- INT8 W8A8 (the reference's int8_mma_gemm contract) on tcgen05 kind::i8 -------
+ * y[m, n] (+)= sum_b (float)(xq[m, b] . wq[n, b]) * sx[m, b] * sw[n, b] over 64-k blocks
+ * b in K order, each block's int8 products summed exactly in int32 by the tensor cores
+ * and scaled on the CUDA cores with the reference's f32 steps (one rounded product by
+ * sx, then a fused multiply-add by sw into the running sum), so every output is the
+ * reference kernel's bits.  CTA pairs take tiles of 256 weight rows x 128 activation
+ * rows; both operands arrive by TMA (int8, K-major, 128-byte swizzle: one stage holds
+ * two 64-k blocks of this CTA's 128 weight rows and 64 activation rows, the bytes of
+ * both CTAs counted on the leader's barrier); the leader's lane 0 issues two kind::i8
+ * UMMAs (M = 256, N = 128, K = 32) per block into one of two 128-column TMEM
+ * accumulators; 8 epilogue warps (64 columns of one lane quadrant each) read a block,
+ * free its accumulator and scale it into their running sums.  Roles: warp 0 TMA
+ * producer, warp 1 TMEM owner and issuer, warps 2-9 epilogue.  Every wait is bounded
+ * as in the kernels above. */
+constexpr int IBMX = 128, IBMH = 64;   /* activation rows per pair tile / per CTA */
+constexpr int IBK2 = 128;              /* K bytes per stage: two 64-k blocks */
+constexpr int ISTAGES = 4;
+/* 11 warps: producer, issuer, scale stager, 8 epilogue warps.  A CTA's warps are spread
+ * over the SM's four sub-partitions, each with a 16K-register file, so at most three
+ * warps share one and each may hold 168 registers (the epilogue keeps 64 running sums
+ * and 64 accumulator values per lane). */
+constexpr int IEpi0 = 3, IEpiWarps = 8;
+constexpr int IThreads = (IEpi0 + IEpiWarps) * 32; /* 352 */
+constexpr int IStageX = IBMH * IBK2;               /* 8 KB */
+constexpr int IStage = IStageX + BN * IBK2;        /* + 16 KB of weights */
+constexpr int ISXC = 8, ISXSTAGES = 4;             /* activation scales: 8 blocks x 128 rows per chunk */
+constexpr int ISxChunk = ISXC * IBMX * 4;          /* 4 KB */
+constexpr int ISmemBytes = 1024 + ISTAGES * IStage + ISXSTAGES * ISxChunk + 256;
+constexpr uint32_t kITmemCols = 2 * IBMX;
+/* instruction descriptor: s32 accumulate, s8 A and B, both K-major, N = 128, M = 256 (pair) */
+constexpr uint32_t kIdescI8 =
+    (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(IBMX >> 3) << 17) | ((uint32_t)((2 * BN) >> 4) << 24);
+/* Each accumulator starts a block at the bits of the float 1.5 * 2^23 (0x4B400000), so
+ * the int32 it holds after the block, 0x4B400000 + sum with |sum| <= 64 * 128 * 128 =
+ * 2^20, read as a float is exactly 1.5 * 2^23 + sum: one exact subtraction gives
+ * (float)sum without a conversion instruction. */
+constexpr uint32_t kI8Bias = 0x4B400000u;
+constexpr float kI8BiasF = 12582912.0f;
+
+struct I8Maps {
+    CUtensorMap x, w;
+};
+struct I8Args {
+    const float *sx, *sw;
+    float *y;
+    int M, N, K;
+    int accumulate;
+    int mtiles, tiles;
+};
+
+/* D[tmem] (+)= A[smem] * B[smem]^T over the CTA pair, kind::i8 */
+__device__ __forceinline__ void umma_pair_ss_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc)
+{
+    asm volatile("tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, 1;" ::"r"(d), "l"(a), "l"(b), "r"(idesc));
+}
+/* 32 columns of this warp's 32 TMEM lanes set to one value */
+__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t c)
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+                 "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+                 "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+                 "r"(c)
+                 : "memory");
+}
+/* two f32 lanes at once, each rounded as its scalar operation */
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
+    int8_tc_kernel(const __grid_constant__ I8Maps maps, const I8Args args)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *sxs = reinterpret_cast<float *>(ring + ISTAGES * IStage); /* [stage][block][128 rows] */
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + ISTAGES * IStage + ISXSTAGES * ISxChunk);
+    uint64_t *empty = full + ISTAGES;
+    uint64_t *acc_full = empty + ISTAGES; /* [2] */
+    uint64_t *acc_empty = acc_full + 2;   /* [2] leader: both CTAs' epilogues release it */
+    uint64_t *sx_full = acc_empty + 2;    /* [ISXSTAGES] the stager's 32 lanes */
+    uint64_t *sx_empty = sx_full + ISXSTAGES; /* [ISXSTAGES] this CTA's epilogue warps */
+    uint64_t *mma_done = sx_empty + ISXSTAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const uint32_t lane = lane_id();
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    const int nkb = args.K / 64, KS2 = args.K / IBK2;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ISTAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * IEpiWarps);
+        }
+        for (int s = 0; s < ISXSTAGES; ++s) {
+            mbar_init(&sx_full[s], 32);
+            mbar_init(&sx_empty[s], IEpiWarps);
+        }
+        mbar_init(mma_done, 1);
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                     "r"(kITmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync(); /* both CTAs' barriers initialised and TMEM allocated */
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool alive = true;
+
+    if (warp == 0) {
+        /* ---- producer (both CTAs): this CTA's 64 activation rows and 128 weight rows */
+        if (lane == 0) {
+            Ring st;
+            int64_t issued = 0;
+            for (int T = pair; T < args.tiles && alive; T += npairs) {
+                const int mr = (T % args.mtiles) * IBMX + (int)rank * IBMH;
+                const int nr = (T / args.mtiles) * (2 * BN) + (int)rank * BN;
+                for (int ks = 0; ks < KS2 && alive; ++ks, st.next<ISTAGES>()) {
+                    if (!wait_or_fail(&empty[st.i], st.ph ^ 1u, alive))
+                        break;
+                    if (leader)
+                        mbar_expect_tx(&full[st.i], 2 * IStage);
+                    const uint32_t fb = peer_addr(saddr(&full[st.i]), 0);
+                    tma_load_2d_pair(ring + st.i * IStage, &maps.x, fb, ks * IBK2, mr);
+                    tma_load_2d_pair(ring + st.i * IStage + IStageX, &maps.w, fb, ks * IBK2, nr);
+                    ++issued;
+                }
+            }
+            if (!alive && leader) {
+                /* let the loads already issued land before the CTA exits */
+                bool drain = true;
+                for (int64_t j = issued > ISTAGES ? issued - ISTAGES : 0; j < issued && drain; ++j)
+                    drain = mbar_wait_bounded(&full[(int)(j % ISTAGES)], (uint32_t)(j / ISTAGES) & 1u,
+                                              &g_glint_kernel_error);
+            }
+        }
+    } else if (warp == 1) {
+        /* ---- UMMA issuer (leader CTA only): each block accumulates onto the bias the
+         * epilogue wrote into the accumulator (its first release of each one is the
+         * initial fill, so use u of an accumulator waits on phase u) */
+        if (leader && lane == 0) {
+            Ring st;
+            int64_t g = 0; /* blocks issued by this pair: accumulator g & 1, its use g >> 1 */
+            const uint32_t e0 = peer_addr(saddr(&empty[0]), 0), e1 = peer_addr(saddr(&empty[0]), 1);
+            const uint32_t af0 = peer_addr(saddr(&acc_full[0]), 0), af1 = peer_addr(saddr(&acc_full[0]), 1);
+            for (int T = pair; T < args.tiles && alive; T += npairs) {
+                for (int ks = 0; ks < KS2 && alive; ++ks, st.next<ISTAGES>()) {
+                    if (!wait_or_fail(&full[st.i], st.ph, alive))
+                        break;
+                    tc_fence_after();
+                    const uint32_t xs = saddr(ring + st.i * IStage), ws = xs + (uint32_t)IStageX;
+                    for (int blk = 0; blk < 2 && alive; ++blk, ++g) {
+                        const int b = (int)(g & 1);
+                        if (!wait_or_fail(&acc_empty[b], (uint32_t)((g >> 1) & 1), alive))
+                            break;
+                        tc_fence_after();
+                        const uint32_t d = tmem + (uint32_t)b * IBMX;
+#pragma unroll
+                        for (int kk = 0; kk < 2; ++kk) {
+                            const uint32_t off = (uint32_t)(blk * 2 + kk) * 32u; /* K = 32 bytes per UMMA */
+                            umma_pair_ss_i8(d, sw128_desc(ws + off), sw128_desc(xs + off), kIdescI8);
+                        }
+                        umma_commit_to(af0 + (uint32_t)b * 8u);
+                        umma_commit_to(af1 + (uint32_t)b * 8u);
+                    }
+                    if (!alive)
+                        break;
+                    umma_commit_to(e0 + (uint32_t)st.i * 8u);
+                    umma_commit_to(e1 + (uint32_t)st.i * 8u);
+                }
+            }
+            /* all UMMAs issued by this thread have completed before TMEM is released */
+            umma_commit_to(peer_addr(saddr(mma_done), 0));
+            mbar_wait_bounded(mma_done, 0, &g_glint_kernel_error);
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        /* ---- scale stager: the tile's 128 activation rows' sx, 8 blocks at a time,
+         * transposed to [block][row] so an epilogue warp reads its rows' scales of one
+         * block as contiguous 16-byte words */
+        Ring cs;
+        for (int T = pair; T < args.tiles && alive; T += npairs) {
+            const int mb = (T % args.mtiles) * IBMX;
+            for (int kb0 = 0; kb0 < nkb && alive; kb0 += ISXC, cs.next<ISXSTAGES>()) {
+                if (!warp_wait(&sx_empty[cs.i], cs.ph ^ 1u, alive))
+                    break;
+                __syncwarp();
+                float *dst = sxs + cs.i * (ISXC * IBMX);
+                const int nb = min(ISXC, nkb - kb0);
+#pragma unroll
+                for (int rr = 0; rr < IBMX / 32; ++rr) {
+                    const int r = rr * 32 + (int)lane, m = mb + r;
+                    const float *src = args.sx + (size_t)m * nkb + kb0;
+#pragma unroll
+                    for (int j = 0; j < ISXC; ++j)
+                        dst[j * IBMX + r] = (m < args.M && j < nb) ? __ldg(src + j) : 0.f;
+                }
+                mbar_arrive(&sx_full[cs.i]);
+            }
+        }
+    } else {
+        /* ---- epilogue: warp w -> TMEM lanes 32*(w%4) (weight rows n), columns c0 .. c0+63
+         * (activation rows m) */
+        const int q = warp & 3, c0 = ((warp - IEpi0) >> 2) * 64;
+        const uint32_t ae0 = peer_addr(saddr(&acc_empty[0]), 0);
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+        const uint64_t nbias = pack2u(__float_as_uint(-kI8BiasF), __float_as_uint(-kI8BiasF));
+        /* both accumulators start at the bias */
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            tmem_fill32(tb + (uint32_t)b * IBMX, kI8Bias);
+            tmem_fill32(tb + (uint32_t)b * IBMX + 32u, kI8Bias);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive_remote(ae0);
+            mbar_arrive_remote(ae0 + 8u);
+        }
+        Ring cs;
+        int64_t g = 0;
+        for (int T = pair; T < args.tiles && alive; T += npairs) {
+            const int m0 = (T % args.mtiles) * IBMX + c0;
+            const int n = (T / args.mtiles) * (2 * BN) + (int)rank * BN + q * 32 + (int)lane;
+            const bool nok = n < args.N;
+            const int jl = min(64, args.M - m0);
+            uint64_t run[32]; /* rows m0 + 2i and m0 + 2i + 1 */
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                run[i] = 0;
+            for (int kb = 0; kb < nkb && alive; ++kb, ++g) {
+                const int b = (int)(g & 1), j = kb % ISXC;
+                /* sw of this lane's row, fetched before the waits */
+                const float swf = nok ? __ldg(args.sw + (size_t)n * nkb + kb) : 0.f;
+                const uint64_t sw2 = pack2u(__float_as_uint(swf), __float_as_uint(swf));
+                if (j == 0) {
+                    if (!warp_wait(&sx_full[cs.i], cs.ph, alive))
+                        break;
+                    __syncwarp();
+                }
+                if (!warp_wait(&acc_full[b], (uint32_t)(g >> 1) & 1u, alive))
+                    break;
+                tc_fence_after();
+                /* one 32-column half at a time: read, scale into the running sums */
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t v[32];
+                    tmem_ld32(tb + (uint32_t)b * IBMX + (uint32_t)h * 32u, v);
+                    tmem_ld_wait();
+                    const ulonglong2 *sp = reinterpret_cast<const ulonglong2 *>(sxs + cs.i * (ISXC * IBMX) +
+                                                                                 j * IBMX + c0 + h * 32);
+#pragma unroll
+                    for (int i4 = 0; i4 < 8; ++i4) {
+                        const ulonglong2 s4 = sp[i4]; /* sx of rows 4*i4 .. 4*i4 + 3 of this half */
+                        const int i = h * 16 + 2 * i4;
+                        run[i] = f2_fma(f2_mul(f2_add(pack2u(v[4 * i4], v[4 * i4 + 1]), nbias), s4.x), sw2, run[i]);
+                        run[i + 1] = f2_fma(f2_mul(f2_add(pack2u(v[4 * i4 + 2], v[4 * i4 + 3]), nbias), s4.y), sw2,
+                                            run[i + 1]);
+                    }
+                }
+                /* the accumulator back to the bias for its next block, then free */
+                tmem_fill32(tb + (uint32_t)b * IBMX, kI8Bias);
+                tmem_fill32(tb + (uint32_t)b * IBMX + 32u, kI8Bias);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_remote(ae0 + (uint32_t)b * 8u);
+                if (j == ISXC - 1 || kb == nkb - 1) {
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive(&sx_empty[cs.i]);
+                    cs.next<ISXSTAGES>();
+                }
+            }
+            if (!alive || !nok)
+                continue;
+            float *yp = args.y + (size_t)m0 * args.N + n;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float lo = __uint_as_float((uint32_t)run[i]), hi = __uint_as_float((uint32_t)(run[i] >> 32));
+                if (2 * i < jl)
+                    yp[0] = (args.accumulate ? yp[0] : 0.f) + lo;
+                yp += args.N;
+                if (2 * i + 1 < jl)
+                    yp[0] = (args.accumulate ? yp[0] : 0.f) + hi;
+                yp += args.N;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync(); /* the peer no longer reads this CTA's TMEM or shared memory */
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kITmemCols) : "memory");
+    }
+}
+
 } // namespace
 
 bool htile_gemm_supported(const uint8_t *hole, const uint8_t *plug, const float *am, const __nv_bfloat16 *x,
@@ -1090,10 +1421,10 @@ bool gemm_scratch(cudaStream_t st, size_t ws_floats, size_t n_counters, float **
 }
 
 /* CTA pairs of `kernel` that fit on the device at once (one pair per two SMs at
- * most); cached per device and kernel kind (0 fast, 1 precise) */
+ * most); cached per device and kernel kind (0 fast, 1 precise, 2 int8) */
 int max_pairs(int kind = 0)
 {
-    static int cached[64][2] = {};
+    static int cached[64][3] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return std::max(1, sm_count() / 2);
@@ -1105,11 +1436,13 @@ int max_pairs(int kind = 0)
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * std::max(1, sm_count() / 2));
-    cfg.blockDim = dim3(kind ? PThreads : kThreads);
-    cfg.dynamicSmemBytes = kind ? PSmemBytes : kSmemBytes;
+    cfg.blockDim = dim3(kind == 2 ? IThreads : kind ? PThreads : kThreads);
+    cfg.dynamicSmemBytes = kind == 2 ? ISmemBytes : kind ? PSmemBytes : kSmemBytes;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const void *kern = kind ? (const void *)htile_gemm_precise_kernel : (const void *)htile_gemm_kernel;
+    const void *kern = kind == 2   ? (const void *)int8_tc_kernel
+                       : kind == 1 ? (const void *)htile_gemm_precise_kernel
+                                   : (const void *)htile_gemm_kernel;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
         cudaGetLastError();
         n = std::max(1, sm_count() / 2);
@@ -1205,6 +1538,31 @@ int htile_gemm_precise_launch(const uint8_t *hole, const uint8_t *plug, const fl
     const int pairs = std::max(1, std::min(a.tiles, max_pairs(1)));
     htile_gemm_precise_kernel<<<2 * pairs, PThreads, PSmemBytes, st>>>(maps, a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
+}
+
+bool int8_tc_supported(const int8_t *xq, const int8_t *wq, int M, int K)
+{
+    return M > 64 && K >= IBK2 && K % IBK2 == 0 && aligned_to(xq, 16) && aligned_to(wq, 16) &&
+           tensor_map_encoder() != nullptr;
+}
+
+cudaError_t int8_tc_gemm_launch(const int8_t *xq, const float *sx, const int8_t *wq, const float *sw, float *y, int M,
+                                int N, int K, int accumulate, cudaStream_t st)
+{
+    I8Maps maps;
+    if (!encode_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)K, (uint64_t)M, (uint64_t)K, IBK2, IBMH,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_map(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K, (uint64_t)N, (uint64_t)K, IBK2, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !ensure_smem((const void *)int8_tc_kernel, ISmemBytes))
+        return cudaErrorNotSupported;
+    I8Args a{};
+    a.sx = sx, a.sw = sw, a.y = y, a.M = M, a.N = N, a.K = K, a.accumulate = accumulate;
+    a.mtiles = (M + IBMX - 1) / IBMX;
+    a.tiles = a.mtiles * ((N + 2 * BN - 1) / (2 * BN));
+    const int pairs = std::max(1, std::min(a.tiles, max_pairs(2)));
+    int8_tc_kernel<<<2 * pairs, IThreads, ISmemBytes, st>>>(maps, a);
+    return cudaGetLastError();
 }
 
 int read_kernel_error(bool clear)
