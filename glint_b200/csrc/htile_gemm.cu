@@ -1040,21 +1040,27 @@ constexpr int ISTAGES = 4;
  * over the SM's four sub-partitions, each with a 16K-register file, so at most three
  * warps share one and each may hold 168 registers (the epilogue keeps 64 running sums
  * and 64 accumulator values per lane). */
-constexpr int IEpi0 = 3, IEpiWarps = 8;
-constexpr int IThreads = (IEpi0 + IEpiWarps) * 32; /* 352 */
+constexpr int IEpiCols = 32;                       /* accumulator columns per epilogue warp */
+constexpr int IEpi0 = 3, IEpiWarps = 4 * (IBMX / IEpiCols);
+constexpr int IThreads = (IEpi0 + IEpiWarps) * 32;
 constexpr int IStageX = IBMH * IBK2;               /* 8 KB */
 constexpr int IStage = IStageX + BN * IBK2;        /* + 16 KB of weights */
-constexpr int ISXC = 8, ISXSTAGES = 4;             /* activation scales: 8 blocks x 128 rows per chunk */
-constexpr int ISxChunk = ISXC * IBMX * 4;          /* 4 KB */
+constexpr int ISXC = 8, ISXSTAGES = 4;             /* scales: 8 blocks per chunk */
+/* a chunk: sx of the tile's 128 activation rows, then sw of this CTA's 128 weight rows,
+ * each [block][row] */
+constexpr int ISxChunk = 2 * ISXC * IBMX * 4; /* 8 KB */
 constexpr int ISmemBytes = 1024 + ISTAGES * IStage + ISXSTAGES * ISxChunk + 256;
-constexpr uint32_t kITmemCols = 2 * IBMX;
+/* four 128-column accumulators (all of TMEM): the tensor cores run up to three blocks
+ * ahead of the epilogue, which hides the per-block hand-over (commit, wake, read,
+ * release, issue) */
+constexpr int IACC = 4;
+constexpr uint32_t kITmemCols = IACC * IBMX;
 /* instruction descriptor: s32 accumulate, s8 A and B, both K-major, N = 128, M = 256 (pair) */
 constexpr uint32_t kIdescI8 =
     (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(IBMX >> 3) << 17) | ((uint32_t)((2 * BN) >> 4) << 24);
-/* Each accumulator starts a block at the bits of the float 1.5 * 2^23 (0x4B400000), so
- * the int32 it holds after the block, 0x4B400000 + sum with |sum| <= 64 * 128 * 128 =
- * 2^20, read as a float is exactly 1.5 * 2^23 + sum: one exact subtraction gives
- * (float)sum without a conversion instruction. */
+/* (float)sum of a block on the full-rate pipes: 0x4B400000 + sum, with |sum| <= 64 * 128
+ * * 128 = 2^20, read as a float is exactly 1.5 * 2^23 + sum, so one integer add and one
+ * exact float subtraction give (float)sum without a conversion instruction. */
 constexpr uint32_t kI8Bias = 0x4B400000u;
 constexpr float kI8BiasF = 12582912.0f;
 
@@ -1070,18 +1076,11 @@ struct I8Args {
 };
 
 /* D[tmem] (+)= A[smem] * B[smem]^T over the CTA pair, kind::i8 */
-__device__ __forceinline__ void umma_pair_ss_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc)
+__device__ __forceinline__ void umma_pair_ss_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
 {
-    asm volatile("tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, 1;" ::"r"(d), "l"(a), "l"(b), "r"(idesc));
-}
-/* 32 columns of this warp's 32 TMEM lanes set to one value */
-__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t c)
-{
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-                 "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-                 "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-                 "r"(c)
-                 : "memory");
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+                 "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 /* two f32 lanes at once, each rounded as its scalar operation */
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
@@ -1114,12 +1113,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *sxs = reinterpret_cast<float *>(ring + ISTAGES * IStage); /* [stage][block][128 rows] */
+    float *sxs = reinterpret_cast<float *>(ring + ISTAGES * IStage); /* [stage][sx | sw][block][128 rows] */
     uint64_t *full = reinterpret_cast<uint64_t *>(ring + ISTAGES * IStage + ISXSTAGES * ISxChunk);
     uint64_t *empty = full + ISTAGES;
-    uint64_t *acc_full = empty + ISTAGES; /* [2] */
-    uint64_t *acc_empty = acc_full + 2;   /* [2] leader: both CTAs' epilogues release it */
-    uint64_t *sx_full = acc_empty + 2;    /* [ISXSTAGES] the stager's 32 lanes */
+    uint64_t *acc_full = empty + ISTAGES; /* [IACC] */
+    uint64_t *acc_empty = acc_full + IACC; /* [IACC] leader: both CTAs' epilogues release it */
+    uint64_t *sx_full = acc_empty + IACC;  /* [ISXSTAGES] the stager's 32 lanes */
     uint64_t *sx_empty = sx_full + ISXSTAGES; /* [ISXSTAGES] this CTA's epilogue warps */
     uint64_t *mma_done = sx_empty + ISXSTAGES;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
@@ -1136,7 +1135,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < IACC; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 2 * IEpiWarps);
         }
@@ -1187,12 +1186,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
             }
         }
     } else if (warp == 1) {
-        /* ---- UMMA issuer (leader CTA only): each block accumulates onto the bias the
-         * epilogue wrote into the accumulator (its first release of each one is the
-         * initial fill, so use u of an accumulator waits on phase u) */
+        /* ---- UMMA issuer (leader CTA only): one fresh accumulator per 64-k block */
         if (leader && lane == 0) {
             Ring st;
-            int64_t g = 0; /* blocks issued by this pair: accumulator g & 1, its use g >> 1 */
+            int64_t g = 0; /* blocks issued by this pair: accumulator g % IACC, its use g / IACC */
             const uint32_t e0 = peer_addr(saddr(&empty[0]), 0), e1 = peer_addr(saddr(&empty[0]), 1);
             const uint32_t af0 = peer_addr(saddr(&acc_full[0]), 0), af1 = peer_addr(saddr(&acc_full[0]), 1);
             for (int T = pair; T < args.tiles && alive; T += npairs) {
@@ -1202,15 +1199,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
                     tc_fence_after();
                     const uint32_t xs = saddr(ring + st.i * IStage), ws = xs + (uint32_t)IStageX;
                     for (int blk = 0; blk < 2 && alive; ++blk, ++g) {
-                        const int b = (int)(g & 1);
-                        if (!wait_or_fail(&acc_empty[b], (uint32_t)((g >> 1) & 1), alive))
+                        const int b = (int)(g % IACC);
+                        /* the first use of each accumulator waits on parity 1: returns at once */
+                        if (!wait_or_fail(&acc_empty[b], (uint32_t)((g / IACC) & 1) ^ 1u, alive))
                             break;
                         tc_fence_after();
                         const uint32_t d = tmem + (uint32_t)b * IBMX;
 #pragma unroll
                         for (int kk = 0; kk < 2; ++kk) {
                             const uint32_t off = (uint32_t)(blk * 2 + kk) * 32u; /* K = 32 bytes per UMMA */
-                            umma_pair_ss_i8(d, sw128_desc(ws + off), sw128_desc(xs + off), kIdescI8);
+                            umma_pair_ss_i8(d, sw128_desc(ws + off), sw128_desc(xs + off), kIdescI8, kk > 0 ? 1u : 0u);
                         }
                         umma_commit_to(af0 + (uint32_t)b * 8u);
                         umma_commit_to(af1 + (uint32_t)b * 8u);
@@ -1227,25 +1225,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
         }
         __syncwarp();
     } else if (warp == 2) {
-        /* ---- scale stager: the tile's 128 activation rows' sx, 8 blocks at a time,
-         * transposed to [block][row] so an epilogue warp reads its rows' scales of one
-         * block as contiguous 16-byte words */
+        /* ---- scale stager: sx of the tile's 128 activation rows and sw of this CTA's
+         * 128 weight rows, 8 blocks at a time, transposed to [block][row] so an epilogue
+         * warp reads its rows' sx of one block as contiguous 16-byte words and each lane
+         * its row's sw without a global load in the block loop */
         Ring cs;
         for (int T = pair; T < args.tiles && alive; T += npairs) {
             const int mb = (T % args.mtiles) * IBMX;
+            const int nb0 = (T / args.mtiles) * (2 * BN) + (int)rank * BN;
             for (int kb0 = 0; kb0 < nkb && alive; kb0 += ISXC, cs.next<ISXSTAGES>()) {
                 if (!warp_wait(&sx_empty[cs.i], cs.ph ^ 1u, alive))
                     break;
                 __syncwarp();
-                float *dst = sxs + cs.i * (ISXC * IBMX);
+                float *dst = sxs + cs.i * (2 * ISXC * IBMX);
                 const int nb = min(ISXC, nkb - kb0);
 #pragma unroll
                 for (int rr = 0; rr < IBMX / 32; ++rr) {
-                    const int r = rr * 32 + (int)lane, m = mb + r;
-                    const float *src = args.sx + (size_t)m * nkb + kb0;
+                    const int r = rr * 32 + (int)lane, m = mb + r, nr = nb0 + r;
+                    const float *srcx = args.sx + (size_t)m * nkb + kb0;
+                    const float *srcw = args.sw + (size_t)nr * nkb + kb0;
 #pragma unroll
                     for (int j = 0; j < ISXC; ++j)
-                        dst[j * IBMX + r] = (m < args.M && j < nb) ? __ldg(src + j) : 0.f;
+                        dst[j * IBMX + r] = (m < args.M && j < nb) ? __ldg(srcx + j) : 0.f;
+#pragma unroll
+                    for (int j = 0; j < ISXC; ++j)
+                        dst[(ISXC + j) * IBMX + r] = (nr < args.N && j < nb) ? __ldg(srcw + j) : 0.f;
                 }
                 mbar_arrive(&sx_full[cs.i]);
             }
@@ -1253,72 +1257,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
     } else {
         /* ---- epilogue: warp w -> TMEM lanes 32*(w%4) (weight rows n), columns c0 .. c0+63
          * (activation rows m) */
-        const int q = warp & 3, c0 = ((warp - IEpi0) >> 2) * 64;
+        const int q = warp & 3, c0 = ((warp - IEpi0) >> 2) * IEpiCols;
         const uint32_t ae0 = peer_addr(saddr(&acc_empty[0]), 0);
         const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
         const uint64_t nbias = pack2u(__float_as_uint(-kI8BiasF), __float_as_uint(-kI8BiasF));
-        /* both accumulators start at the bias */
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-            tmem_fill32(tb + (uint32_t)b * IBMX, kI8Bias);
-            tmem_fill32(tb + (uint32_t)b * IBMX + 32u, kI8Bias);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-            mbar_arrive_remote(ae0);
-            mbar_arrive_remote(ae0 + 8u);
-        }
         Ring cs;
         int64_t g = 0;
         for (int T = pair; T < args.tiles && alive; T += npairs) {
             const int m0 = (T % args.mtiles) * IBMX + c0;
             const int n = (T / args.mtiles) * (2 * BN) + (int)rank * BN + q * 32 + (int)lane;
             const bool nok = n < args.N;
-            const int jl = min(64, args.M - m0);
-            uint64_t run[32]; /* rows m0 + 2i and m0 + 2i + 1 */
+            const int jl = min(IEpiCols, args.M - m0);
+            uint64_t run[IEpiCols / 2]; /* rows m0 + 2i and m0 + 2i + 1 */
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 0; i < IEpiCols / 2; ++i)
                 run[i] = 0;
             for (int kb = 0; kb < nkb && alive; ++kb, ++g) {
-                const int b = (int)(g & 1), j = kb % ISXC;
-                /* sw of this lane's row, fetched before the waits */
-                const float swf = nok ? __ldg(args.sw + (size_t)n * nkb + kb) : 0.f;
-                const uint64_t sw2 = pack2u(__float_as_uint(swf), __float_as_uint(swf));
+                const int b = (int)(g % IACC), j = kb % ISXC;
                 if (j == 0) {
                     if (!warp_wait(&sx_full[cs.i], cs.ph, alive))
                         break;
                     __syncwarp();
                 }
-                if (!warp_wait(&acc_full[b], (uint32_t)(g >> 1) & 1u, alive))
+                const float *chunk = sxs + cs.i * (2 * ISXC * IBMX);
+                const float swf = chunk[(ISXC + j) * IBMX + q * 32 + (int)lane]; /* this lane's row */
+                const uint64_t sw2 = pack2u(__float_as_uint(swf), __float_as_uint(swf));
+                if (!warp_wait(&acc_full[b], (uint32_t)(g / IACC) & 1u, alive))
                     break;
                 tc_fence_after();
-                /* one 32-column half at a time: read, scale into the running sums */
+                uint32_t v[IEpiCols];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t v[32];
-                    tmem_ld32(tb + (uint32_t)b * IBMX + (uint32_t)h * 32u, v);
-                    tmem_ld_wait();
-                    const ulonglong2 *sp = reinterpret_cast<const ulonglong2 *>(sxs + cs.i * (ISXC * IBMX) +
-                                                                                 j * IBMX + c0 + h * 32);
-#pragma unroll
-                    for (int i4 = 0; i4 < 8; ++i4) {
-                        const ulonglong2 s4 = sp[i4]; /* sx of rows 4*i4 .. 4*i4 + 3 of this half */
-                        const int i = h * 16 + 2 * i4;
-                        run[i] = f2_fma(f2_mul(f2_add(pack2u(v[4 * i4], v[4 * i4 + 1]), nbias), s4.x), sw2, run[i]);
-                        run[i + 1] = f2_fma(f2_mul(f2_add(pack2u(v[4 * i4 + 2], v[4 * i4 + 3]), nbias), s4.y), sw2,
-                                            run[i + 1]);
-                    }
-                }
-                /* the accumulator back to the bias for its next block, then free */
-                tmem_fill32(tb + (uint32_t)b * IBMX, kI8Bias);
-                tmem_fill32(tb + (uint32_t)b * IBMX + 32u, kI8Bias);
-                tmem_st_wait();
+                for (int h = 0; h < IEpiCols / 32; ++h)
+                    tmem_ld32(tb + (uint32_t)b * IBMX + (uint32_t)h * 32u,
+                              *reinterpret_cast<uint32_t(*)[32]>(&v[h * 32]));
+                tmem_ld_wait();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
-                    mbar_arrive_remote(ae0 + (uint32_t)b * 8u);
+                    mbar_arrive_remote(ae0 + (uint32_t)b * 8u); /* accumulator free: the sums are in registers */
+                const ulonglong2 *sp = reinterpret_cast<const ulonglong2 *>(chunk + j * IBMX + c0);
+#pragma unroll
+                for (int i4 = 0; i4 < IEpiCols / 4; ++i4) {
+                    const ulonglong2 s4 = sp[i4]; /* sx of rows 4*i4 .. 4*i4 + 3 */
+                    const int i = 2 * i4;
+                    run[i] = f2_fma(f2_mul(f2_add(pack2u(v[4 * i4] + kI8Bias, v[4 * i4 + 1] + kI8Bias), nbias), s4.x),
+                                    sw2, run[i]);
+                    run[i + 1] = f2_fma(
+                        f2_mul(f2_add(pack2u(v[4 * i4 + 2] + kI8Bias, v[4 * i4 + 3] + kI8Bias), nbias), s4.y), sw2,
+                        run[i + 1]);
+                }
                 if (j == ISXC - 1 || kb == nkb - 1) {
                     __syncwarp();
                     if (lane == 0)
@@ -1330,7 +1317,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
                 continue;
             float *yp = args.y + (size_t)m0 * args.N + n;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < IEpiCols / 2; ++i) {
                 const float lo = __uint_as_float((uint32_t)run[i]), hi = __uint_as_float((uint32_t)(run[i] >> 32));
                 if (2 * i < jl)
                     yp[0] = (args.accumulate ? yp[0] : 0.f) + lo;
