@@ -76,9 +76,10 @@ int htile_gemm_precise_launch(const uint8_t *hole, const uint8_t *plug, const fl
 /* The INT8 W8A8 GEMM (int8_mma_gemm contract, no fused plug) on tcgen05 kind::i8:
  * M > 64, K % 128 == 0, 16-byte aligned int8 operands; y (+)= bit for bit what the
  * mma.sync path gives. */
-bool int8_tc_supported(const int8_t *xq, const int8_t *wq, int M, int K);
-cudaError_t int8_tc_gemm_launch(const int8_t *xq, const float *sx, const int8_t *wq, const float *sw, float *y, int M,
-                                int N, int K, int accumulate, cudaStream_t stream); /* cudaErrorNotSupported: not launched */
+bool int8_tc_supported(const int8_t *xq, const int8_t *wq, const uint8_t *pq4, int M, int K);
+cudaError_t int8_tc_gemm_launch(const int8_t *xq, const float *sx, const int8_t *wq, const float *sw,
+                                const uint8_t *pq4, const float *psc, float *y, int M, int N, int K, int accumulate,
+                                cudaStream_t stream); /* cudaErrorNotSupported: not launched */
 /* Sticky error words written by kernels whose bounded waits ran out (0 = none),
  * one per kernel file; read_kernel_error ORs them. */
 int read_kernel_error(bool clear);

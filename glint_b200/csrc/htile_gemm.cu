@@ -1035,26 +1035,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PThreads, 1)
  * as in the kernels above. */
 constexpr int IBMX = 128, IBMH = 64;   /* activation rows per pair tile / per CTA */
 constexpr int IBK2 = 128;              /* K bytes per stage: two 64-k blocks */
-constexpr int ISTAGES = 4;
-/* 11 warps: producer, issuer, scale stager, 8 epilogue warps.  A CTA's warps are spread
- * over the SM's four sub-partitions, each with a 16K-register file, so at most three
- * warps share one and each may hold 168 registers (the epilogue keeps 64 running sums
- * and 64 accumulator values per lane). */
-constexpr int IEpiCols = 32;                       /* accumulator columns per epilogue warp */
+/* Warps: 0 TMA producer, 1 UMMA issuer, 2 scale stager, 3-18 epilogue (32 columns of one
+ * TMEM lane quadrant each), and with the fused plug 19, the plug unpacker.  A CTA's warps
+ * are spread over the SM's four sub-partitions, each with a 16K-register file: with 19 or
+ * 20 warps five share one, so each may hold 96 registers. */
+constexpr int IEpiCols = 32;
 constexpr int IEpi0 = 3, IEpiWarps = 4 * (IBMX / IEpiCols);
-constexpr int IThreads = (IEpi0 + IEpiWarps) * 32;
-constexpr int IStageX = IBMH * IBK2;               /* 8 KB */
-constexpr int IStage = IStageX + BN * IBK2;        /* + 16 KB of weights */
-constexpr int ISXC = 8, ISXSTAGES = 4;             /* scales: 8 blocks per chunk */
-/* a chunk: sx of the tile's 128 activation rows, then sw of this CTA's 128 weight rows,
- * each [block][row] */
-constexpr int ISxChunk = 2 * ISXC * IBMX * 4; /* 8 KB */
-constexpr int ISmemBytes = 1024 + ISTAGES * IStage + ISXSTAGES * ISxChunk + 256;
-/* four 128-column accumulators (all of TMEM): the tensor cores run up to three blocks
- * ahead of the epilogue, which hides the per-block hand-over (commit, wake, read,
- * release, issue) */
-constexpr int IACC = 4;
-constexpr uint32_t kITmemCols = IACC * IBMX;
+constexpr int IUnpackWarp = IEpi0 + IEpiWarps;
+constexpr int IStageX = IBMH * IBK2;            /* 8 KB of activations per CTA */
+constexpr int IStageW = BN * IBK2;              /* 16 KB of weights per CTA */
+constexpr int IStagePQ = BN * IBK2 / 2;         /* 8 KB of packed plug nibbles */
+constexpr int ISXC = 8;                         /* scale chunks: 8 blocks */
+constexpr uint32_t kITmemCols = 4 * IBMX;       /* all of TMEM */
 /* instruction descriptor: s32 accumulate, s8 A and B, both K-major, N = 128, M = 256 (pair) */
 constexpr uint32_t kIdescI8 =
     (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(IBMX >> 3) << 17) | ((uint32_t)((2 * BN) >> 4) << 24);
@@ -1064,11 +1056,31 @@ constexpr uint32_t kIdescI8 =
 constexpr uint32_t kI8Bias = 0x4B400000u;
 constexpr float kI8BiasF = 12582912.0f;
 
+/* Layout per variant.  Plain: four stages of [x | w], four scale chunks [sx | sw], four
+ * 128-column accumulators (the tensor cores run up to three blocks ahead of the
+ * epilogue).  Fused plug: three stages of [x | w | plug int8 (128-byte swizzle, written by
+ * the unpacker) | packed nibbles (TMA)], two chunks [sx | sw | ps], two accumulator slots
+ * of base and plug sums. */
+template <bool PLUG> struct I8Cfg {
+    static constexpr int kStages = PLUG ? 3 : 4;
+    static constexpr int kStage = IStageX + IStageW + (PLUG ? IStageW + IStagePQ : 0);
+    static constexpr int kOffP = IStageX + IStageW;           /* unpacked plug (1 KB aligned) */
+    static constexpr int kOffQ = IStageX + 2 * IStageW;       /* packed nibbles */
+    static constexpr int kSxStages = PLUG ? 2 : 4;
+    static constexpr int kArrays = PLUG ? 3 : 2;
+    static constexpr int kChunk = kArrays * ISXC * IBMX;      /* floats */
+    static constexpr int kSlots = PLUG ? 2 : 4;
+    static constexpr int kSlotCols = PLUG ? 2 * IBMX : IBMX;
+    static constexpr int kWarps = IEpi0 + IEpiWarps + (PLUG ? 1 : 0);
+    static constexpr int kThreads = kWarps * 32;
+    static constexpr int kSmem = 1024 + kStages * kStage + kSxStages * kChunk * 4 + 512; /* + barriers */
+};
+
 struct I8Maps {
-    CUtensorMap x, w;
+    CUtensorMap x, w, q;
 };
 struct I8Args {
-    const float *sx, *sw;
+    const float *sx, *sw, *ps;
     float *y;
     int M, N, K;
     int accumulate;
@@ -1108,19 +1120,40 @@ __device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi)
     return r;
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
+/* int8 (nibble - 8) of 8 packed bytes: 16 weights, element 2i in the low nibble */
+__device__ __forceinline__ uint32_t nib_s8(uint32_t lo4, uint32_t hi4, uint32_t sel)
+{
+    /* bytes n in 0..15 -> n - 8 as int8: m = n ^ 8 is n - 8 in 4-bit two's complement,
+     * and bit 3 of m times 0x1E is its sign extension into the byte's high nibble */
+    const uint32_t m = __byte_perm(lo4, hi4, sel) ^ 0x08080808u;
+    return m | ((m & 0x08080808u) * 0x1Eu);
+}
+__device__ __forceinline__ uint4 unpack16(uint2 pk)
+{
+    const uint32_t l0 = pk.x & 0x0F0F0F0Fu, h0 = (pk.x >> 4) & 0x0F0F0F0Fu;
+    const uint32_t l1 = pk.y & 0x0F0F0F0Fu, h1 = (pk.y >> 4) & 0x0F0F0F0Fu;
+    return make_uint4(nib_s8(l0, h0, 0x5140), nib_s8(l0, h0, 0x7362), nib_s8(l1, h1, 0x5140),
+                      nib_s8(l1, h1, 0x7362));
+}
+
+template <bool PLUG>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(I8Cfg<PLUG>::kThreads, 1)
     int8_tc_kernel(const __grid_constant__ I8Maps maps, const I8Args args)
 {
+    using C = I8Cfg<PLUG>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *sxs = reinterpret_cast<float *>(ring + ISTAGES * IStage); /* [stage][sx | sw][block][128 rows] */
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + ISTAGES * IStage + ISXSTAGES * ISxChunk);
-    uint64_t *empty = full + ISTAGES;
-    uint64_t *acc_full = empty + ISTAGES; /* [IACC] */
-    uint64_t *acc_empty = acc_full + IACC; /* [IACC] leader: both CTAs' epilogues release it */
-    uint64_t *sx_full = acc_empty + IACC;  /* [ISXSTAGES] the stager's 32 lanes */
-    uint64_t *sx_empty = sx_full + ISXSTAGES; /* [ISXSTAGES] this CTA's epilogue warps */
-    uint64_t *mma_done = sx_empty + ISXSTAGES;
+    float *sxs = reinterpret_cast<float *>(ring + C::kStages * C::kStage); /* [chunk][array][block][128 rows] */
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + C::kStages * C::kStage + C::kSxStages * C::kChunk * 4);
+    uint64_t *empty = full + C::kStages;
+    uint64_t *q_full = empty + C::kStages;     /* plug: this CTA's packed nibbles landed */
+    uint64_t *q_empty = q_full + C::kStages;   /* plug: the unpacker has read them */
+    uint64_t *pl_full = q_empty + C::kStages;  /* plug, leader: both CTAs' unpacked plug written */
+    uint64_t *acc_full = pl_full + C::kStages; /* [slots] */
+    uint64_t *acc_empty = acc_full + C::kSlots; /* [slots] leader: both CTAs' epilogues release it */
+    uint64_t *sx_full = acc_empty + C::kSlots;  /* the stager's 32 lanes */
+    uint64_t *sx_empty = sx_full + C::kSxStages; /* this CTA's epilogue warps */
+    uint64_t *mma_done = sx_empty + C::kSxStages;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -1131,15 +1164,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
     const int nkb = args.K / 64, KS2 = args.K / IBK2;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < ISTAGES; ++s) {
+        for (int s = 0; s < C::kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&q_full[s], 1);
+            mbar_init(&q_empty[s], 1);
+            mbar_init(&pl_full[s], 2);
         }
-        for (int b = 0; b < IACC; ++b) {
+        for (int b = 0; b < C::kSlots; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 2 * IEpiWarps);
         }
-        for (int s = 0; s < ISXSTAGES; ++s) {
+        for (int s = 0; s < C::kSxStages; ++s) {
             mbar_init(&sx_full[s], 32);
             mbar_init(&sx_empty[s], IEpiWarps);
         }
@@ -1159,56 +1195,79 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
     bool alive = true;
 
     if (warp == 0) {
-        /* ---- producer (both CTAs): this CTA's 64 activation rows and 128 weight rows */
+        /* ---- producer (both CTAs): this CTA's 64 activation rows and 128 weight rows (and
+         * their packed plug) */
         if (lane == 0) {
             Ring st;
             int64_t issued = 0;
             for (int T = pair; T < args.tiles && alive; T += npairs) {
                 const int mr = (T % args.mtiles) * IBMX + (int)rank * IBMH;
                 const int nr = (T / args.mtiles) * (2 * BN) + (int)rank * BN;
-                for (int ks = 0; ks < KS2 && alive; ++ks, st.next<ISTAGES>()) {
+                for (int ks = 0; ks < KS2 && alive; ++ks, st.next<C::kStages>()) {
                     if (!wait_or_fail(&empty[st.i], st.ph ^ 1u, alive))
                         break;
+                    uint8_t *sb = ring + st.i * C::kStage;
                     if (leader)
-                        mbar_expect_tx(&full[st.i], 2 * IStage);
+                        mbar_expect_tx(&full[st.i], 2 * (IStageX + IStageW));
                     const uint32_t fb = peer_addr(saddr(&full[st.i]), 0);
-                    tma_load_2d_pair(ring + st.i * IStage, &maps.x, fb, ks * IBK2, mr);
-                    tma_load_2d_pair(ring + st.i * IStage + IStageX, &maps.w, fb, ks * IBK2, nr);
+                    tma_load_2d_pair(sb, &maps.x, fb, ks * IBK2, mr);
+                    tma_load_2d_pair(sb + IStageX, &maps.w, fb, ks * IBK2, nr);
                     ++issued;
+                    if (PLUG) {
+                        if (!wait_or_fail(&q_empty[st.i], st.ph ^ 1u, alive))
+                            break;
+                        mbar_expect_tx(&q_full[st.i], IStagePQ);
+                        tma_load_2d(sb + C::kOffQ, &maps.q, &q_full[st.i], ks * (IBK2 / 2), nr);
+                    }
                 }
             }
-            if (!alive && leader) {
+            if (!alive) {
                 /* let the loads already issued land before the CTA exits */
                 bool drain = true;
-                for (int64_t j = issued > ISTAGES ? issued - ISTAGES : 0; j < issued && drain; ++j)
-                    drain = mbar_wait_bounded(&full[(int)(j % ISTAGES)], (uint32_t)(j / ISTAGES) & 1u,
-                                              &g_glint_kernel_error);
+                for (int64_t j = issued > C::kStages ? issued - C::kStages : 0; j < issued && drain; ++j) {
+                    const int s = (int)(j % C::kStages);
+                    const uint32_t ph = (uint32_t)(j / C::kStages) & 1u;
+                    if (leader)
+                        drain = mbar_wait_bounded(&full[s], ph, &g_glint_kernel_error);
+                    if (PLUG && drain)
+                        drain = mbar_wait_bounded(&q_full[s], ph, &g_glint_kernel_error);
+                }
             }
         }
     } else if (warp == 1) {
-        /* ---- UMMA issuer (leader CTA only): one fresh accumulator per 64-k block */
+        /* ---- UMMA issuer (leader CTA only): fresh accumulators per 64-k block (base, and
+         * plug beside it) */
         if (leader && lane == 0) {
             Ring st;
-            int64_t g = 0; /* blocks issued by this pair: accumulator g % IACC, its use g / IACC */
+            int64_t g = 0; /* blocks issued by this pair: slot g % slots, its use g / slots */
             const uint32_t e0 = peer_addr(saddr(&empty[0]), 0), e1 = peer_addr(saddr(&empty[0]), 1);
             const uint32_t af0 = peer_addr(saddr(&acc_full[0]), 0), af1 = peer_addr(saddr(&acc_full[0]), 1);
             for (int T = pair; T < args.tiles && alive; T += npairs) {
-                for (int ks = 0; ks < KS2 && alive; ++ks, st.next<ISTAGES>()) {
+                for (int ks = 0; ks < KS2 && alive; ++ks, st.next<C::kStages>()) {
                     if (!wait_or_fail(&full[st.i], st.ph, alive))
                         break;
+                    if (PLUG) {
+                        if (!wait_or_fail(&pl_full[st.i], st.ph, alive))
+                            break;
+                        asm volatile("fence.acq_rel.cluster;" ::: "memory"); /* the peer's unpacked plug */
+                    }
                     tc_fence_after();
-                    const uint32_t xs = saddr(ring + st.i * IStage), ws = xs + (uint32_t)IStageX;
+                    const uint32_t xs = saddr(ring + st.i * C::kStage), ws = xs + (uint32_t)IStageX;
+                    const uint32_t ps = xs + (uint32_t)C::kOffP;
                     for (int blk = 0; blk < 2 && alive; ++blk, ++g) {
-                        const int b = (int)(g % IACC);
-                        /* the first use of each accumulator waits on parity 1: returns at once */
-                        if (!wait_or_fail(&acc_empty[b], (uint32_t)((g / IACC) & 1) ^ 1u, alive))
+                        const int b = (int)(g % C::kSlots);
+                        /* the first use of each slot waits on parity 1: returns at once */
+                        if (!wait_or_fail(&acc_empty[b], (uint32_t)((g / C::kSlots) & 1) ^ 1u, alive))
                             break;
                         tc_fence_after();
-                        const uint32_t d = tmem + (uint32_t)b * IBMX;
+                        const uint32_t d = tmem + (uint32_t)(b * C::kSlotCols);
 #pragma unroll
                         for (int kk = 0; kk < 2; ++kk) {
                             const uint32_t off = (uint32_t)(blk * 2 + kk) * 32u; /* K = 32 bytes per UMMA */
                             umma_pair_ss_i8(d, sw128_desc(ws + off), sw128_desc(xs + off), kIdescI8, kk > 0 ? 1u : 0u);
+                            if (PLUG)
+                                umma_pair_ss_i8(d + (uint32_t)IBMX, sw128_desc(ps + off), sw128_desc(xs + off),
+                                                kIdescI8, kk > 0 ? 1u : 0u);
                         }
                         umma_commit_to(af0 + (uint32_t)b * 8u);
                         umma_commit_to(af1 + (uint32_t)b * 8u);
@@ -1225,19 +1284,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
         }
         __syncwarp();
     } else if (warp == 2) {
-        /* ---- scale stager: sx of the tile's 128 activation rows and sw of this CTA's
-         * 128 weight rows, 8 blocks at a time, transposed to [block][row] so an epilogue
-         * warp reads its rows' sx of one block as contiguous 16-byte words and each lane
-         * its row's sw without a global load in the block loop */
+        /* ---- scale stager: sx of the tile's 128 activation rows and sw (and ps) of this
+         * CTA's 128 weight rows, 8 blocks at a time, transposed to [block][row] so an
+         * epilogue warp reads its rows' sx of one block as contiguous 16-byte words and
+         * each lane its row's weight scales without a global load in the block loop */
         Ring cs;
         for (int T = pair; T < args.tiles && alive; T += npairs) {
             const int mb = (T % args.mtiles) * IBMX;
             const int nb0 = (T / args.mtiles) * (2 * BN) + (int)rank * BN;
-            for (int kb0 = 0; kb0 < nkb && alive; kb0 += ISXC, cs.next<ISXSTAGES>()) {
+            for (int kb0 = 0; kb0 < nkb && alive; kb0 += ISXC, cs.next<C::kSxStages>()) {
                 if (!warp_wait(&sx_empty[cs.i], cs.ph ^ 1u, alive))
                     break;
                 __syncwarp();
-                float *dst = sxs + cs.i * (2 * ISXC * IBMX);
+                float *dst = sxs + cs.i * C::kChunk;
                 const int nb = min(ISXC, nkb - kb0);
 #pragma unroll
                 for (int rr = 0; rr < IBMX / 32; ++rr) {
@@ -1250,12 +1309,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
 #pragma unroll
                     for (int j = 0; j < ISXC; ++j)
                         dst[(ISXC + j) * IBMX + r] = (nr < args.N && j < nb) ? __ldg(srcw + j) : 0.f;
+                    if (PLUG) {
+                        const float *srcp = args.ps + (size_t)nr * nkb + kb0;
+#pragma unroll
+                        for (int j = 0; j < ISXC; ++j)
+                            dst[(2 * ISXC + j) * IBMX + r] = (nr < args.N && j < nb) ? __ldg(srcp + j) : 0.f;
+                    }
                 }
                 mbar_arrive(&sx_full[cs.i]);
             }
         }
-    } else {
-        /* ---- epilogue: warp w -> TMEM lanes 32*(w%4) (weight rows n), columns c0 .. c0+63
+    } else if (warp < IUnpackWarp) {
+        /* ---- epilogue: warp w -> TMEM lanes 32*(w%4) (weight rows n), columns c0 .. c0+31
          * (activation rows m) */
         const int q = warp & 3, c0 = ((warp - IEpi0) >> 2) * IEpiCols;
         const uint32_t ae0 = peer_addr(saddr(&acc_empty[0]), 0);
@@ -1273,44 +1338,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
             for (int i = 0; i < IEpiCols / 2; ++i)
                 run[i] = 0;
             for (int kb = 0; kb < nkb && alive; ++kb, ++g) {
-                const int b = (int)(g % IACC), j = kb % ISXC;
+                const int b = (int)(g % C::kSlots), j = kb % ISXC;
                 if (j == 0) {
                     if (!warp_wait(&sx_full[cs.i], cs.ph, alive))
                         break;
                     __syncwarp();
                 }
-                const float *chunk = sxs + cs.i * (2 * ISXC * IBMX);
-                const float swf = chunk[(ISXC + j) * IBMX + q * 32 + (int)lane]; /* this lane's row */
-                const uint64_t sw2 = pack2u(__float_as_uint(swf), __float_as_uint(swf));
-                if (!warp_wait(&acc_full[b], (uint32_t)(g / IACC) & 1u, alive))
+                const float *chunk = sxs + cs.i * C::kChunk;
+                const ulonglong2 *sp = reinterpret_cast<const ulonglong2 *>(chunk + j * IBMX + c0);
+                if (!warp_wait(&acc_full[b], (uint32_t)(g / C::kSlots) & 1u, alive))
                     break;
                 tc_fence_after();
-                uint32_t v[IEpiCols];
+                /* base sums, then (fused plug) the plug sums: per block the reference adds
+                 * the base term and then the plug term to each output */
 #pragma unroll
-                for (int h = 0; h < IEpiCols / 32; ++h)
-                    tmem_ld32(tb + (uint32_t)b * IBMX + (uint32_t)h * 32u,
-                              *reinterpret_cast<uint32_t(*)[32]>(&v[h * 32]));
-                tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive_remote(ae0 + (uint32_t)b * 8u); /* accumulator free: the sums are in registers */
-                const ulonglong2 *sp = reinterpret_cast<const ulonglong2 *>(chunk + j * IBMX + c0);
+                for (int term = 0; term < (PLUG ? 2 : 1); ++term) {
+                    const float wsf = chunk[((1 + term) * ISXC + j) * IBMX + q * 32 + (int)lane]; /* lane's row */
+                    const uint64_t sw2 = pack2u(__float_as_uint(wsf), __float_as_uint(wsf));
+                    uint32_t v[IEpiCols];
+                    tmem_ld32(tb + (uint32_t)(b * C::kSlotCols + term * IBMX), v);
+                    tmem_ld_wait();
+                    if (term == (PLUG ? 1 : 0)) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            mbar_arrive_remote(ae0 + (uint32_t)b * 8u); /* slot free: the sums are in registers */
+                    }
 #pragma unroll
-                for (int i4 = 0; i4 < IEpiCols / 4; ++i4) {
-                    const ulonglong2 s4 = sp[i4]; /* sx of rows 4*i4 .. 4*i4 + 3 */
-                    const int i = 2 * i4;
-                    run[i] = f2_fma(f2_mul(f2_add(pack2u(v[4 * i4] + kI8Bias, v[4 * i4 + 1] + kI8Bias), nbias), s4.x),
-                                    sw2, run[i]);
-                    run[i + 1] = f2_fma(
-                        f2_mul(f2_add(pack2u(v[4 * i4 + 2] + kI8Bias, v[4 * i4 + 3] + kI8Bias), nbias), s4.y), sw2,
-                        run[i + 1]);
+                    for (int i4 = 0; i4 < IEpiCols / 4; ++i4) {
+                        const ulonglong2 s4 = sp[i4]; /* sx of rows 4*i4 .. 4*i4 + 3 */
+                        const int i = 2 * i4;
+                        run[i] = f2_fma(
+                            f2_mul(f2_add(pack2u(v[4 * i4] + kI8Bias, v[4 * i4 + 1] + kI8Bias), nbias), s4.x), sw2,
+                            run[i]);
+                        run[i + 1] = f2_fma(
+                            f2_mul(f2_add(pack2u(v[4 * i4 + 2] + kI8Bias, v[4 * i4 + 3] + kI8Bias), nbias), s4.y),
+                            sw2, run[i + 1]);
+                    }
                 }
                 if (j == ISXC - 1 || kb == nkb - 1) {
                     __syncwarp();
                     if (lane == 0)
                         mbar_arrive(&sx_empty[cs.i]);
-                    cs.next<ISXSTAGES>();
+                    cs.next<C::kSxStages>();
                 }
             }
             if (!alive || !nok)
@@ -1325,6 +1395,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(IThreads, 1)
                 if (2 * i + 1 < jl)
                     yp[0] = (args.accumulate ? yp[0] : 0.f) + hi;
                 yp += args.N;
+            }
+        }
+    } else if (PLUG) {
+        /* ---- plug unpacker (both CTAs): each stage's packed nibbles [128 rows][64 B] into
+         * int8 (nibble - 8) rows of 128 B in the 128-byte swizzle the UMMA reads (16-byte
+         * chunk c of row r at c ^ (r & 7)), once the stage's previous UMMAs are done */
+        Ring st;
+        const uint32_t pf0 = peer_addr(saddr(&pl_full[0]), 0);
+        for (int T = pair; T < args.tiles && alive; T += npairs) {
+            for (int ks = 0; ks < KS2 && alive; ++ks, st.next<C::kStages>()) {
+                if (!warp_wait(&q_full[st.i], st.ph, alive) || !warp_wait(&empty[st.i], st.ph ^ 1u, alive))
+                    break;
+                __syncwarp();
+                const uint8_t *src = ring + st.i * C::kStage + C::kOffQ;
+                uint8_t *dst = ring + st.i * C::kStage + C::kOffP;
+#pragma unroll 4
+                for (int it = 0; it < BN * 8 / 32; ++it) {
+                    const int item = it * 32 + (int)lane, r = item >> 3, c = item & 7;
+                    const uint2 pk = *reinterpret_cast<const uint2 *>(src + r * 64 + c * 8);
+                    *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = unpack16(pk);
+                }
+                fence_proxy_async_smem(); /* the UMMA reads these bytes through the async proxy */
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&q_empty[st.i]);
+                    /* release at cluster scope: the leader's UMMAs read these bytes */
+                    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                                     pf0 + (uint32_t)st.i * 8u)
+                                 : "memory");
+                }
             }
         }
     }
@@ -1423,11 +1523,11 @@ int max_pairs(int kind = 0)
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(2 * std::max(1, sm_count() / 2));
-    cfg.blockDim = dim3(kind == 2 ? IThreads : kind ? PThreads : kThreads);
-    cfg.dynamicSmemBytes = kind == 2 ? ISmemBytes : kind ? PSmemBytes : kSmemBytes;
+    cfg.blockDim = dim3(kind == 2 ? I8Cfg<false>::kThreads : kind ? PThreads : kThreads);
+    cfg.dynamicSmemBytes = kind == 2 ? I8Cfg<false>::kSmem : kind ? PSmemBytes : kSmemBytes;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const void *kern = kind == 2   ? (const void *)int8_tc_kernel
+    const void *kern = kind == 2   ? (const void *)int8_tc_kernel<false>
                        : kind == 1 ? (const void *)htile_gemm_precise_kernel
                                    : (const void *)htile_gemm_kernel;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
@@ -1527,29 +1627,42 @@ int htile_gemm_precise_launch(const uint8_t *hole, const uint8_t *plug, const fl
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunch;
 }
 
-bool int8_tc_supported(const int8_t *xq, const int8_t *wq, int M, int K)
+bool int8_tc_supported(const int8_t *xq, const int8_t *wq, const uint8_t *pq4, int M, int K)
 {
     return M > 64 && K >= IBK2 && K % IBK2 == 0 && aligned_to(xq, 16) && aligned_to(wq, 16) &&
-           tensor_map_encoder() != nullptr;
+           (!pq4 || aligned_to(pq4, 16)) && tensor_map_encoder() != nullptr;
 }
 
-cudaError_t int8_tc_gemm_launch(const int8_t *xq, const float *sx, const int8_t *wq, const float *sw, float *y, int M,
-                                int N, int K, int accumulate, cudaStream_t st)
+namespace {
+template <bool PLUG> cudaError_t int8_tc_launch_t(const I8Maps &maps, const I8Args &a, int pairs, cudaStream_t st)
+{
+    using C = I8Cfg<PLUG>;
+    if (!ensure_smem((const void *)int8_tc_kernel<PLUG>, C::kSmem))
+        return cudaErrorNotSupported;
+    int8_tc_kernel<PLUG><<<2 * pairs, C::kThreads, C::kSmem, st>>>(maps, a);
+    return cudaGetLastError();
+}
+} // namespace
+
+cudaError_t int8_tc_gemm_launch(const int8_t *xq, const float *sx, const int8_t *wq, const float *sw,
+                                const uint8_t *pq4, const float *psc, float *y, int M, int N, int K, int accumulate,
+                                cudaStream_t st)
 {
     I8Maps maps;
     if (!encode_map(&maps.x, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)K, (uint64_t)M, (uint64_t)K, IBK2, IBMH,
                     CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_map(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, (uint64_t)K, (uint64_t)N, (uint64_t)K, IBK2, BN,
-                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !ensure_smem((const void *)int8_tc_kernel, ISmemBytes))
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorNotSupported;
+    if (pq4 && !encode_map(&maps.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, pq4, (uint64_t)K / 2, (uint64_t)N,
+                           (uint64_t)K / 2, IBK2 / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorNotSupported;
     I8Args a{};
-    a.sx = sx, a.sw = sw, a.y = y, a.M = M, a.N = N, a.K = K, a.accumulate = accumulate;
+    a.sx = sx, a.sw = sw, a.ps = psc, a.y = y, a.M = M, a.N = N, a.K = K, a.accumulate = accumulate;
     a.mtiles = (M + IBMX - 1) / IBMX;
     a.tiles = a.mtiles * ((N + 2 * BN - 1) / (2 * BN));
     const int pairs = std::max(1, std::min(a.tiles, max_pairs(2)));
-    int8_tc_kernel<<<2 * pairs, IThreads, ISmemBytes, st>>>(maps, a);
-    return cudaGetLastError();
+    return pq4 ? int8_tc_launch_t<true>(maps, a, pairs, st) : int8_tc_launch_t<false>(maps, a, pairs, st);
 }
 
 int read_kernel_error(bool clear)

@@ -12,9 +12,9 @@
  * fused multiply-add per block and output), so the outputs match it bit for bit
  * whatever the tiling.
  *
- * On sm_100a, prefill shapes without a fused plug (M > 64, K % 128 == 0) run the
- * tcgen05 kind::i8 kernel of htile_gemm.cu (TMA operands, int32 block sums in TMEM,
- * the same f32 steps in the epilogue); the rest run `mma.sync` m16n8k32 s8 tiles (64 activation rows x 128 weight rows
+ * On sm_100a, prefill shapes (M > 64, K % 128 == 0) run the tcgen05 kind::i8 kernel of
+ * htile_gemm.cu (TMA operands, int32 block sums in TMEM, a fused plug unpacked to int8
+ * in shared memory, the same f32 steps in the epilogue); the rest run `mma.sync` m16n8k32 s8 tiles (64 activation rows x 128 weight rows
  * with a three-stage ring, or for M <= 16, 16 x 64 with an eight-stage ring), 8 warps,
  * shared-memory rings filled with 16-byte asynchronous copies (later K slices land
  * while this one multiplies), plug nibbles unpacked in shared memory.  No split over
@@ -279,9 +279,9 @@ cudaError_t quant(const __nv_bfloat16 *x, const int8_t *xq_prev, const float *sx
 cudaError_t gemm(const int8_t *xq, const float *sx, const int8_t *wq, const float *sw, float *y, int m, int n, int k,
                  int accumulate, const uint8_t *pq4, const float *psc, cudaStream_t st)
 {
-    /* prefill shapes without a fused plug: tcgen05 kind::i8 (the same bits) */
-    if (!pq4 && int8_tc_supported(xq, wq, m, k)) {
-        const cudaError_t e = int8_tc_gemm_launch(xq, sx, wq, sw, y, m, n, k, accumulate, st);
+    /* prefill shapes: tcgen05 kind::i8 (the same bits) */
+    if (int8_tc_supported(xq, wq, pq4, m, k)) {
+        const cudaError_t e = int8_tc_gemm_launch(xq, sx, wq, sw, pq4, psc, y, m, n, k, accumulate, st);
         if (e != cudaErrorNotSupported)
             return e;
     }
