@@ -1120,20 +1120,22 @@ __device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi)
     return r;
 }
 
-/* int8 (nibble - 8) of 8 packed bytes: 16 weights, element 2i in the low nibble */
-__device__ __forceinline__ uint32_t nib_s8(uint32_t lo4, uint32_t hi4, uint32_t sel)
+/* int8 (nibble - 8) of 16 packed bytes: 32 weights, element 2i in the low nibble of
+ * byte i.  Per byte n in 0..15, (n + 0x78) ^ 0x80 is n - 8 as int8 (the add never
+ * carries out of the byte), so one add and one xor handle four nibbles. */
+__device__ __forceinline__ void unpack32(uint4 pk, uint4 &o0, uint4 &o1)
 {
-    /* bytes n in 0..15 -> n - 8 as int8: m = n ^ 8 is n - 8 in 4-bit two's complement,
-     * and bit 3 of m times 0x1E is its sign extension into the byte's high nibble */
-    const uint32_t m = __byte_perm(lo4, hi4, sel) ^ 0x08080808u;
-    return m | ((m & 0x08080808u) * 0x1Eu);
-}
-__device__ __forceinline__ uint4 unpack16(uint2 pk)
-{
-    const uint32_t l0 = pk.x & 0x0F0F0F0Fu, h0 = (pk.x >> 4) & 0x0F0F0F0Fu;
-    const uint32_t l1 = pk.y & 0x0F0F0F0Fu, h1 = (pk.y >> 4) & 0x0F0F0F0Fu;
-    return make_uint4(nib_s8(l0, h0, 0x5140), nib_s8(l0, h0, 0x7362), nib_s8(l1, h1, 0x5140),
-                      nib_s8(l1, h1, 0x7362));
+    uint32_t r[8];
+    const uint32_t w[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = ((w[i] & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        const uint32_t hi = (((w[i] >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        r[2 * i] = __byte_perm(lo, hi, 0x5140);
+        r[2 * i + 1] = __byte_perm(lo, hi, 0x7362);
+    }
+    o0 = make_uint4(r[0], r[1], r[2], r[3]);
+    o1 = make_uint4(r[4], r[5], r[6], r[7]);
 }
 
 template <bool PLUG>
@@ -1410,11 +1412,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(I8Cfg<PLUG>::kThread
                 __syncwarp();
                 const uint8_t *src = ring + st.i * C::kStage + C::kOffQ;
                 uint8_t *dst = ring + st.i * C::kStage + C::kOffP;
+                /* 16 packed bytes (output chunks 2c and 2c + 1 of row r) per lane and step */
 #pragma unroll 4
-                for (int it = 0; it < BN * 8 / 32; ++it) {
-                    const int item = it * 32 + (int)lane, r = item >> 3, c = item & 7;
-                    const uint2 pk = *reinterpret_cast<const uint2 *>(src + r * 64 + c * 8);
-                    *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = unpack16(pk);
+                for (int it = 0; it < BN * 4 / 32; ++it) {
+                    const int item = it * 32 + (int)lane, r = item >> 2, c = item & 3;
+                    uint4 o0, o1;
+                    unpack32(*reinterpret_cast<const uint4 *>(src + r * 64 + c * 16), o0, o1);
+                    *reinterpret_cast<uint4 *>(dst + r * 128 + (((2 * c) ^ (r & 7)) << 4)) = o0;
+                    *reinterpret_cast<uint4 *>(dst + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4)) = o1;
                 }
                 fence_proxy_async_smem(); /* the UMMA reads these bytes through the async proxy */
                 __syncwarp();
