@@ -80,6 +80,12 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool full
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src), "r"(full ? 16 : 0)
                  : "memory");
 }
+/* 4-byte asynchronous copy (zero-filled when !full) */
+__device__ __forceinline__ void cp_async4(void *dst, const void *src, bool full)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(saddr(dst)), "l"(src), "r"(full ? 4 : 0)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -114,8 +120,9 @@ struct __align__(16) Int8Stage {
     float sx[BM], sw[BN], sp[BN];
 };
 
-/* the 64-wide K slice kb of this tile into stage st (x, weights, packed plug: 16-byte
- * asynchronous copies, zero-filled past m / n; scales: plain loads) */
+/* the 64-wide K slice kb of this tile into stage st, all by asynchronous copies
+ * zero-filled past m / n (x, weights, packed plug: 16 bytes; scales: 4 bytes), so no
+ * thread waits on a global load before the slice's barrier */
 template <bool PLUG, int BM, int BN>
 __device__ __forceinline__ void load_slice(const Int8Args &a, Int8Stage<BM, BN> &st, int m0, int n0, int kb, int nkb)
 {
@@ -138,12 +145,15 @@ __device__ __forceinline__ void load_slice(const Int8Args &a, Int8Stage<BM, BN> 
                        ok);
         }
     }
-    if (tid < BM)
-        st.sx[tid] = m0 + tid < a.m ? a.sx[(int64_t)(m0 + tid) * nkb + kb] : 0.f;
+    if (tid < BM) {
+        const bool ok = m0 + tid < a.m;
+        cp_async4(&st.sx[tid], ok ? a.sx + (int64_t)(m0 + tid) * nkb + kb : a.sx, ok);
+    }
     if (tid < BN) {
-        st.sw[tid] = n0 + tid < a.n ? a.sw[(int64_t)(n0 + tid) * nkb + kb] : 0.f;
+        const bool ok = n0 + tid < a.n;
+        cp_async4(&st.sw[tid], ok ? a.sw + (int64_t)(n0 + tid) * nkb + kb : a.sw, ok);
         if (PLUG)
-            st.sp[tid] = n0 + tid < a.n ? a.psc[(int64_t)(n0 + tid) * nkb + kb] : 0.f;
+            cp_async4(&st.sp[tid], ok ? a.psc + (int64_t)(n0 + tid) * nkb + kb : a.psc, ok);
     }
 }
 
