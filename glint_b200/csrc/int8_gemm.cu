@@ -298,6 +298,8 @@ cudaError_t gemm(const int8_t *xq, const float *sx, const int8_t *wq, const floa
     Int8Args a{xq, sx, wq, sw, y, m, n, k, accumulate, pq4, psc};
     if (m <= 16)
         return pq4 ? launch_gemm<true, 16, 64, 8>(a, st) : launch_gemm<false, 16, 64, 8>(a, st);
+    if (m <= 32)
+        return pq4 ? launch_gemm<true, 32, 64, 8>(a, st) : launch_gemm<false, 32, 64, 8>(a, st);
     return pq4 ? launch_gemm<true, 64, 128, 3>(a, st) : launch_gemm<false, 64, 128, 3>(a, st);
 }
 
