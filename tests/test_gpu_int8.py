@@ -18,8 +18,8 @@ import glint_oracle as O  # noqa: E402
 REF = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libp7_int8.so"
 # M > 64 with K % 128 == 0 runs the tcgen05 kind::i8 kernel (every entry point and
 # pass, the fused plug included); the rest run the mma.sync kernel
-SHAPES = [(1, 4096, 4096), (7, 1000, 192), (64, 128, 64), (130, 300, 640), (32, 4096, 14336), (96, 520, 384),
-          (256, 4096, 4096), (520, 1000, 2048)]
+SHAPES = [(1, 4096, 4096), (7, 1000, 192), (24, 1000, 640), (64, 128, 64), (130, 300, 640), (32, 4096, 14336),
+          (96, 520, 384), (256, 4096, 4096), (520, 1000, 2048)]
 
 
 @pytest.fixture(scope="module", autouse=True)
